@@ -1,0 +1,445 @@
+#!/usr/bin/env python
+"""Paged-decode attention throughput on B200 — one JSON line per run.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c4]
+
+A step is one decode-attention call (one layer) over one batch of the
+workload: ``c2`` (default) is the Qwen2.5-7B geometry batch of 64 sequences
+with contexts U[512, 4096]; ``c3`` adds the fused K/V cache write over 256
+sequences with shared prefixes; ``c4`` is 4 x 32k contexts. At N GPUs (one
+process per GPU, launched by torchrun) every rank decodes its own batch of
+the workload — the sequences are sharded, there is no collective on the data
+path — so the scaling is weak and ``value`` is the bytes all ranks moved
+divided by the slowest rank's time.
+
+* ``value``: HBM GB/s of useful bytes (K/V of every cached token of every
+  sequence, q, out, block tables) with inputs resident on the device; the K
+  steps are captured in one CUDA graph and timed with CUDA events; inputs
+  rotate over 3 pool sets and each step touches > L2 (126 MB) of K/V.
+* ``e2e``: the same metric through the public Python API
+  (``infrared_b200.paged_decode``) with host buffers: every step copies q,
+  block tables and context lengths from pinned host memory and reads the
+  output back.
+* ``roofline``: the decode call's bytes / its measured duration against the
+  measured HBM copy bandwidth in MEASURED_PEAKS.json.
+* ``cpu_baseline`` / ``--impl reference``: the reference's naive CPU path
+  (restated in oracle/, numpy) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged-decode attn HBM GB/s (% of ~8 TB/s) + decode tok/s at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", choices=["c2", "c3", "c4"], default="c2")
+    p.add_argument("--sets", type=int, default=3)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    return p.parse_args()
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            d = json.loads(path.read_text())
+            return float(d["hbm_gbs"]), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+# ------------------------------------------------------------------ CPU side
+
+
+def cpu_sample_workload(w, seqs, seed=0):
+    """Compact host copy of a few sequences of ``w`` (their blocks renumbered)."""
+    from infrared_b200 import workloads as wl
+
+    rng = np.random.default_rng(seed)
+    bs = w.block_size
+    ctx = w.context_lens[seqs].astype(np.int32)
+    nblk = (ctx.astype(np.int64) + bs - 1) // bs
+    bt = np.zeros((len(seqs), int(nblk.max())), np.int32)
+    perm = rng.permutation(int(nblk.sum()))
+    off = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[off:off + n]
+        off += n
+    sub = wl.Workload(w.name + "-sample", len(seqs), w.num_heads, w.num_kv_heads, w.head_dim,
+                      bs, int(nblk.sum()), "float32", w.scale, w.std, ctx, bt,
+                      wl.tail_slots(bt, ctx, bs))
+    q, kp, vp, _, _ = wl.numpy_values(sub, seed)
+    return sub, q, kp[None], vp[None]
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:  # noqa: BLE001
+        return 1
+
+
+def time_cpu_oracle(w, steps, warmup, budget_s=None):
+    """Time the oracle's naive path over one sequence per step (rotating)."""
+    from oracle import paged_attention_np as orc
+
+    order = list(range(w.batch))
+    samples = [cpu_sample_workload(w, [i], seed=i) for i in order[:8]]
+    times, nbytes = [], []
+    t_start = time.perf_counter()
+    for it in range(warmup + steps):
+        sub, q, kp, vp = samples[it % len(samples)]
+        t0 = time.perf_counter()
+        orc.decode_from_tables(q, kp, vp, 0, sub.block_tables, sub.context_lens,
+                               sub.block_size, sub.scale, sub.n_rep)
+        dt = time.perf_counter() - t0
+        if it >= warmup:
+            times.append(dt)
+            nbytes.append(sub.algorithmic_bytes() * w.elem_bytes // 4)
+        if budget_s is not None and it >= warmup and time.perf_counter() - t_start > budget_s:
+            break
+    total_t = sum(times)
+    gbs = sum(nbytes) / total_t / 1e9
+    return gbs, total_t, len(times)
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        import torch
+
+        self.proc = None
+        try:
+            props = torch.cuda.get_device_properties(device_index)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", bus, "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                smax.append(float(f[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ GPU side
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_workload(name, rank):
+    from infrared_b200 import workloads as wl
+
+    return wl.CONFIGS[name](seed=rank)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import infrared_b200 as irb
+    from infrared_b200 import ops
+    from infrared_b200 import workloads as wl
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    w = make_workload(args.config, rank)
+    fused = args.config == "c3"
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    ctx = torch.from_numpy(w.context_lens).to(dev)
+    sm = torch.from_numpy(w.slot_mapping).to(dev)
+    sets = [wl.torch_values(w, 1000 * rank + s, dev) for s in range(args.sets)]
+    out = torch.empty_like(sets[0][0])
+    _, _, ws_bytes = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    nbytes = w.algorithmic_bytes(with_write=fused)
+
+    def step(i):
+        q, kp, vp, kn, vn = sets[i % len(sets)]
+        if fused:
+            irb.paged_decode_write(q, kn, vn, kp, vp, sm, bt, ctx, w.scale, w.block_size,
+                                   out=out, ws=ws)
+        else:
+            irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size, out=out, ws=ws)
+
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        ops.check_device_errors(dev)
+        # K steps in one graph: the timed region is a single replay
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                step(i)
+        # per-call duration of the decode path (eager, events on the stream)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        clocks = ClockSampler(local)
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < 1.5:   # clocks settle under load
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev[0].record(stream)
+        graph.replay()
+        ev[1].record(stream)
+        ev[1].synchronize()
+        clk = clocks.stop()
+        ms = ev[0].elapsed_time(ev[1])
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        ops.check_device_errors(dev)
+
+        # e2e: public API with pinned host buffers, copies inside the timed region
+        q_host = sets[0][0].cpu().pin_memory()
+        bt_host = bt.cpu().pin_memory()
+        ctx_host = ctx.cpu().pin_memory()
+        out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        q_dev = torch.empty_like(sets[0][0])
+        bt_dev, ctx_dev = torch.empty_like(bt), torch.empty_like(ctx)
+        kn_host = sets[0][3].cpu().pin_memory()
+        vn_host = sets[0][4].cpu().pin_memory()
+        sm_host = sm.cpu().pin_memory()
+        kn_dev, vn_dev, sm_dev = (torch.empty_like(sets[0][3]), torch.empty_like(sets[0][4]),
+                                  torch.empty_like(sm))
+        _, kp0, vp0, _, _ = sets[0]
+
+        def e2e_step():
+            q_dev.copy_(q_host, non_blocking=True)
+            bt_dev.copy_(bt_host, non_blocking=True)
+            ctx_dev.copy_(ctx_host, non_blocking=True)
+            if fused:
+                kn_dev.copy_(kn_host, non_blocking=True)
+                vn_dev.copy_(vn_host, non_blocking=True)
+                sm_dev.copy_(sm_host, non_blocking=True)
+                o = irb.paged_decode_write(q_dev, kn_dev, vn_dev, kp0, vp0, sm_dev, bt_dev,
+                                           ctx_dev, w.scale, w.block_size, ws=ws)
+            else:
+                o = irb.paged_decode(q_dev, kp0, vp0, bt_dev, ctx_dev, w.scale, w.block_size,
+                                     ws=ws)
+            out_host.copy_(o, non_blocking=True)
+
+        for _ in range(max(args.warmup, 3)):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        ev[0].record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ev[1].record(stream)
+        ev[1].synchronize()
+        e2e_ms = ev[0].elapsed_time(ev[1])
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        h2d = (q_host.numel() * q_host.element_size() + bt_host.numel() * 4 +
+               ctx_host.numel() * 4)
+        if fused:
+            h2d += 2 * kn_host.numel() * kn_host.element_size() + sm_host.numel() * 8
+        d2h = out_host.numel() * out_host.element_size()
+
+    path, ctas, _ = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale)
+    peak, peak_kind = measured_peaks()
+    per_step_ms = ms / args.steps
+    value = world * nbytes * args.steps / (ms / 1e3) / 1e9
+    per_gpu = nbytes / (per_step_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_step_ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1)*0.5 q/K/V, uniform context lengths, random block "
+                "tables (no dataset: the reference benchmarks none)",
+        "config": {
+            "workload": {"c2": "C2: Qwen2.5-7B attention (28 q / 4 kv heads, head_dim 128), "
+                               "B=64/GPU, ctx U[512,4096], block 16, 32768-block pool",
+                         "c3": "C3: fused K/V write + decode, B=256/GPU, ctx U[128,2048], "
+                               "~30% shared prefixes",
+                         "c4": "C4: B=4 x ctx 32768 per GPU"}[args.config],
+            "global_batch": w.batch * world,
+            "batch_per_gpu": w.batch,
+            "tokens_per_gpu": int(w.context_lens.sum()),
+            "bytes_per_step_per_gpu": nbytes,
+            "parallelism": f"sequence-sharded x{world}, no collective",
+            "l2": "inputs larger than L2: >=200 MB of K/V per step, 3 rotating pool sets",
+            "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
+            "kernel_path": {1: "cuda-core", 2: "tma+mma.sync"}[path],
+            "ctas_per_kv_head": ctas,
+        },
+        "decode_tok_s_per_layer": round(world * w.batch / (per_step_ms / 1e3), 1),
+        "hbm_frac_per_gpu": round(per_gpu / peak, 4),
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(per_gpu, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(per_gpu / peak, 4),
+            "peak_kind": peak_kind,
+            "traffic": traffic_from_profiles(args.config),
+            "scope": "one decode call (decode kernel + merge kernel), per GPU",
+        },
+        "e2e": {
+            "value": round(world * nbytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(e2e_ms / args.steps, 5),
+        },
+        "clocks": clk,
+        "gpu_launches": 2 * args.steps,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs, secs, n = time_cpu_oracle(w, steps=10 ** 6, warmup=1, budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = {
+            "value": round(gbs, 4), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+            "sample": f"oracle naive path (gather+repeat_kv+softmax, numpy fp32) on {n} "
+                      f"single-sequence samples of {args.config} ({secs:.1f} s), bytes "
+                      f"counted at the workload's bf16 size",
+            "host_cpus": os.cpu_count(),
+        }
+    if world > 1:
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def traffic_from_profiles(config):
+    """DRAM bytes per decode call from the committed ncu summary, if present."""
+    f = ROOT / "profiles" / f"decode_{config}_traffic.json"
+    if f.exists():
+        try:
+            return json.loads(f.read_text()).get("dram_bytes_per_call")
+        except Exception:  # noqa: BLE001
+            return None
+    return None
+
+
+def run_reference(args):
+    world, rank, _ = dist_info()
+    if rank != 0:
+        return
+    w = make_workload(args.config, 0)
+    gbs, secs, n = time_cpu_oracle(w, steps=args.steps, warmup=args.warmup)
+    per_step = secs / max(n, 1)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 4),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": n,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_step * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (same generator and geometry as the GPU arm)",
+        "config": {"workload": f"{args.config} geometry, one sequence per step (bounded sample)",
+                   "global_batch": w.batch},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cpu_threads(),
+                         "kind": "port",
+                         "sample": "reference naive CPU path restated in oracle/ (numpy): "
+                                   "one sequence of the workload per step"},
+        "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

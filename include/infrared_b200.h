@@ -1,0 +1,217 @@
+/*
+ * infrared_b200 — C ABI of the B200 paged-decode attention path.
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, element
+ * counts and strides (in elements, 64-bit), launches only on the given
+ * stream, never synchronises and never allocates, so every call can sit
+ * inside a CUDA graph capture. The caller owns every buffer, including the
+ * workspace of the decode calls (size it with ir_paged_decode_workspace_size).
+ *
+ * Return value: IR_OK (0) or a non-zero IR_ERR_* status for a bad argument,
+ * an unsupported shape or a CUDA launch error; ir_last_error() gives the
+ * message of the calling thread's last failure. Errors found on the device
+ * (a block id or slot outside the pool, a context longer than the block
+ * table, metadata that is not block structured) never trap: the kernel
+ * skips the access and ORs an IR_DEVERR_* bit into the caller's int32
+ * `err_flag` word, which the host reads when it chooses (outside capture).
+ *
+ * Pool layout (one layer): k_pool / v_pool are [num_slots, num_kv_heads,
+ * head_dim] contiguous, slot = block_id * block_size + offset — the layout of
+ * PagedKVPool (infrared/cache/paged_kv_cache.py:30-46) with the layer index
+ * already applied by the caller (pointer of pool.k[layer]).
+ */
+#ifndef INFRARED_B200_H_
+#define INFRARED_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* ir_stream_t; /* == cudaStream_t */
+
+/* element types */
+#define IR_DTYPE_F32 0
+#define IR_DTYPE_BF16 1
+#define IR_DTYPE_F16 2
+
+/* host-side status codes */
+#define IR_OK 0
+#define IR_ERR_INVALID_ARG 1
+#define IR_ERR_UNSUPPORTED 2
+#define IR_ERR_CUDA 3
+#define IR_ERR_WORKSPACE 4
+
+/* device-side error bits ORed into *err_flag */
+#define IR_DEVERR_BLOCK_ID 0x1      /* block table entry outside [0, num_blocks) */
+#define IR_DEVERR_CONTEXT_LEN 0x2   /* context_len < 0 or > max_blocks * block_size */
+#define IR_DEVERR_SLOT 0x4          /* slot_mapping entry outside [0, num_slots) */
+#define IR_DEVERR_NOT_BLOCKED 0x8   /* gather_slots row is not block structured */
+#define IR_DEVERR_MASK 0x10         /* decode mask row is not a prefix of zeros */
+#define IR_DEVERR_TIMEOUT 0x20      /* a pipeline wait ran past its time limit */
+#define IR_DEVERR_WRITE_SLOT 0x40   /* fused write: slot is not the tail position */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int ir_version(void);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* ir_last_error(void);
+
+/* Number of device-side error bits, names by bit index (0-based). */
+const char* ir_deverr_name(int bit);
+
+/*
+ * Scatter this step's new K/V rows into the pool:
+ *   k_pool[slot_mapping[i], h, :] = k[i, h, :]   (same for v)
+ * Replaces PagedKVPool.write (infrared/cache/paged_kv_cache.py:48-57).
+ * k, v: [num_tokens, num_kv_heads, head_dim] with row stride k_stride /
+ * v_stride (elements) between tokens and [num_kv_heads, head_dim]
+ * contiguous. A negative slot skips the row (padding); a slot >= num_slots
+ * is skipped and flagged IR_DEVERR_SLOT. Duplicate slots: the rows must be
+ * identical (CUDA-graph pad rows repeat row 0), otherwise which row lands is
+ * unspecified.
+ */
+int ir_cache_write(const void* k, const void* v, int64_t k_stride,
+                   int64_t v_stride, void* k_pool, void* v_pool,
+                   const int64_t* slot_mapping, int64_t num_tokens,
+                   int num_kv_heads, int head_dim, int64_t num_slots,
+                   int dtype, int32_t* err_flag, ir_stream_t stream);
+
+/*
+ * Gather pool rows by slot: out[i, h, :] = pool[slots[i], h, :].
+ * Replaces PagedKVPool.gather (infrared/cache/paged_kv_cache.py:59-72) for
+ * one of k or v; out is [num_rows, num_kv_heads, head_dim] contiguous. A
+ * slot outside [0, num_slots) gives a zero row and sets IR_DEVERR_SLOT.
+ */
+int ir_cache_gather(void* out, const void* pool, const int64_t* slots,
+                    int64_t num_rows, int num_kv_heads, int head_dim,
+                    int64_t num_slots, int dtype, int32_t* err_flag,
+                    ir_stream_t stream);
+
+/*
+ * Turn the reference seam's per-forward metadata into block form.
+ * gather_slots [B, T] int64 (row stride gs_stride) and the additive decode
+ * mask [B, 1, 1, T] (row stride mask_stride, dtype mask_dtype) as built by
+ * PagedBatchEngine._decode_logits_eager (infrared/engine/paged_engine.py:
+ * 300-315) or build_decode_static_inputs (infrared/engine/cuda_graph.py:
+ * 105-155) become
+ *   context_lens[b]       = number of zero mask columns of row b
+ *   block_tables[b, j]    = gather_slots[b, j*block_size] / block_size
+ *                           (0 for blocks past the context)
+ * block_tables is [B, ceil(T/block_size)] int32 with row stride bt_stride.
+ * Rows whose valid slots are not bt[p/bs]*bs + p%bs set
+ * IR_DEVERR_NOT_BLOCKED; masks that are not a prefix of zeros set
+ * IR_DEVERR_MASK.
+ */
+int ir_derive_block_metadata(const int64_t* gather_slots, int64_t gs_stride,
+                             const void* mask, int64_t mask_stride,
+                             int mask_dtype, int batch, int64_t t,
+                             int block_size, int32_t* block_tables,
+                             int64_t bt_stride, int32_t* context_lens,
+                             int32_t* err_flag, ir_stream_t stream);
+
+/* Shape of one decode call (shared by the decode entry points). */
+typedef struct ir_decode_shape {
+  int batch;          /* B sequences, one query token each */
+  int num_heads;      /* H query heads */
+  int num_kv_heads;   /* Hkv; H % Hkv == 0, group = H / Hkv (<= 16) */
+  int head_dim;       /* D: 64 or 128 */
+  int block_size;     /* tokens per block */
+  int max_blocks;     /* columns of block_tables that may be read */
+  int64_t bt_stride;  /* row stride of block_tables (elements) */
+  int64_t q_stride;   /* stride between sequences in q (elements); [H, D] contiguous */
+  int64_t out_stride; /* stride between sequences in out (elements) */
+  int64_t num_slots;  /* rows of the pool (num_blocks * block_size) */
+  float scale;        /* softmax scale, usually head_dim ** -0.5 */
+  int dtype;          /* IR_DTYPE_* of q, pools and out */
+} ir_decode_shape;
+
+/* Bytes of workspace the decode calls need for this shape on the current
+ * device (0 on an invalid shape; the workspace must be 256-byte aligned).
+ * It holds the tile prefix and the partials of sequences split across CTAs;
+ * it needs no initialisation and is dead after the call's merge kernel. */
+size_t ir_paged_decode_workspace_size(const ir_decode_shape* shape);
+
+/* Kernel choice for this shape on the current device: *path = 1 (CUDA-core
+ * kernel: fp32, groups of 9-16, other block sizes) or 2 (TMA + mma kernel:
+ * bf16/fp16, group <= 8, block_size 8 or a multiple of 16), and the number
+ * of CTAs each kv head's tiles are divided among. No reference counterpart
+ * (the gate of the reference is _should_use_triton,
+ * infrared/model/triton_attention.py:68-76). */
+int ir_paged_decode_plan(const ir_decode_shape* shape, int* path,
+                         int* ctas_per_kv_head);
+
+/* Process-wide kernel override for testing and tuning: 0 = automatic,
+ * 1 = always the CUDA-core kernel, 2 = the TMA kernel (calls whose shape is
+ * not eligible then fail with IR_ERR_UNSUPPORTED). */
+int ir_set_decode_path(int path);
+
+/*
+ * Decode attention of one query token per sequence over its paged history:
+ *   out[b, h, :] = softmax_j(q[b, h, :] . K[slot_j, h / G, :] * scale) V[slot_j, h / G, :]
+ * over the context_lens[b] positions j whose slots come from block_tables.
+ * Replaces the decode read of paged_attention (infrared/model/
+ * triton_attention.py:81-107): _paged_attention_naive (:110-129) and
+ * _paged_attention_triton (:310-359). A sequence with context_len 0 gets a
+ * zero row (the l_safe convention of the reference kernel, :293-297).
+ * Work is split across the GPU's SMs in equal token shares; sequences that
+ * span several CTAs are combined with a log-sum-exp merge in `workspace`.
+ */
+int ir_paged_decode(void* out, const void* q, const void* k_pool,
+                    const void* v_pool, const int32_t* block_tables,
+                    const int32_t* context_lens, const ir_decode_shape* shape,
+                    void* workspace, size_t workspace_bytes,
+                    int32_t* err_flag, ir_stream_t stream);
+
+/*
+ * ir_paged_decode fused with the cache write of this step's K/V:
+ * k_new / v_new [B, Hkv, D] (row stride kv_stride) are written to pool slot
+ * slot_mapping[b] and used as the key/value of position context_lens[b]-1.
+ * slot_mapping[b] must be the tail slot of sequence b (the engine's
+ * invariant, infrared/engine/paged_engine.py:303-305); otherwise
+ * IR_DEVERR_WRITE_SLOT is set. Replaces the write + read of paged_attention
+ * (infrared/model/triton_attention.py:100-107) in one launch.
+ */
+int ir_paged_decode_write(void* out, const void* q, void* k_pool, void* v_pool,
+                          const void* k_new, const void* v_new,
+                          int64_t kv_stride, const int64_t* slot_mapping,
+                          const int32_t* block_tables,
+                          const int32_t* context_lens,
+                          const ir_decode_shape* shape, void* workspace,
+                          size_t workspace_bytes, int32_t* err_flag,
+                          ir_stream_t stream);
+
+/*
+ * Decode attention returning the softmax-normalised fp32 output and its
+ * log-sum-exp instead of the final row: o [B, H, D] fp32 contiguous,
+ * lse [B, H] fp32 natural log (-inf for an empty context, o = 0). These are
+ * the partials of a KV range held on one GPU; ir_lse_merge combines ranges.
+ * No reference counterpart: the reference defers split-KV
+ * (infrared docs/research/t4-triton-cudagraph-api.md:130).
+ */
+int ir_paged_decode_lse(float* o, float* lse, const void* q,
+                        const void* k_pool, const void* v_pool,
+                        const int32_t* block_tables,
+                        const int32_t* context_lens,
+                        const ir_decode_shape* shape, void* workspace,
+                        size_t workspace_bytes, int32_t* err_flag,
+                        ir_stream_t stream);
+
+/*
+ * Combine P partials: out[b, h, :] = sum_p w_p o_parts[p, b, h, :] with
+ * w_p = exp(lse_parts[p, b, h] - LSE), LSE = log sum_p exp(lse_parts[p]).
+ * o_parts [P, B, H, D] fp32, lse_parts [P, B, H] fp32 contiguous; out is
+ * [B, H, D] of `dtype` with sequence stride out_stride. Rows whose partials
+ * are all -inf become zero. No reference counterpart (see above).
+ */
+int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
+                 const float* lse_parts, int num_parts, int batch,
+                 int num_heads, int head_dim, int dtype, ir_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INFRARED_B200_H_ */

@@ -1,0 +1,200 @@
+// K/V pool scatter (cache write), gather, and block-metadata derivation.
+//
+// Rows are moved in 16-byte vectors when every row start is 16-byte aligned
+// (the usual case: [Hkv, D] rows of 512 B - 1 KB), else element by element.
+// Each thread moves one vector of one row of K and the same vector of V, so
+// a warp writes 512 contiguous bytes of a pool row.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace irb {
+
+namespace {
+
+template <typename V>
+__global__ void cache_write_kernel(const V* __restrict__ k,
+                                   const V* __restrict__ v, int64_t k_stride,
+                                   int64_t v_stride, V* __restrict__ kp,
+                                   V* __restrict__ vp,
+                                   const int64_t* __restrict__ slots,
+                                   int64_t n, int row_vecs, int64_t num_slots,
+                                   int32_t* err) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n * row_vecs) return;
+  const int64_t tok = i / row_vecs;
+  const int c = static_cast<int>(i - tok * row_vecs);
+  const int64_t s = slots[tok];
+  if (s < 0) return;  // padding row
+  if (s >= num_slots) {
+    if (c == 0) set_err(err, IR_DEVERR_SLOT);
+    return;
+  }
+  kp[s * row_vecs + c] = k[tok * k_stride + c];
+  vp[s * row_vecs + c] = v[tok * v_stride + c];
+}
+
+template <typename V>
+__global__ void cache_gather_kernel(V* __restrict__ out,
+                                    const V* __restrict__ pool,
+                                    const int64_t* __restrict__ slots,
+                                    int64_t n, int row_vecs, int64_t num_slots,
+                                    int32_t* err) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n * row_vecs) return;
+  const int64_t r = i / row_vecs;
+  const int c = static_cast<int>(i - r * row_vecs);
+  const int64_t s = slots[r];
+  if (s < 0 || s >= num_slots) {
+    if (c == 0) set_err(err, IR_DEVERR_SLOT);
+    out[i] = V{};
+    return;
+  }
+  out[i] = pool[s * row_vecs + c];
+}
+
+// Mask element is "allowed" iff it is +0 or -0 (any float width).
+__device__ __forceinline__ bool mask_zero(const void* mask, int elem_bytes,
+                                          int64_t idx) {
+  if (elem_bytes == 4)
+    return (reinterpret_cast<const uint32_t*>(mask)[idx] & 0x7fffffffu) == 0u;
+  return (reinterpret_cast<const uint16_t*>(mask)[idx] & 0x7fffu) == 0u;
+}
+
+__global__ void derive_metadata_kernel(const int64_t* __restrict__ gs,
+                                       int64_t gs_stride,
+                                       const void* __restrict__ mask,
+                                       int64_t mask_stride, int elem_bytes,
+                                       int64_t T, int bs,
+                                       int32_t* __restrict__ bt,
+                                       int64_t bt_stride,
+                                       int32_t* __restrict__ ctx_out,
+                                       int32_t* err) {
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int64_t* row = gs + b * gs_stride;
+  __shared__ int64_t s_count[32], s_first[32];
+  int64_t count = 0, first_nz = T;
+  for (int64_t t = tid; t < T; t += blockDim.x) {
+    if (mask_zero(mask, elem_bytes, b * mask_stride + t))
+      ++count;
+    else if (t < first_nz)
+      first_nz = t;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    count += __shfl_xor_sync(0xffffffffu, count, o);
+    first_nz = min(first_nz, __shfl_xor_sync(0xffffffffu, first_nz, o));
+  }
+  const int warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    s_count[warp] = count;
+    s_first[warp] = first_nz;
+  }
+  __syncthreads();
+  count = 0;
+  first_nz = T;
+  for (int w = 0; w < nw; ++w) {
+    count += s_count[w];
+    first_nz = min(first_nz, s_first[w]);
+  }
+  // a decode mask is a prefix of zeros: the first blocked column is `count`
+  if (tid == 0 && first_nz < count) set_err(err, IR_DEVERR_MASK);
+  const int64_t ctx = count;
+  if (tid == 0) ctx_out[b] = static_cast<int32_t>(ctx);
+  const int64_t ncols = (T + bs - 1) / bs;
+  const int64_t nblk = (ctx + bs - 1) / bs;
+  bool bad = false;
+  for (int64_t j = tid; j < ncols; j += blockDim.x) {
+    int32_t id = 0;
+    if (j < nblk) {
+      const int64_t s0 = row[j * bs];
+      if (s0 < 0 || s0 % bs != 0 || s0 / bs > INT32_MAX) bad = true;
+      id = static_cast<int32_t>(s0 / bs);
+    }
+    bt[b * bt_stride + j] = id;
+  }
+  for (int64_t t = tid; t < ctx; t += blockDim.x) {
+    const int64_t s0 = row[(t / bs) * bs];
+    if (row[t] != (s0 / bs) * bs + t % bs) bad = true;
+  }
+  if (bad) set_err(err, IR_DEVERR_NOT_BLOCKED);
+}
+
+int grid_for(int64_t work, int threads) {
+  return static_cast<int>((work + threads - 1) / threads);
+}
+
+}  // namespace
+
+int launch_cache_write(const void* k, const void* v, int64_t k_stride,
+                       int64_t v_stride, void* k_pool, void* v_pool,
+                       const int64_t* slots, int64_t n, int row_elems,
+                       int64_t num_slots, int elem_bytes, int32_t* err,
+                       cudaStream_t stream) {
+  if (n == 0) return 0;
+  const int row_bytes = row_elems * elem_bytes;
+  const bool vec = (row_bytes % 16 == 0) && ((k_stride * elem_bytes) % 16 == 0) &&
+                   ((v_stride * elem_bytes) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(k) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(v) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(k_pool) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(v_pool) % 16 == 0);
+  const int threads = 256;
+  if (vec) {
+    const int rv = row_bytes / 16;
+    const int64_t ks = k_stride * elem_bytes / 16, vs = v_stride * elem_bytes / 16;
+    cache_write_kernel<uint4><<<grid_for(n * rv, threads), threads, 0, stream>>>(
+        static_cast<const uint4*>(k), static_cast<const uint4*>(v), ks, vs,
+        static_cast<uint4*>(k_pool), static_cast<uint4*>(v_pool), slots, n, rv,
+        num_slots, err);
+  } else if (elem_bytes == 4) {
+    cache_write_kernel<uint32_t><<<grid_for(n * row_elems, threads), threads, 0, stream>>>(
+        static_cast<const uint32_t*>(k), static_cast<const uint32_t*>(v), k_stride,
+        v_stride, static_cast<uint32_t*>(k_pool), static_cast<uint32_t*>(v_pool),
+        slots, n, row_elems, num_slots, err);
+  } else {
+    cache_write_kernel<uint16_t><<<grid_for(n * row_elems, threads), threads, 0, stream>>>(
+        static_cast<const uint16_t*>(k), static_cast<const uint16_t*>(v), k_stride,
+        v_stride, static_cast<uint16_t*>(k_pool), static_cast<uint16_t*>(v_pool),
+        slots, n, row_elems, num_slots, err);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_cache_gather(void* out, const void* pool, const int64_t* slots,
+                        int64_t n, int row_elems, int64_t num_slots,
+                        int elem_bytes, int32_t* err, cudaStream_t stream) {
+  if (n == 0) return 0;
+  const int row_bytes = row_elems * elem_bytes;
+  const int threads = 256;
+  const bool vec = (row_bytes % 16 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(pool) % 16 == 0);
+  if (vec) {
+    const int rv = row_bytes / 16;
+    cache_gather_kernel<uint4><<<grid_for(n * rv, threads), threads, 0, stream>>>(
+        static_cast<uint4*>(out), static_cast<const uint4*>(pool), slots, n, rv,
+        num_slots, err);
+  } else if (elem_bytes == 4) {
+    cache_gather_kernel<uint32_t><<<grid_for(n * row_elems, threads), threads, 0, stream>>>(
+        static_cast<uint32_t*>(out), static_cast<const uint32_t*>(pool), slots, n,
+        row_elems, num_slots, err);
+  } else {
+    cache_gather_kernel<uint16_t><<<grid_for(n * row_elems, threads), threads, 0, stream>>>(
+        static_cast<uint16_t*>(out), static_cast<const uint16_t*>(pool), slots, n,
+        row_elems, num_slots, err);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_derive_metadata(const int64_t* gs, int64_t gs_stride,
+                           const void* mask, int64_t mask_stride,
+                           int mask_elem_bytes, int B, int64_t T, int bs,
+                           int32_t* bt, int64_t bt_stride, int32_t* ctx,
+                           int32_t* err, cudaStream_t stream) {
+  if (B == 0) return 0;
+  derive_metadata_kernel<<<B, 256, 0, stream>>>(gs, gs_stride, mask, mask_stride,
+                                                mask_elem_bytes, T, bs, bt,
+                                                bt_stride, ctx, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace irb

@@ -1,0 +1,456 @@
+// C ABI of infrared_b200 (declared in include/infrared_b200.h).
+//
+// Argument validation, device-property caching, TMA descriptor encoding,
+// workspace layout and kernel dispatch. Nothing here allocates or
+// synchronises; every launch goes to the caller's stream.
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "decode_common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_status(int e, const char* what) {
+  if (e == 0) return IR_OK;
+  return fail(IR_ERR_CUDA, std::string(what) + ": " +
+                               cudaGetErrorString(static_cast<cudaError_t>(e)));
+}
+
+int elem_bytes(int dtype) {
+  switch (dtype) {
+    case IR_DTYPE_F32: return 4;
+    case IR_DTYPE_BF16:
+    case IR_DTYPE_F16: return 2;
+    default: return 0;
+  }
+}
+
+bool aligned(const void* p, size_t n) {
+  return (reinterpret_cast<uintptr_t>(p) % n) == 0;
+}
+
+// ------------------------------------------------------------ device cache
+
+std::mutex g_mu;
+std::map<std::pair<int, int>, int> g_cache;  // (device, key) -> value
+int g_forced_path = 0;
+
+int cached(int key, int (*compute)(int), int arg, int* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_cache.find({dev, key});
+  if (it != g_cache.end()) {
+    *out = it->second;
+    return 0;
+  }
+  const int v = compute(arg);
+  g_cache[{dev, key}] = v;
+  *out = v;
+  return 0;
+}
+
+int sm_count_now(int) {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 1;
+}
+
+// key encoding for the occupancy cache: path(2 bits) dtype(2) D==128(1) bs8(1)
+int occ_compute(int key) {
+  const int path = key & 3, dtype = (key >> 2) & 3, d128 = (key >> 4) & 1,
+            bs8 = (key >> 5) & 1;
+  const int D = d128 ? 128 : 64;
+  if (path == 2) return irb::decode_tma_occupancy(dtype, D, bs8 ? 8 : 16);
+  return irb::decode_generic_occupancy(dtype, D);
+}
+
+// ------------------------------------------------------------ TMA encode
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn,
+                                cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode;
+}
+
+// [num_slots, Hkv, D] pool as a 3-D map with [box_rows x 1 x 64] boxes and
+// the 128-byte swizzle.
+bool make_pool_map(CUtensorMap* map, const void* pool, int64_t num_slots,
+                   int hkv, int d, int dtype, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d),
+                              static_cast<cuuint64_t>(hkv),
+                              static_cast<cuuint64_t>(num_slots)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
+                                 static_cast<cuuint64_t>(hkv) * d * 2};
+  const cuuint32_t box[3] = {64, 1, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == IR_DTYPE_BF16
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(pool), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------ planning
+
+struct Plan {
+  int path;  // 1 generic, 2 tma
+  int G;     // CTAs per kv head
+  size_t prefix_off, lse_off, o_off, bytes;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+int check_shape(const ir_decode_shape* s) {
+  if (!s) return fail(IR_ERR_INVALID_ARG, "shape is null");
+  if (s->batch < 0) return fail(IR_ERR_INVALID_ARG, "batch < 0");
+  if (s->num_heads <= 0 || s->num_kv_heads <= 0 ||
+      s->num_heads % s->num_kv_heads != 0)
+    return fail(IR_ERR_INVALID_ARG,
+                "num_heads must be a positive multiple of num_kv_heads");
+  if (s->num_heads / s->num_kv_heads > 16)
+    return fail(IR_ERR_UNSUPPORTED, "GQA group larger than 16");
+  if (s->head_dim != 64 && s->head_dim != 128)
+    return fail(IR_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (s->block_size <= 0) return fail(IR_ERR_INVALID_ARG, "block_size <= 0");
+  if (s->max_blocks < 0) return fail(IR_ERR_INVALID_ARG, "max_blocks < 0");
+  if (s->bt_stride < s->max_blocks)
+    return fail(IR_ERR_INVALID_ARG, "bt_stride < max_blocks");
+  const int64_t row = static_cast<int64_t>(s->num_heads) * s->head_dim;
+  if (s->q_stride < row) return fail(IR_ERR_INVALID_ARG, "q_stride < H*D");
+  if (s->out_stride < row) return fail(IR_ERR_INVALID_ARG, "out_stride < H*D");
+  if (s->num_slots < s->block_size || s->num_slots % s->block_size != 0)
+    return fail(IR_ERR_INVALID_ARG,
+                "num_slots must be a positive multiple of block_size");
+  if (elem_bytes(s->dtype) == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
+  if (static_cast<int64_t>(s->max_blocks) * s->block_size > INT32_MAX)
+    return fail(IR_ERR_UNSUPPORTED, "max_blocks * block_size overflows int32");
+  return IR_OK;
+}
+
+bool tma_eligible(const ir_decode_shape* s) {
+  const int n_rep = s->num_heads / s->num_kv_heads;
+  return (s->dtype == IR_DTYPE_BF16 || s->dtype == IR_DTYPE_F16) &&
+         n_rep <= 8 && (s->block_size == 8 || s->block_size % 16 == 0) &&
+         s->num_slots <= INT32_MAX && (s->q_stride % 2) == 0;
+}
+
+int make_plan(const ir_decode_shape* s, Plan* p) {
+  int rc = check_shape(s);
+  if (rc) return rc;
+  int path = tma_eligible(s) ? 2 : 1;
+  if (g_forced_path == 1) path = 1;
+  if (g_forced_path == 2) {
+    if (path != 2)
+      return fail(IR_ERR_UNSUPPORTED, "TMA path forced but shape not eligible");
+  }
+  int sms = 1, occ = 1;
+  int e = cached(-1, sm_count_now, 0, &sms);
+  if (e) return cuda_status(e, "cudaGetDevice");
+  const int key = path | (s->dtype << 2) | ((s->head_dim == 128) << 4) |
+                  ((s->block_size == 8) << 5);
+  e = cached(key, occ_compute, key, &occ);
+  if (e) return cuda_status(e, "cudaGetDevice");
+  int G = (sms * occ) / s->num_kv_heads;
+  if (G < 1) G = 1;
+  if (G > 65535) G = 65535;
+  p->path = path;
+  p->G = G;
+  const int64_t B = s->batch, H = s->num_heads, D = s->head_dim;
+  const int64_t slots = static_cast<int64_t>(s->num_kv_heads) * (G + B) *
+                        (H / s->num_kv_heads);
+  p->prefix_off = 0;
+  p->lse_off = align256(static_cast<size_t>(B + 1) * 8);
+  p->o_off = p->lse_off + align256(static_cast<size_t>(slots) * 4);
+  p->bytes = p->o_off + align256(static_cast<size_t>(slots * D) * 4);
+  return IR_OK;
+}
+
+enum class Mode { kFinal, kLse, kWrite };
+
+int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
+                const void* q, const void* k_pool, const void* v_pool,
+                const void* k_new, const void* v_new, int64_t kv_stride,
+                const int64_t* slot_mapping, const int32_t* block_tables,
+                const int32_t* context_lens, const ir_decode_shape* s,
+                void* workspace, size_t workspace_bytes, int32_t* err,
+                cudaStream_t stream) {
+  Plan plan;
+  int rc = make_plan(s, &plan);
+  if (rc) return rc;
+  if (s->batch == 0) return IR_OK;
+  if (!q || !k_pool || !v_pool || !context_lens ||
+      (s->max_blocks > 0 && !block_tables))
+    return fail(IR_ERR_INVALID_ARG, "null input pointer");
+  if (mode == Mode::kLse ? (!lse_o || !lse_out) : !out)
+    return fail(IR_ERR_INVALID_ARG, "null output pointer");
+  if (mode == Mode::kWrite && (!k_new || !v_new || !slot_mapping))
+    return fail(IR_ERR_INVALID_ARG, "null k_new / v_new / slot_mapping");
+  if (mode == Mode::kWrite && kv_stride < static_cast<int64_t>(s->num_kv_heads) * s->head_dim)
+    return fail(IR_ERR_INVALID_ARG, "kv_stride < Hkv*D");
+  if (!workspace || workspace_bytes < plan.bytes)
+    return fail(IR_ERR_WORKSPACE, "workspace smaller than ir_paged_decode_workspace_size");
+  if (!aligned(workspace, 256))
+    return fail(IR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  const int eb = elem_bytes(s->dtype);
+  if (plan.path == 2) {
+    // TMA descriptors need 16-byte aligned pools; q fragments are read as
+    // 32-bit words; the fused write moves 16-byte vectors.
+    bool ok = aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4);
+    if (mode == Mode::kWrite)
+      ok = ok && aligned(k_new, 16) && aligned(v_new, 16) &&
+           (kv_stride * eb) % 16 == 0;
+    if (!ok) {
+      if (g_forced_path == 2)
+        return fail(IR_ERR_UNSUPPORTED, "TMA path forced but pointers misaligned");
+      plan.path = 1;
+      // the generic path may have a different CTA count: re-plan for sizing
+      int sms = 1, occ = 1;
+      cached(-1, sm_count_now, 0, &sms);
+      const int key = 1 | (s->dtype << 2) | ((s->head_dim == 128) << 4) |
+                      ((s->block_size == 8) << 5);
+      cached(key, occ_compute, key, &occ);
+      int G = (sms * occ) / s->num_kv_heads;
+      plan.G = G < 1 ? 1 : (G > plan.G ? plan.G : G);  // never exceed sized G
+    }
+  }
+  irb::DecodeArgs a{};
+  a.q = q;
+  a.q_stride = s->q_stride;
+  a.out = out;
+  a.out_stride = s->out_stride;
+  a.lse_o = lse_o;
+  a.lse_out = lse_out;
+  a.lse_mode = mode == Mode::kLse ? 1 : 0;
+  a.block_tables = block_tables;
+  a.bt_stride = s->bt_stride;
+  a.context_lens = context_lens;
+  a.B = s->batch;
+  a.H = s->num_heads;
+  a.Hkv = s->num_kv_heads;
+  a.n_rep = s->num_heads / s->num_kv_heads;
+  a.D = s->head_dim;
+  a.bs = s->block_size;
+  a.max_blocks = s->max_blocks;
+  a.num_slots = s->num_slots;
+  a.num_blocks = s->num_slots / s->block_size;
+  a.scale_log2 = s->scale * irb::kLog2e;
+  a.G = plan.G;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.ws_prefix = reinterpret_cast<int64_t*>(ws + plan.prefix_off);
+  a.ws_lse = reinterpret_cast<float*>(ws + plan.lse_off);
+  a.ws_o = reinterpret_cast<float*>(ws + plan.o_off);
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.k_new = mode == Mode::kWrite ? k_new : nullptr;
+  a.v_new = mode == Mode::kWrite ? v_new : nullptr;
+  a.kv_stride = kv_stride;
+  a.slot_mapping = slot_mapping;
+  a.err = err;
+
+  int e;
+  if (plan.path == 2) {
+    CUtensorMap tmk, tmv;
+    const int rows = s->block_size == 8 ? 8 : 16;
+    if (!make_pool_map(&tmk, k_pool, s->num_slots, s->num_kv_heads,
+                       s->head_dim, s->dtype, rows) ||
+        !make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads,
+                       s->head_dim, s->dtype, rows))
+      return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    e = irb::launch_decode_tma(tmk, tmv, a, s->dtype, stream);
+  } else {
+    e = irb::launch_decode_generic(a, s->dtype, stream);
+  }
+  if (e) return cuda_status(e, "decode kernel launch");
+  e = irb::launch_split_merge(a, s->dtype, stream);
+  if (e) return cuda_status(e, "merge kernel launch");
+  return IR_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ir_version(void) { return 100; }
+
+const char* ir_last_error(void) { return g_last_error.c_str(); }
+
+const char* ir_deverr_name(int bit) {
+  static const char* names[] = {"BLOCK_ID", "CONTEXT_LEN", "SLOT",
+                                "NOT_BLOCKED", "MASK", "TIMEOUT", "WRITE_SLOT"};
+  if (bit < 0 || bit >= static_cast<int>(sizeof(names) / sizeof(names[0])))
+    return "";
+  return names[bit];
+}
+
+int ir_set_decode_path(int path) {
+  if (path < 0 || path > 2) return fail(IR_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_forced_path = path;
+  return IR_OK;
+}
+
+int ir_paged_decode_plan(const ir_decode_shape* shape, int* path,
+                         int* ctas_per_kv_head) {
+  Plan p;
+  int rc = make_plan(shape, &p);
+  if (rc) return rc;
+  if (path) *path = p.path;
+  if (ctas_per_kv_head) *ctas_per_kv_head = p.G;
+  return IR_OK;
+}
+
+size_t ir_paged_decode_workspace_size(const ir_decode_shape* shape) {
+  Plan p;
+  if (make_plan(shape, &p)) return 0;
+  return p.bytes;
+}
+
+int ir_cache_write(const void* k, const void* v, int64_t k_stride,
+                   int64_t v_stride, void* k_pool, void* v_pool,
+                   const int64_t* slot_mapping, int64_t num_tokens,
+                   int num_kv_heads, int head_dim, int64_t num_slots,
+                   int dtype, int32_t* err_flag, ir_stream_t stream) {
+  const int eb = elem_bytes(dtype);
+  if (eb == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || num_slots < 0)
+    return fail(IR_ERR_INVALID_ARG, "bad sizes");
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (row > INT32_MAX) return fail(IR_ERR_UNSUPPORTED, "row too long");
+  if (num_tokens == 0) return IR_OK;
+  if (k_stride < row || v_stride < row)
+    return fail(IR_ERR_INVALID_ARG, "token stride < Hkv*D");
+  if (!k || !v || !k_pool || !v_pool || !slot_mapping)
+    return fail(IR_ERR_INVALID_ARG, "null pointer");
+  int e = irb::launch_cache_write(k, v, k_stride, v_stride, k_pool, v_pool,
+                                  slot_mapping, num_tokens,
+                                  static_cast<int>(row), num_slots, eb,
+                                  err_flag, stream);
+  return cuda_status(e, "cache write launch");
+}
+
+int ir_cache_gather(void* out, const void* pool, const int64_t* slots,
+                    int64_t num_rows, int num_kv_heads, int head_dim,
+                    int64_t num_slots, int dtype, int32_t* err_flag,
+                    ir_stream_t stream) {
+  const int eb = elem_bytes(dtype);
+  if (eb == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
+  if (num_rows < 0 || num_kv_heads <= 0 || head_dim <= 0 || num_slots < 0)
+    return fail(IR_ERR_INVALID_ARG, "bad sizes");
+  const int64_t row = static_cast<int64_t>(num_kv_heads) * head_dim;
+  if (row > INT32_MAX) return fail(IR_ERR_UNSUPPORTED, "row too long");
+  if (num_rows == 0) return IR_OK;
+  if (!out || !pool || !slots) return fail(IR_ERR_INVALID_ARG, "null pointer");
+  int e = irb::launch_cache_gather(out, pool, slots, num_rows,
+                                   static_cast<int>(row), num_slots, eb,
+                                   err_flag, stream);
+  return cuda_status(e, "cache gather launch");
+}
+
+int ir_derive_block_metadata(const int64_t* gather_slots, int64_t gs_stride,
+                             const void* mask, int64_t mask_stride,
+                             int mask_dtype, int batch, int64_t t,
+                             int block_size, int32_t* block_tables,
+                             int64_t bt_stride, int32_t* context_lens,
+                             int32_t* err_flag, ir_stream_t stream) {
+  const int eb = elem_bytes(mask_dtype);
+  if (eb == 0) return fail(IR_ERR_INVALID_ARG, "bad mask dtype");
+  if (batch < 0 || t < 0 || block_size <= 0)
+    return fail(IR_ERR_INVALID_ARG, "bad sizes");
+  if (t > INT32_MAX) return fail(IR_ERR_UNSUPPORTED, "T overflows int32");
+  if (batch == 0) return IR_OK;
+  if (bt_stride < (t + block_size - 1) / block_size || gs_stride < t ||
+      mask_stride < t)
+    return fail(IR_ERR_INVALID_ARG, "stride smaller than row length");
+  if (!gather_slots || !mask || !block_tables || !context_lens)
+    return fail(IR_ERR_INVALID_ARG, "null pointer");
+  int e = irb::launch_derive_metadata(gather_slots, gs_stride, mask,
+                                      mask_stride, eb, batch, t, block_size,
+                                      block_tables, bt_stride, context_lens,
+                                      err_flag, stream);
+  return cuda_status(e, "metadata launch");
+}
+
+int ir_paged_decode(void* out, const void* q, const void* k_pool,
+                    const void* v_pool, const int32_t* block_tables,
+                    const int32_t* context_lens, const ir_decode_shape* shape,
+                    void* workspace, size_t workspace_bytes,
+                    int32_t* err_flag, ir_stream_t stream) {
+  return decode_impl(Mode::kFinal, out, nullptr, nullptr, q, k_pool, v_pool,
+                     nullptr, nullptr, 0, nullptr, block_tables, context_lens,
+                     shape, workspace, workspace_bytes, err_flag, stream);
+}
+
+int ir_paged_decode_write(void* out, const void* q, void* k_pool, void* v_pool,
+                          const void* k_new, const void* v_new,
+                          int64_t kv_stride, const int64_t* slot_mapping,
+                          const int32_t* block_tables,
+                          const int32_t* context_lens,
+                          const ir_decode_shape* shape, void* workspace,
+                          size_t workspace_bytes, int32_t* err_flag,
+                          ir_stream_t stream) {
+  return decode_impl(Mode::kWrite, out, nullptr, nullptr, q, k_pool, v_pool,
+                     k_new, v_new, kv_stride, slot_mapping, block_tables,
+                     context_lens, shape, workspace, workspace_bytes, err_flag,
+                     stream);
+}
+
+int ir_paged_decode_lse(float* o, float* lse, const void* q,
+                        const void* k_pool, const void* v_pool,
+                        const int32_t* block_tables,
+                        const int32_t* context_lens,
+                        const ir_decode_shape* shape, void* workspace,
+                        size_t workspace_bytes, int32_t* err_flag,
+                        ir_stream_t stream) {
+  return decode_impl(Mode::kLse, nullptr, o, lse, q, k_pool, v_pool, nullptr,
+                     nullptr, 0, nullptr, block_tables, context_lens, shape,
+                     workspace, workspace_bytes, err_flag, stream);
+}
+
+int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
+                 const float* lse_parts, int num_parts, int batch,
+                 int num_heads, int head_dim, int dtype, ir_stream_t stream) {
+  if (elem_bytes(dtype) == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
+  if (num_parts <= 0 || batch < 0 || num_heads <= 0 || head_dim <= 0)
+    return fail(IR_ERR_INVALID_ARG, "bad sizes");
+  if (batch == 0) return IR_OK;
+  if (out_stride < static_cast<int64_t>(num_heads) * head_dim)
+    return fail(IR_ERR_INVALID_ARG, "out_stride < H*D");
+  if (!out || !o_parts || !lse_parts) return fail(IR_ERR_INVALID_ARG, "null pointer");
+  if (batch > 2147483647 || num_heads > 65535)
+    return fail(IR_ERR_UNSUPPORTED, "grid too large");
+  int e = irb::launch_lse_merge(out, out_stride, o_parts, lse_parts, num_parts,
+                                batch, num_heads, head_dim, dtype, stream);
+  return cuda_status(e, "lse merge launch");
+}
+
+}  // extern "C"

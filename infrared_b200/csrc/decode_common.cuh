@@ -1,0 +1,187 @@
+// Work partition and output conventions shared by the decode kernels.
+//
+// Units of work are 16-token "tiles" of one (sequence, kv-head) history:
+// sequence b has n_b = ceil(ctx_b / 16) tiles. For each kv head the tiles of
+// all sequences are laid end to end (prefix P_b = sum_{b' < b} n_b', total
+// T) and cut into G equal shares: CTA g of that kv head streams tiles
+// [start(g), start(g+1)) with start(g) = floor(g * T / G). A share may cover
+// the tail of one sequence, several whole sequences and the head of another;
+// each (CTA, sequence) piece is a "segment". A segment that is a whole
+// sequence writes the final row; any other segment writes a normalised fp32
+// partial and its log2-sum-exp into workspace slot g + b (unique: along the
+// monotone path of (g, b) pieces g + b strictly increases), and the merge
+// kernel combines the pieces of every sequence that spans several CTAs.
+#pragma once
+
+#include "common.cuh"
+
+namespace irb {
+
+constexpr int kTile = 16;  // tokens per tile
+
+struct DecodeArgs {
+  const void* q;
+  int64_t q_stride;
+  void* out;  // final output (dtype T) [B, H, D] with out_stride
+  int64_t out_stride;
+  float* lse_o;    // LSE mode: o [B, H, D] fp32 contiguous
+  float* lse_out;  // LSE mode: lse [B, H] natural log
+  int lse_mode;
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  const int32_t* context_lens;
+  int B, H, Hkv, n_rep, D, bs, max_blocks;
+  int64_t num_slots, num_blocks;
+  float scale_log2;  // scale * log2(e)
+  int G;             // CTAs per kv head
+  // workspace
+  int64_t* ws_prefix;  // [B + 1] tile prefix (written by CTA (0, 0))
+  float* ws_lse;       // [Hkv, G + B, n_rep] log2-sum-exp of partials
+  float* ws_o;         // [Hkv, G + B, n_rep, D] normalised partials
+  // pools (generic kernel reads them directly; fused write stores into them)
+  const void* k_pool;
+  const void* v_pool;
+  // fused cache write of this step's K/V (null when not fused)
+  const void* k_new;
+  const void* v_new;
+  int64_t kv_stride;
+  const int64_t* slot_mapping;
+  int32_t* err;
+};
+
+__device__ __forceinline__ int clamp_ctx(int c, const DecodeArgs& a) {
+  const int maxc = a.max_blocks * a.bs;
+  return c < 0 ? 0 : (c > maxc ? maxc : c);
+}
+
+__device__ __forceinline__ int tiles_of(const DecodeArgs& a, int b) {
+  return (clamp_ctx(a.context_lens[b], a) + kTile - 1) / kTile;
+}
+
+__device__ __forceinline__ int64_t share_start(int64_t g, int64_t total,
+                                               int G) {
+  return (g * total) / G;
+}
+
+// CTA whose share holds tile t (0 <= t < total).
+__device__ __forceinline__ int share_of(int64_t t, int64_t total, int G) {
+  return static_cast<int>(((t + 1) * G + total - 1) / total - 1);
+}
+
+struct RangeInfo {
+  int64_t total;    // T
+  int64_t start;    // first tile of this CTA
+  int64_t end;      // one past the last tile
+  int64_t p_first;  // prefix of b_first
+  int b_first;      // sequence holding tile `start`
+};
+
+// Block-wide exclusive scan of one int64 per thread (NT threads, NT % 32 == 0).
+template <int NT>
+__device__ __forceinline__ int64_t block_excl_scan(int64_t v, int64_t* sm,
+                                                   int64_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int64_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int64_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) sm[warp] = x;
+  __syncthreads();
+  int64_t before = 0, all = 0;
+#pragma unroll
+  for (int w = 0; w < NT / 32; ++w) {
+    const int64_t s = sm[w];
+    if (w < warp) before += s;
+    all += s;
+  }
+  __syncthreads();
+  *total = all;
+  return before + x - v;
+}
+
+// Find this CTA's share. All NT threads must call it. CTA (0, 0) also
+// publishes the tile prefix to the workspace and writes the rows of
+// sequences with no context (no CTA streams them).
+template <int NT, typename T>
+__device__ void find_share(const DecodeArgs& a, int g, int kvh, RangeInfo* ri,
+                           int64_t* sm_scan) {
+  const int tid = threadIdx.x;
+  // pass 1: total tiles (and context validation)
+  int64_t mine = 0;
+  for (int b = tid; b < a.B; b += NT) {
+    const int c = a.context_lens[b];
+    if (c < 0 || c > a.max_blocks * a.bs) set_err(a.err, IR_DEVERR_CONTEXT_LEN);
+    mine += tiles_of(a, b);
+  }
+  int64_t total = 0;
+  block_excl_scan<NT>(mine, sm_scan, &total);
+  const int64_t start = share_start(g, total, a.G);
+  const int64_t end = share_start(g + 1, total, a.G);
+  if (tid == 0) {
+    ri->total = total;
+    ri->start = start;
+    ri->end = end;
+    ri->b_first = -1;
+    ri->p_first = 0;
+  }
+  __syncthreads();
+  // pass 2: prefix of every sequence; locate `start`
+  const bool publish = (g == 0 && kvh == 0 && a.ws_prefix != nullptr);
+  int64_t running = 0;
+  for (int base = 0; base < a.B; base += NT) {
+    const int b = base + tid;
+    const int n = b < a.B ? tiles_of(a, b) : 0;
+    int64_t chunk_total = 0;
+    const int64_t p = running + block_excl_scan<NT>(n, sm_scan, &chunk_total);
+    if (b < a.B) {
+      if (publish) a.ws_prefix[b] = p;
+      if (n > 0 && p <= start && start < p + n) {
+        ri->b_first = b;
+        ri->p_first = p;
+      }
+      if (n == 0 && g == 0) {
+        // empty context: zero row (and lse = -inf) for this kv head's group
+        for (int i = 0; i < a.n_rep * a.D; ++i) {
+          const int h = kvh * a.n_rep + i / a.D, d = i % a.D;
+          if (a.lse_mode) {
+            a.lse_o[(static_cast<int64_t>(b) * a.H + h) * a.D + d] = 0.f;
+            if (d == 0) a.lse_out[static_cast<int64_t>(b) * a.H + h] = -INFINITY;
+          } else {
+            reinterpret_cast<T*>(a.out)[b * a.out_stride + h * a.D + d] =
+                DT<T>::from_f(0.f);
+          }
+        }
+      }
+    }
+    running += chunk_total;
+  }
+  if (publish && tid == 0) a.ws_prefix[a.B] = total;
+  __syncthreads();
+}
+
+// Write one output value of a segment: final row, LSE-mode row or partial.
+template <typename T>
+__device__ __forceinline__ void write_segment_value(const DecodeArgs& a,
+                                                   int kvh, int g, int b,
+                                                   bool whole, int n, int d,
+                                                   float val, float lse2) {
+  const int h = kvh * a.n_rep + n;
+  if (whole) {
+    if (a.lse_mode) {
+      a.lse_o[(static_cast<int64_t>(b) * a.H + h) * a.D + d] = val;
+      if (d == 0) a.lse_out[static_cast<int64_t>(b) * a.H + h] = lse2 * kLn2;
+    } else {
+      reinterpret_cast<T*>(a.out)[b * a.out_stride + static_cast<int64_t>(h) * a.D + d] =
+          DT<T>::from_f(val);
+    }
+  } else {
+    const int64_t slot =
+        static_cast<int64_t>(kvh) * (a.G + a.B) + g + b;
+    a.ws_o[(slot * a.n_rep + n) * a.D + d] = val;
+    if (d == 0) a.ws_lse[slot * a.n_rep + n] = lse2;
+  }
+}
+
+}  // namespace irb

@@ -1,0 +1,302 @@
+// Paged decode attention on CUDA cores for every dtype/shape the TMA kernel
+// does not take (fp32 pools, GQA groups of 9-16, block sizes other than 8 or a
+// multiple of 16), plus the two log-sum-exp merge kernels.
+//
+// The generic kernel uses the same balanced tile shares and segment outputs
+// as the TMA kernel (decode_common.cuh) so the split merge serves both. A CTA
+// of 128 threads walks its tiles in order: it stages the 16 K and V rows of a
+// tile in shared memory (gathered row by row through the block table),
+// computes the 16 x group scores with fp32 dot products, updates the
+// per-head online softmax (exp2 with the scale folded into log2 units) and
+// accumulates P.V with each thread owning one head-dim column.
+#include "decode_common.cuh"
+#include "kernels.h"
+
+namespace irb {
+
+namespace {
+
+constexpr int kGenThreads = 128;
+constexpr int kMaxGroup = 16;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kGenThreads)
+    decode_generic_kernel(const DecodeArgs a) {
+  constexpr int HPT = kGenThreads / D;            // head groups per column
+  constexpr int NH = (kMaxGroup + HPT - 1) / HPT;  // heads per thread
+  __shared__ float q_s[kMaxGroup][D];
+  __shared__ float k_s[kTile][D + 1];
+  __shared__ float v_s[kTile][D];
+  __shared__ float p_s[kMaxGroup][kTile];
+  __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
+  __shared__ RangeInfo ri;
+  __shared__ int64_t sm_scan[kGenThreads / 32];
+
+  const int kvh = blockIdx.x, g = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  find_share<kGenThreads, T>(a, g, kvh, &ri, sm_scan);
+  const int64_t start = ri.start, end = ri.end;
+  if (start >= end) return;
+
+  const int d = tid % D, hg = tid / D;
+  const T* kpool = reinterpret_cast<const T*>(a.k_pool);
+  const T* vpool = reinterpret_cast<const T*>(a.v_pool);
+  float acc[NH];
+  int b = ri.b_first;
+  int64_t pb = ri.p_first;
+  int nb = tiles_of(a, b);
+  int cur_b = -1;
+
+  for (int64_t t = start; t < end; ++t) {
+    while (t >= pb + nb) {
+      pb += nb;
+      ++b;
+      nb = tiles_of(a, b);
+    }
+    const int j = static_cast<int>(t - pb);
+    const int tok0 = j * kTile;
+    const int ctx = clamp_ctx(a.context_lens[b], a);
+    const int nvalid = min(kTile, ctx - tok0);
+    if (t == start || j == 0) {  // segment start
+      if (b != cur_b) {
+        cur_b = b;
+        const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_stride +
+                        static_cast<int64_t>(kvh * a.n_rep) * D;
+        for (int i = tid; i < a.n_rep * D; i += kGenThreads)
+          q_s[i / D][i % D] = DT<T>::to_f(qrow[i]);
+      }
+      if (tid < kMaxGroup) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < NH; ++k) acc[k] = 0.f;
+    }
+    // stage the tile's K and V rows
+    const int32_t* btr = a.block_tables + b * a.bt_stride;
+    for (int i = tid; i < kTile * D; i += kGenThreads) {
+      const int r = i / D, c = i % D;
+      float kv = 0.f, vv = 0.f;
+      if (r < nvalid) {
+        const int pos = tok0 + r;
+        const int id = btr[pos / a.bs];
+        if (a.k_new != nullptr && pos == ctx - 1) {
+          // fused cache write: the new token's K/V come from the inputs
+          const int64_t src = b * a.kv_stride + static_cast<int64_t>(kvh) * D + c;
+          const T kn = reinterpret_cast<const T*>(a.k_new)[src];
+          const T vn = reinterpret_cast<const T*>(a.v_new)[src];
+          kv = DT<T>::to_f(kn);
+          vv = DT<T>::to_f(vn);
+          const int64_t sw = a.slot_mapping[b];
+          const int64_t want = static_cast<int64_t>(id) * a.bs + pos % a.bs;
+          if (c == 0 && sw != want) set_err(a.err, IR_DEVERR_WRITE_SLOT);
+          if (sw >= 0 && sw < a.num_slots) {
+            const int64_t dst = (sw * a.Hkv + kvh) * D + c;
+            const_cast<T*>(kpool)[dst] = kn;
+            const_cast<T*>(vpool)[dst] = vn;
+          } else if (c == 0 && sw >= a.num_slots) {
+            set_err(a.err, IR_DEVERR_SLOT);
+          }
+        } else if (id >= 0 && id < a.num_blocks) {
+          const int64_t row = static_cast<int64_t>(id) * a.bs + pos % a.bs;
+          const int64_t off = (row * a.Hkv + kvh) * D + c;
+          kv = DT<T>::to_f(kpool[off]);
+          vv = DT<T>::to_f(vpool[off]);
+        } else if (c == 0) {
+          set_err(a.err, IR_DEVERR_BLOCK_ID);
+        }
+      }
+      k_s[r][c] = kv;
+      v_s[r][c] = vv;
+    }
+    __syncthreads();
+    for (int i = tid; i < kTile * a.n_rep; i += kGenThreads) {
+      const int r = i % kTile, n = i / kTile;
+      float s = 0.f;
+#pragma unroll 8
+      for (int c = 0; c < D; ++c) s = fmaf(q_s[n][c], k_s[r][c], s);
+      p_s[n][r] = r < nvalid ? s * a.scale_log2 : -INFINITY;
+    }
+    __syncthreads();
+    for (int n = warp; n < a.n_rep; n += kGenThreads / 32) {
+      const float s = lane < kTile ? p_s[n][lane] : -INFINITY;
+      float mx = s;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mold = m_s[n];
+      const float mnew = fmaxf(mold, mx);
+      const float muse = mnew == -INFINITY ? 0.f : mnew;
+      const float p = ex2(s - muse);
+      float sum = p;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float alpha = ex2(mold - muse);
+      __syncwarp();
+      if (lane < kTile) p_s[n][lane] = p;
+      if (lane == 0) {
+        l_s[n] = l_s[n] * alpha + sum;
+        m_s[n] = mnew;
+        alpha_s[n] = alpha;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < NH; ++k) {
+      const int n = hg + k * HPT;
+      if (n < a.n_rep) {
+        float x = acc[k] * alpha_s[n];
+#pragma unroll
+        for (int r = 0; r < kTile; ++r) x = fmaf(p_s[n][r], v_s[r][d], x);
+        acc[k] = x;
+      }
+    }
+    if (t == end - 1 || j == nb - 1) {  // segment end
+      const bool whole = (pb >= start) && (pb + nb <= end);
+#pragma unroll
+      for (int k = 0; k < NH; ++k) {
+        const int n = hg + k * HPT;
+        if (n < a.n_rep) {
+          const float M = m_s[n], Lsum = l_s[n];
+          const bool empty = (M == -INFINITY);
+          const float val = empty ? 0.f : acc[k] / Lsum;
+          const float lse2 = empty ? -INFINITY : M + log2f(Lsum);
+          write_segment_value<T>(a, kvh, g, b, whole, n, d, val, lse2);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+__global__ void split_merge_kernel(const DecodeArgs a) {
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int64_t pb = a.ws_prefix[b];
+  const int64_t nb = a.ws_prefix[b + 1] - pb;
+  const int64_t total = a.ws_prefix[a.B];
+  if (nb <= 0) return;
+  const int glo = share_of(pb, total, a.G);
+  const int ghi = share_of(pb + nb - 1, total, a.G);
+  if (glo == ghi) return;  // written whole by one CTA
+  const int64_t base = static_cast<int64_t>(kvh) * (a.G + a.B) + b;
+  for (int idx = threadIdx.x; idx < a.n_rep * a.D; idx += blockDim.x) {
+    const int n = idx / a.D, d = idx % a.D;
+    float M = -INFINITY;
+    for (int g = glo; g <= ghi; ++g) {
+      if (share_start(g, total, a.G) == share_start(g + 1, total, a.G)) continue;
+      M = fmaxf(M, a.ws_lse[(base + g) * a.n_rep + n]);
+    }
+    float val = 0.f, lse2 = -INFINITY;
+    if (M != -INFINITY) {
+      float lsum = 0.f, osum = 0.f;
+      for (int g = glo; g <= ghi; ++g) {
+        if (share_start(g, total, a.G) == share_start(g + 1, total, a.G)) continue;
+        const int64_t sl = base + g;
+        const float w = ex2(a.ws_lse[sl * a.n_rep + n] - M);
+        lsum += w;
+        osum += w * a.ws_o[(sl * a.n_rep + n) * a.D + d];
+      }
+      val = osum / lsum;
+      lse2 = M + log2f(lsum);
+    }
+    write_segment_value<T>(a, kvh, 0, b, true, n, d, val, lse2);
+  }
+}
+
+template <typename T>
+__global__ void lse_merge_kernel(T* out, int64_t out_stride,
+                                 const float* o_parts, const float* lse_parts,
+                                 int P, int B, int H, int D) {
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int64_t row = static_cast<int64_t>(b) * H + h;
+  const int64_t pstride = static_cast<int64_t>(B) * H;
+  float M = -INFINITY;
+  for (int p = 0; p < P; ++p) M = fmaxf(M, lse_parts[p * pstride + row]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float val = 0.f;
+    if (M != -INFINITY) {
+      float lsum = 0.f, osum = 0.f;
+      for (int p = 0; p < P; ++p) {
+        const float lp = lse_parts[p * pstride + row];
+        if (lp == -INFINITY) continue;
+        const float w = ex2((lp - M) * kLog2e);
+        lsum += w;
+        osum += w * o_parts[(p * pstride + row) * D + d];
+      }
+      val = osum / lsum;
+    }
+    out[b * out_stride + static_cast<int64_t>(h) * D + d] = DT<T>::from_f(val);
+  }
+}
+
+template <typename T>
+int launch_generic_t(const DecodeArgs& a, cudaStream_t s) {
+  dim3 grid(a.Hkv, a.G);
+  if (a.D == 128)
+    decode_generic_kernel<T, 128><<<grid, kGenThreads, 0, s>>>(a);
+  else
+    decode_generic_kernel<T, 64><<<grid, kGenThreads, 0, s>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <typename T>
+int occupancy_generic_t(int D) {
+  int n = 0;
+  cudaError_t e = D == 128 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                                 &n, decode_generic_kernel<T, 128>, kGenThreads, 0)
+                           : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                                 &n, decode_generic_kernel<T, 64>, kGenThreads, 0);
+  return (e == cudaSuccess && n > 0) ? n : 1;
+}
+
+}  // namespace
+
+int launch_decode_generic(const DecodeArgs& a, int dtype, cudaStream_t s) {
+  switch (dtype) {
+    case IR_DTYPE_F32: return launch_generic_t<float>(a, s);
+    case IR_DTYPE_BF16: return launch_generic_t<__nv_bfloat16>(a, s);
+    default: return launch_generic_t<__half>(a, s);
+  }
+}
+
+int decode_generic_occupancy(int dtype, int D) {
+  switch (dtype) {
+    case IR_DTYPE_F32: return occupancy_generic_t<float>(D);
+    case IR_DTYPE_BF16: return occupancy_generic_t<__nv_bfloat16>(D);
+    default: return occupancy_generic_t<__half>(D);
+  }
+}
+
+int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
+  dim3 grid(a.B, a.Hkv);
+  switch (dtype) {
+    case IR_DTYPE_F32: split_merge_kernel<float><<<grid, 128, 0, s>>>(a); break;
+    case IR_DTYPE_BF16: split_merge_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(a); break;
+    default: split_merge_kernel<__half><<<grid, 128, 0, s>>>(a); break;
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_lse_merge(void* out, int64_t out_stride, const float* o_parts,
+                     const float* lse_parts, int P, int B, int H, int D,
+                     int dtype, cudaStream_t s) {
+  dim3 grid(B, H);
+  const int threads = D >= 128 ? 128 : 64;
+  switch (dtype) {
+    case IR_DTYPE_F32:
+      lse_merge_kernel<float><<<grid, threads, 0, s>>>(
+          static_cast<float*>(out), out_stride, o_parts, lse_parts, P, B, H, D);
+      break;
+    case IR_DTYPE_BF16:
+      lse_merge_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
+          static_cast<__nv_bfloat16*>(out), out_stride, o_parts, lse_parts, P, B, H, D);
+      break;
+    default:
+      lse_merge_kernel<__half><<<grid, threads, 0, s>>>(
+          static_cast<__half*>(out), out_stride, o_parts, lse_parts, P, B, H, D);
+      break;
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace irb

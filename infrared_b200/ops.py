@@ -1,0 +1,370 @@
+"""Tensor-level entry points over the C ABI (device memory and streams from PyTorch).
+
+Every function takes CUDA tensors, checks shapes/dtypes/contiguity on the
+host, and launches on ``torch.cuda.current_stream()`` without synchronising
+or allocating anything but its outputs (which the caller may pass in), so
+each one can run inside ``torch.cuda.graph`` capture. Device-side errors
+(bad block ids, slots, metadata) are accumulated in a per-device int32 flag
+word that :func:`check_device_errors` reads and clears.
+
+There is no CPU path: CPU tensors raise ``ValueError``.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import DEVERR_BITS, DecodeShape, check
+
+_DTYPES = {
+    torch.float32: _lib.IR_DTYPE_F32,
+    torch.bfloat16: _lib.IR_DTYPE_BF16,
+    torch.float16: _lib.IR_DTYPE_F16,
+}
+
+
+class DeviceError(RuntimeError):
+    """Errors a kernel recorded on the device (see ``IR_DEVERR_*``)."""
+
+    def __init__(self, bits: int):
+        names = [n for b, n in DEVERR_BITS.items() if bits & b]
+        super().__init__(f"infrared_b200 device error 0x{bits:x}: {', '.join(names)}")
+        self.bits = bits
+
+
+_state_lock = threading.Lock()
+_err_flags: dict[int, torch.Tensor] = {}
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return _DTYPES[dtype]
+    except KeyError:
+        raise _lib.UnsupportedShape(_lib.IR_ERR_UNSUPPORTED, f"dtype {dtype} not supported")
+
+
+def _dev_index(t: torch.Tensor) -> int:
+    if not t.is_cuda:
+        raise ValueError("infrared_b200 kernels take CUDA tensors (no CPU path)")
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def _index_of(device) -> int:
+    if device is None:
+        return torch.cuda.current_device()
+    if isinstance(device, int):
+        return device
+    d = torch.device(device)
+    return d.index if d.index is not None else torch.cuda.current_device()
+
+
+def error_flag(device: torch.device | int | None = None) -> torch.Tensor:
+    """The per-device int32 error word the kernels OR their error bits into."""
+    idx = _index_of(device)
+    with _state_lock:
+        t = _err_flags.get(idx)
+        if t is None:
+            t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            _err_flags[idx] = t
+    return t
+
+
+def check_device_errors(device=None, clear: bool = True) -> None:
+    """Synchronise on the flag word; raise :class:`DeviceError` if any bit is set."""
+    flag = error_flag(device)
+    bits = int(flag.item())
+    if bits and clear:
+        flag.zero_()
+    if bits:
+        raise DeviceError(bits)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device_index: int) -> int:
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
+def workspace(nbytes: int, device_index: int) -> torch.Tensor:
+    """A cached, growing per-device workspace buffer (256-byte aligned)."""
+    with _state_lock:
+        t = _workspaces.get(device_index)
+        if t is None or t.numel() < nbytes:
+            t = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8,
+                            device=torch.device("cuda", device_index))
+            _workspaces[device_index] = t
+    return t
+
+
+def set_decode_path(path: int) -> None:
+    """0 = automatic kernel choice, 1 = CUDA-core kernel, 2 = TMA kernel."""
+    check(_lib.load().ir_set_decode_path(path))
+
+
+# --- pool scatter / gather ----------------------------------------------------
+
+
+def _check_pool(pool: torch.Tensor, name: str) -> None:
+    if pool.dim() != 3 or not pool.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous [num_slots, Hkv, D] tensor")
+
+
+def cache_write(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
+                v_pool: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+    """``k_pool[slot_mapping] = k; v_pool[slot_mapping] = v`` (one layer's pools)."""
+    dev = _dev_index(k_pool)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    if k_pool.shape != v_pool.shape or k_pool.dtype != v_pool.dtype:
+        raise ValueError("k_pool and v_pool differ")
+    n = slot_mapping.numel()
+    hkv, d = k_pool.shape[1], k_pool.shape[2]
+    k = k.reshape(n, hkv, d)
+    v = v.reshape(n, hkv, d)
+    for t, nm in ((k, "k"), (v, "v")):
+        if t.dtype != k_pool.dtype or t.device != k_pool.device:
+            raise ValueError(f"{nm} must match the pool's dtype and device")
+        if n and (t.stride(2) != 1 or t.stride(1) != d):
+            raise ValueError(f"{nm} rows must be [Hkv, D] contiguous")
+    slots = slot_mapping.reshape(-1)
+    if slots.dtype != torch.int64 or not slots.is_contiguous() or slots.device != k_pool.device:
+        raise ValueError("slot_mapping must be a contiguous int64 tensor on the pool's device")
+    if n == 0:
+        return
+    lib = _lib.load()
+    check(lib.ir_cache_write(
+        k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0), k_pool.data_ptr(),
+        v_pool.data_ptr(), slots.data_ptr(), n, hkv, d, k_pool.shape[0],
+        dtype_code(k_pool.dtype), error_flag(dev).data_ptr(), _stream(dev)))
+
+
+def cache_gather(pool: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
+    """``pool[slots]`` for a 1-D or 2-D int64 slot tensor -> ``[*slots.shape, Hkv, D]``."""
+    dev = _dev_index(pool)
+    _check_pool(pool, "pool")
+    flat = slots.reshape(-1)
+    if flat.dtype != torch.int64 or flat.device != pool.device:
+        raise ValueError("slots must be int64 on the pool's device")
+    flat = flat.contiguous()
+    out = torch.empty((flat.numel(), pool.shape[1], pool.shape[2]), dtype=pool.dtype,
+                      device=pool.device)
+    if flat.numel():
+        check(_lib.load().ir_cache_gather(
+            out.data_ptr(), pool.data_ptr(), flat.data_ptr(), flat.numel(), pool.shape[1],
+            pool.shape[2], pool.shape[0], dtype_code(pool.dtype),
+            error_flag(dev).data_ptr(), _stream(dev)))
+    return out.reshape(*slots.shape, pool.shape[1], pool.shape[2])
+
+
+def derive_block_metadata(gather_slots: torch.Tensor, mask: torch.Tensor, block_size: int,
+                          block_tables: torch.Tensor | None = None,
+                          context_lens: torch.Tensor | None = None):
+    """``(gather_slots [B, T], decode mask [B, 1, 1, T]) -> (block_tables, context_lens)``.
+
+    ``block_tables`` is int32 ``[B, ceil(T / block_size)]``, ``context_lens``
+    int32 ``[B]``; both may be passed in (e.g. static graph buffers).
+    """
+    dev = _dev_index(gather_slots)
+    if gather_slots.dim() != 2 or gather_slots.dtype != torch.int64:
+        raise ValueError("gather_slots must be int64 [B, T]")
+    b, t = gather_slots.shape
+    if gather_slots.stride(1) != 1:
+        gather_slots = gather_slots.contiguous()
+    m2 = mask.reshape(b, t) if mask.numel() == b * t else None
+    if m2 is None:
+        raise ValueError("mask must have B*T elements ([B, 1, 1, T])")
+    if m2.stride(1) != 1:
+        m2 = m2.contiguous()
+    nb = -(-t // block_size)
+    if block_tables is None:
+        block_tables = torch.empty((b, max(nb, 1)), dtype=torch.int32, device=gather_slots.device)
+    if context_lens is None:
+        context_lens = torch.empty((b,), dtype=torch.int32, device=gather_slots.device)
+    if b:
+        check(_lib.load().ir_derive_block_metadata(
+            gather_slots.data_ptr(), gather_slots.stride(0), m2.data_ptr(), m2.stride(0),
+            dtype_code(m2.dtype), b, t, block_size, block_tables.data_ptr(),
+            block_tables.stride(0), context_lens.data_ptr(), error_flag(dev).data_ptr(),
+            _stream(dev)))
+    return block_tables, context_lens
+
+
+# --- decode -------------------------------------------------------------------
+
+
+def _shape(q: torch.Tensor, k_pool: torch.Tensor, block_tables: torch.Tensor,
+           block_size: int, scale: float, out_stride: int) -> DecodeShape:
+    b, h, d = q.shape
+    hkv = k_pool.shape[1]
+    s = DecodeShape()
+    s.batch = b
+    s.num_heads = h
+    s.num_kv_heads = hkv
+    s.head_dim = d
+    s.block_size = block_size
+    s.max_blocks = block_tables.shape[1]
+    s.bt_stride = block_tables.stride(0) if block_tables.shape[0] else block_tables.shape[1]
+    s.q_stride = q.stride(0)
+    s.out_stride = out_stride
+    s.num_slots = k_pool.shape[0]
+    s.scale = float(scale)
+    s.dtype = dtype_code(q.dtype)
+    return s
+
+
+def _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens):
+    _dev_index(q)
+    if q.dim() != 3:
+        raise ValueError("q must be [B, H, D]")
+    if q.stride(2) != 1 or q.stride(1) != q.shape[2]:
+        raise ValueError("q rows must be [H, D] contiguous")
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    if k_pool.shape != v_pool.shape:
+        raise ValueError("k_pool and v_pool shapes differ")
+    if k_pool.dtype != q.dtype or v_pool.dtype != q.dtype:
+        raise ValueError("q and the pools must share a dtype")
+    if k_pool.shape[2] != q.shape[2]:
+        raise ValueError("head_dim of q and pools differ")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or \
+            (block_tables.numel() and block_tables.stride(1) != 1):
+        raise ValueError("block_tables must be int32 [B, max_blocks] with unit column stride")
+    if context_lens.dtype != torch.int32 or not context_lens.is_contiguous():
+        raise ValueError("context_lens must be contiguous int32 [B]")
+    if block_tables.shape[0] != q.shape[0] or context_lens.numel() != q.shape[0]:
+        raise ValueError("batch sizes of q, block_tables and context_lens differ")
+    for t in (k_pool, v_pool, block_tables, context_lens):
+        if t.device != q.device:
+            raise ValueError("all tensors must be on the same device")
+
+
+def decode_plan(q, k_pool, block_tables, block_size, scale=1.0):
+    """``(path, ctas_per_kv_head, workspace_bytes)`` the library picks for this call."""
+    s = _shape(q, k_pool, block_tables, block_size, scale, q.shape[1] * q.shape[2])
+    lib = _lib.load()
+    path, g = _lib.c_int(), _lib.c_int()
+    check(lib.ir_paged_decode_plan(s, path, g))
+    return path.value, g.value, lib.ir_paged_decode_workspace_size(s)
+
+
+def _ws(s: DecodeShape, dev: int, ws: torch.Tensor | None):
+    nbytes = _lib.load().ir_paged_decode_workspace_size(s)
+    if nbytes == 0:
+        check(_lib.load().ir_paged_decode_plan(s, None, None))
+    if ws is None:
+        ws = workspace(nbytes, dev)
+    return ws, nbytes
+
+
+def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                 block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
+                 block_size: int, out: torch.Tensor | None = None,
+                 ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode attention: ``q [B, H, D]`` over paged K/V -> ``[B, H, D]`` (q's dtype).
+
+    ``k_pool``/``v_pool`` are one layer's ``[num_slots, Hkv, D]`` pools,
+    ``block_tables`` int32 ``[B, max_blocks]`` of block ids, ``context_lens``
+    int32 ``[B]``. GQA: query head h reads kv head ``h // (H // Hkv)``.
+    """
+    _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+    dev = _dev_index(q)
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
+            out.stride(1) != q.shape[2]:
+        raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
+    s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
+    ws, nbytes = _ws(s, dev, ws)
+    check(_lib.load().ir_paged_decode(
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
+        error_flag(dev).data_ptr(), _stream(dev)))
+    return out
+
+
+def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                       k_pool: torch.Tensor, v_pool: torch.Tensor,
+                       slot_mapping: torch.Tensor, block_tables: torch.Tensor,
+                       context_lens: torch.Tensor, scale: float, block_size: int,
+                       out: torch.Tensor | None = None,
+                       ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Cache write of ``k_new/v_new [B, Hkv, D]`` at ``slot_mapping`` fused with decode.
+
+    ``slot_mapping[b]`` must be the slot of position ``context_lens[b] - 1``
+    (the new token), as in the engine's decode step; otherwise the device
+    error ``WRITE_SLOT`` is raised by :func:`check_device_errors`.
+    """
+    _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+    dev = _dev_index(q)
+    b, hkv, d = q.shape[0], k_pool.shape[1], k_pool.shape[2]
+    k_new = k_new.reshape(b, hkv, d)
+    v_new = v_new.reshape(b, hkv, d)
+    if k_new.stride(0) != v_new.stride(0) or k_new.stride(2) != 1 or k_new.stride(1) != d \
+            or v_new.stride(2) != 1 or v_new.stride(1) != d:
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
+        raise ValueError("k_new/v_new must match q's dtype")
+    slots = slot_mapping.reshape(-1)
+    if slots.dtype != torch.int64 or not slots.is_contiguous() or slots.numel() != b:
+        raise ValueError("slot_mapping must be contiguous int64 [B]")
+    if out is None:
+        out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
+    ws, nbytes = _ws(s, dev, ws)
+    check(_lib.load().ir_paged_decode_write(
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
+        slots.data_ptr(), block_tables.data_ptr(), context_lens.data_ptr(), s,
+        ws.data_ptr(), ws.numel(), error_flag(dev).data_ptr(), _stream(dev)))
+    return out
+
+
+def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                     block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
+                     block_size: int, o: torch.Tensor | None = None,
+                     lse: torch.Tensor | None = None, ws: torch.Tensor | None = None):
+    """Partial decode: ``(o [B, H, D] fp32 normalised, lse [B, H] fp32 natural log)``."""
+    _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+    dev = _dev_index(q)
+    b, h, d = q.shape
+    if o is None:
+        o = torch.empty((b, h, d), dtype=torch.float32, device=q.device)
+    if lse is None:
+        lse = torch.empty((b, h), dtype=torch.float32, device=q.device)
+    if not (o.is_contiguous() and lse.is_contiguous() and o.dtype == torch.float32
+            and lse.dtype == torch.float32):
+        raise ValueError("o and lse must be contiguous fp32")
+    s = _shape(q, k_pool, block_tables, block_size, scale, h * d)
+    ws, nbytes = _ws(s, dev, ws)
+    check(_lib.load().ir_paged_decode_lse(
+        o.data_ptr(), lse.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
+        error_flag(dev).data_ptr(), _stream(dev)))
+    return o, lse
+
+
+def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor,
+              dtype: torch.dtype = torch.float32,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Combine ``o_parts [P, B, H, D]`` / ``lse_parts [P, B, H]`` (fp32) -> ``[B, H, D]``."""
+    dev = _dev_index(o_parts)
+    if o_parts.dim() != 4 or lse_parts.shape != o_parts.shape[:3]:
+        raise ValueError("o_parts must be [P, B, H, D] and lse_parts [P, B, H]")
+    if o_parts.dtype != torch.float32 or lse_parts.dtype != torch.float32:
+        raise ValueError("partials must be fp32")
+    o_parts, lse_parts = o_parts.contiguous(), lse_parts.contiguous()
+    p, b, h, d = o_parts.shape
+    if out is None:
+        out = torch.empty((b, h, d), dtype=dtype, device=o_parts.device)
+    if out.stride(2) != 1 or out.stride(1) != d:
+        raise ValueError("out rows must be [H, D] contiguous")
+    check(_lib.load().ir_lse_merge(
+        out.data_ptr(), out.stride(0), o_parts.data_ptr(), lse_parts.data_ptr(), p, b, h, d,
+        dtype_code(out.dtype), _stream(dev)))
+    return out

@@ -1,0 +1,96 @@
+"""Generate the golden fixtures by running the REFERENCE engine's own code.
+
+Run in a checkout where the infrared reference is importable (default
+location ``/root/reference``; override with ``INFRARED_REF``):
+
+    python tests/golden/make_golden.py
+
+For every case in ``cases.py`` it rebuilds the seeded inputs, calls
+infrared's naive path ``paged_attention(..., PagedContext(use_triton=False))``
+(infrared/model/triton_attention.py:81-129) in fp32 on the CPU, its
+``build_decode_static_inputs`` (infrared/engine/cuda_graph.py:105-155) and
+``paged_attention_blockwise_reference`` (:135-177), and stores outputs plus
+input digests in ``tests/golden/golden.npz``. The tests and the GPU runs only
+read that file; they never import the reference.
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(HERE))
+REF = os.environ.get("INFRARED_REF", "/root/reference")
+sys.path.insert(0, REF)
+
+import torch  # noqa: E402
+
+import cases  # noqa: E402
+from infrared.cache.paged_kv_cache import PagedContext, PagedKVPool  # noqa: E402
+from infrared.engine.cuda_graph import build_decode_static_inputs  # noqa: E402
+from infrared.model.layers import repeat_kv  # noqa: E402
+from infrared.model.triton_attention import (  # noqa: E402
+    paged_attention, paged_attention_blockwise_reference)
+
+
+def run_attention_case(name: str, out: dict) -> None:
+    w, q, kp, vp, kn, vn = cases.attention_inputs(name)
+    s = cases.seam_tensors(w, q, kp, vp, kn, vn)
+    pool = PagedKVPool(1, w.num_blocks, w.block_size, w.num_kv_heads, w.head_dim,
+                       torch.float32)
+    pool.k.copy_(torch.from_numpy(s["pool_k"]))
+    pool.v.copy_(torch.from_numpy(s["pool_v"]))
+    ctx = PagedContext(pool, torch.from_numpy(s["write_slots"]),
+                       torch.from_numpy(s["gather_slots"]), use_triton=False)
+    res = paged_attention(torch.from_numpy(s["q"]), torch.from_numpy(s["k"]),
+                          torch.from_numpy(s["v"]), ctx, torch.from_numpy(s["mask"]), 0,
+                          w.scale, w.n_rep)
+    out[f"{name}/out"] = res.numpy()[:, 0]          # [B, H, D]
+    out[f"{name}/input_digest"] = np.array(cases.input_digest(name))
+    out[f"{name}/pool_digest"] = np.array(cases.digest(pool.k.numpy(), pool.v.numpy()))
+
+
+def run_graph_case(name: str, out: dict) -> None:
+    tables, num_cached, last, bucket, t_max, bs = cases.graph_case_args(name)
+    inp = build_decode_static_inputs(tables, num_cached, last, bucket, t_max, bs, "cpu",
+                                     torch.float32)
+    for key in ("ids", "positions", "write_slots", "gather_slots", "mask"):
+        out[f"{name}/{key}"] = getattr(inp, key).numpy()
+
+
+def run_blockwise(out: dict) -> None:
+    w, q, kp, vp, kn, vn = cases.attention_inputs("g7_d64_bs16_shared")
+    s = cases.seam_tensors(w, q, kp, vp, kn, vn)
+    # history incl. the written new token, gathered like the naive path
+    kpool, vpool = s["pool_k"][0].copy(), s["pool_v"][0].copy()
+    kpool[s["write_slots"]] = kn
+    vpool[s["write_slots"]] = vn
+    k_all = repeat_kv(torch.from_numpy(kpool[s["gather_slots"]]), w.n_rep)
+    v_all = repeat_kv(torch.from_numpy(vpool[s["gather_slots"]]), w.n_rep)
+    for bn in cases.BLOCKWISE_BLOCKS:
+        res = paged_attention_blockwise_reference(torch.from_numpy(s["q"]), k_all, v_all,
+                                                  torch.from_numpy(s["mask"]), w.scale, bn)
+        out[f"blockwise/{bn}"] = res.numpy()[:, 0]
+
+
+def main() -> None:
+    torch.manual_seed(0)
+    out: dict = {}
+    for name in cases.ATTENTION_CASES:
+        run_attention_case(name, out)
+    for name in cases.GRAPH_CASES:
+        run_graph_case(name, out)
+    run_blockwise(out)
+    dst = HERE / "golden.npz"
+    np.savez_compressed(dst, **out)
+    print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(out)} arrays)")
+
+
+if __name__ == "__main__":
+    main()
