@@ -58,6 +58,9 @@ def parse_args():
     p.add_argument("--sets", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--soak", type=float, default=1.5,
+                   help="seconds of untimed replays before timing (clock sampling)")
+    p.add_argument("--no-e2e", action="store_true")
     return p.parse_args()
 
 
@@ -247,7 +250,7 @@ def run_ours(args):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         clocks = ClockSampler(local)
         t_soak = time.perf_counter()
-        while time.perf_counter() - t_soak < 1.5:   # clocks settle under load
+        while time.perf_counter() - t_soak < args.soak:   # clocks settle under load
             graph.replay()
             torch.cuda.synchronize(dev)
         if world > 1:
