@@ -61,6 +61,9 @@ def parse_args():
     p.add_argument("--soak", type=float, default=1.5,
                    help="seconds of untimed replays before timing (clock sampling)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--decode-path", type=int, default=0,
+                   help="kernel override (ir_set_decode_path): 0 auto, 1 CUDA-core, "
+                        "2 TMA, 3 TMA with one copy per head and half")
     return p.parse_args()
 
 
@@ -215,6 +218,7 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
+    ops.set_decode_path(args.decode_path)
     w = make_workload(args.config, rank)
     fused = args.config == "c3"
     bt = torch.from_numpy(w.block_tables).to(dev)
@@ -234,41 +238,8 @@ def run_ours(args):
         else:
             irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size, out=out, ws=ws)
 
-    stream = torch.cuda.Stream(dev)
-    stream.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(stream):
-        for i in range(max(args.warmup, 3)):
-            step(i)
-        torch.cuda.synchronize(dev)
-        ops.check_device_errors(dev)
-        # K steps in one graph: the timed region is a single replay
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(args.steps):
-                step(i)
-        # per-call duration of the decode path (eager, events on the stream)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-        clocks = ClockSampler(local)
-        t_soak = time.perf_counter()
-        while time.perf_counter() - t_soak < args.soak:   # clocks settle under load
-            graph.replay()
-            torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-        ev[0].record(stream)
-        graph.replay()
-        ev[1].record(stream)
-        ev[1].synchronize()
-        clk = clocks.stop()
-        ms = ev[0].elapsed_time(ev[1])
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        ops.check_device_errors(dev)
-
-        # e2e: public API with pinned host buffers, copies inside the timed region
+    def measure_e2e():
+        """Public API with pinned host buffers; copies inside the timed region."""
         q_host = sets[0][0].cpu().pin_memory()
         bt_host = bt.cpu().pin_memory()
         ctx_host = ctx.cpu().pin_memory()
@@ -317,6 +288,45 @@ def run_ours(args):
         if fused:
             h2d += 2 * kn_host.numel() * kn_host.element_size() + sm_host.numel() * 8
         d2h = out_host.numel() * out_host.element_size()
+        return e2e_ms, h2d, d2h
+
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize(dev)
+        ops.check_device_errors(dev)
+        # K steps in one graph: the timed region is a single replay
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(args.steps):
+                step(i)
+        # per-call duration of the decode path (eager, events on the stream)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        clocks = ClockSampler(local)
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < args.soak:   # clocks settle under load
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev[0].record(stream)
+        graph.replay()
+        ev[1].record(stream)
+        ev[1].synchronize()
+        clk = clocks.stop()
+        ms = ev[0].elapsed_time(ev[1])
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        ops.check_device_errors(dev)
+
+        e2e_ms = h2d = d2h = None
+        if not args.no_e2e:
+            e2e_ms, h2d, d2h = measure_e2e()
 
     path, ctas, _ = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale)
     peak, peak_kind = measured_peaks()
@@ -350,7 +360,8 @@ def run_ours(args):
             "parallelism": f"sequence-sharded x{world}, no collective",
             "l2": "inputs larger than L2: >=200 MB of K/V per step, 3 rotating pool sets",
             "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
-            "kernel_path": {1: "cuda-core", 2: "tma+mma.sync"}[path],
+            "kernel_path": {1: "cuda-core", 2: "tma+mma.sync"}[path] +
+                           (" (copy per head)" if args.decode_path == 3 else ""),
             "ctas_per_kv_head": ctas,
         },
         "decode_tok_s_per_layer": round(world * w.batch / (per_step_ms / 1e3), 1),
@@ -365,7 +376,7 @@ def run_ours(args):
             "traffic": traffic_from_profiles(args.config),
             "scope": "one decode call (decode kernel + merge kernel), per GPU",
         },
-        "e2e": {
+        "e2e": None if e2e_ms is None else {
             "value": round(world * nbytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
             "unit": "GB/s",
             "h2d_bytes_per_step": h2d,

@@ -129,9 +129,10 @@ typedef struct ir_decode_shape {
 } ir_decode_shape;
 
 /* Bytes of workspace the decode calls need for this shape on the current
- * device (0 on an invalid shape; the workspace must be 256-byte aligned).
- * It holds the tile prefix and the partials of sequences split across CTAs;
- * it needs no initialisation and is dead after the call's merge kernel. */
+ * device (0 on an invalid shape). The workspace holds the tile prefix and the
+ * partial results of sequences split across CTAs; it must be 256-byte
+ * aligned and needs no initialisation. Calls sharing a workspace must not
+ * overlap on the GPU (calls on one stream never do). */
 size_t ir_paged_decode_workspace_size(const ir_decode_shape* shape);
 
 /* Kernel choice for this shape on the current device: *path = 1 (CUDA-core
@@ -145,7 +146,8 @@ int ir_paged_decode_plan(const ir_decode_shape* shape, int* path,
 
 /* Process-wide kernel override for testing and tuning: 0 = automatic,
  * 1 = always the CUDA-core kernel, 2 = the TMA kernel (calls whose shape is
- * not eligible then fail with IR_ERR_UNSUPPORTED). */
+ * not eligible then fail with IR_ERR_UNSUPPORTED), 3 = the TMA kernel with
+ * one tensor copy per (kv head, 64-column half) instead of one per tile. */
 int ir_set_decode_path(int path);
 
 /*
@@ -156,8 +158,10 @@ int ir_set_decode_path(int path);
  * triton_attention.py:81-107): _paged_attention_naive (:110-129) and
  * _paged_attention_triton (:310-359). A sequence with context_len 0 gets a
  * zero row (the l_safe convention of the reference kernel, :293-297).
- * Work is split across the GPU's SMs in equal token shares; sequences that
- * span several CTAs are combined with a log-sum-exp merge in `workspace`.
+ * Work is split across the GPU's SMs in equal token shares; the pieces of a
+ * sequence that spans several CTAs are combined (log-sum-exp) by a merge
+ * kernel launched behind the decode kernel with programmatic dependent
+ * launch (two launches per call, one stream).
  */
 int ir_paged_decode(void* out, const void* q, const void* k_pool,
                     const void* v_pool, const int32_t* block_tables,

@@ -46,6 +46,7 @@ bool aligned(const void* p, size_t n) {
 std::mutex g_mu;
 std::map<std::pair<int, int>, int> g_cache;  // (device, key) -> value
 int g_forced_path = 0;
+int g_one_box = 1;
 
 int cached(int key, int (*compute)(int), int arg, int* out) {
   int dev = 0;
@@ -70,13 +71,36 @@ int sm_count_now(int) {
   return n > 0 ? n : 1;
 }
 
-// key encoding for the occupancy cache: path(2 bits) dtype(2) D==128(1) bs8(1)
+// key encoding for the occupancy cache:
+// path(2 bits) dtype(2) D==128(1) bs8(1) log2(head group)(2)
+int occ_key(int path, const ir_decode_shape* s) {
+  const int hg = path == 2 ? irb::tma_head_group(s->num_kv_heads) : 1;
+  const int lg = hg == 8 ? 3 : hg == 4 ? 2 : hg == 2 ? 1 : 0;
+  return path | (s->dtype << 2) | ((s->head_dim == 128) << 4) |
+         ((s->block_size == 8) << 5) | (lg << 6);
+}
+
 int occ_compute(int key) {
   const int path = key & 3, dtype = (key >> 2) & 3, d128 = (key >> 4) & 1,
-            bs8 = (key >> 5) & 1;
+            bs8 = (key >> 5) & 1, hg = 1 << ((key >> 6) & 3);
   const int D = d128 ? 128 : 64;
-  if (path == 2) return irb::decode_tma_occupancy(dtype, D, bs8 ? 8 : 16);
+  if (path == 2) return irb::decode_tma_occupancy(dtype, D, hg, bs8 ? 8 : 16);
   return irb::decode_generic_occupancy(dtype, D);
+}
+
+// CTAs per kv head (generic) or per head group (TMA) for this path.
+int ctas_per_group(int path, const ir_decode_shape* s, int* out) {
+  int sms = 1, occ = 1;
+  int e = cached(-1, sm_count_now, 0, &sms);
+  if (e) return e;
+  const int key = occ_key(path, s);
+  e = cached(key, occ_compute, key, &occ);
+  if (e) return e;
+  const int groups = path == 2 ? s->num_kv_heads / irb::tma_head_group(s->num_kv_heads)
+                               : s->num_kv_heads;
+  int G = (sms * occ) / groups;
+  *out = G < 1 ? 1 : (G > 65535 ? 65535 : G);
+  return 0;
 }
 
 // ------------------------------------------------------------ TMA encode
@@ -96,8 +120,36 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return g_encode;
 }
 
-// [num_slots, Hkv, D] pool as a 3-D map with [box_rows x 1 x 64] boxes and
-// the 128-byte swizzle.
+// [num_slots, Hkv, D] pool viewed as (element, slot, 64-column half, head)
+// — dimensions ordered so that a box of (64, rows, D/64, head_group) lands
+// in shared memory as one [rows x 128 B] region per (head, half) — with the
+// 128-byte swizzle. One copy moves a tile's rows for a whole head group.
+bool make_pool_map4d(CUtensorMap* map, const void* pool, int64_t num_slots,
+                     int hkv, int d, int dtype, int box_rows, int head_group) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(num_slots),
+                              static_cast<cuuint64_t>(d / 64),
+                              static_cast<cuuint64_t>(hkv)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(hkv) * d * 2, 128,
+                                 static_cast<cuuint64_t>(d) * 2};
+  const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows),
+                             static_cast<cuuint32_t>(d / 64),
+                             static_cast<cuuint32_t>(head_group)};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == IR_DTYPE_BF16
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 4, const_cast<void*>(pool), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// The same pool as a 3-D (D, Hkv, slots) map with [rows x 1 x 64] boxes:
+// one copy per (head, half) of a tile.
 bool make_pool_map(CUtensorMap* map, const void* pool, int64_t num_slots,
                    int hkv, int d, int dtype, int box_rows) {
   auto enc = encode_fn();
@@ -173,16 +225,9 @@ int make_plan(const ir_decode_shape* s, Plan* p) {
     if (path != 2)
       return fail(IR_ERR_UNSUPPORTED, "TMA path forced but shape not eligible");
   }
-  int sms = 1, occ = 1;
-  int e = cached(-1, sm_count_now, 0, &sms);
+  int G = 1;
+  int e = ctas_per_group(path, s, &G);
   if (e) return cuda_status(e, "cudaGetDevice");
-  const int key = path | (s->dtype << 2) | ((s->head_dim == 128) << 4) |
-                  ((s->block_size == 8) << 5);
-  e = cached(key, occ_compute, key, &occ);
-  if (e) return cuda_status(e, "cudaGetDevice");
-  int G = (sms * occ) / s->num_kv_heads;
-  if (G < 1) G = 1;
-  if (G > 65535) G = 65535;
   p->path = path;
   p->G = G;
   const int64_t B = s->batch, H = s->num_heads, D = s->head_dim;
@@ -233,14 +278,11 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
       if (g_forced_path == 2)
         return fail(IR_ERR_UNSUPPORTED, "TMA path forced but pointers misaligned");
       plan.path = 1;
-      // the generic path may have a different CTA count: re-plan for sizing
-      int sms = 1, occ = 1;
-      cached(-1, sm_count_now, 0, &sms);
-      const int key = 1 | (s->dtype << 2) | ((s->head_dim == 128) << 4) |
-                      ((s->block_size == 8) << 5);
-      cached(key, occ_compute, key, &occ);
-      int G = (sms * occ) / s->num_kv_heads;
-      plan.G = G < 1 ? 1 : (G > plan.G ? plan.G : G);  // never exceed sized G
+      // the generic path may want a different CTA count; never exceed the
+      // count the workspace was sized for
+      int G = 1;
+      ctas_per_group(1, s, &G);
+      plan.G = G > plan.G ? plan.G : G;
     }
   }
   irb::DecodeArgs a{};
@@ -281,19 +323,27 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
   if (plan.path == 2) {
     CUtensorMap tmk, tmv;
     const int rows = s->block_size == 8 ? 8 : 16;
-    if (!make_pool_map(&tmk, k_pool, s->num_slots, s->num_kv_heads,
-                       s->head_dim, s->dtype, rows) ||
-        !make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads,
-                       s->head_dim, s->dtype, rows))
+    const int hg = irb::tma_head_group(s->num_kv_heads);
+    int one_box = g_one_box;
+    if (one_box &&
+        !(make_pool_map4d(&tmk, k_pool, s->num_slots, s->num_kv_heads, s->head_dim,
+                          s->dtype, rows, hg) &&
+          make_pool_map4d(&tmv, v_pool, s->num_slots, s->num_kv_heads, s->head_dim,
+                          s->dtype, rows, hg)))
+      one_box = 0;  // the driver refused the permuted view: one copy per (head, half)
+    if (!one_box &&
+        !(make_pool_map(&tmk, k_pool, s->num_slots, s->num_kv_heads, s->head_dim,
+                        s->dtype, rows) &&
+          make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads, s->head_dim,
+                        s->dtype, rows)))
       return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-    e = irb::launch_decode_tma(tmk, tmv, a, s->dtype, stream);
+    e = irb::launch_decode_tma(tmk, tmv, a, s->dtype, one_box, stream);
   } else {
     e = irb::launch_decode_generic(a, s->dtype, stream);
   }
   if (e) return cuda_status(e, "decode kernel launch");
   e = irb::launch_split_merge(a, s->dtype, stream);
-  if (e) return cuda_status(e, "merge kernel launch");
-  return IR_OK;
+  return cuda_status(e, "merge kernel launch");
 }
 
 }  // namespace
@@ -313,9 +363,10 @@ const char* ir_deverr_name(int bit) {
 }
 
 int ir_set_decode_path(int path) {
-  if (path < 0 || path > 2) return fail(IR_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+  if (path < 0 || path > 3) return fail(IR_ERR_INVALID_ARG, "path must be 0, 1, 2 or 3");
   std::lock_guard<std::mutex> lk(g_mu);
-  g_forced_path = path;
+  g_forced_path = path == 3 ? 2 : path;
+  g_one_box = path == 3 ? 0 : 1;
   return IR_OK;
 }
 

@@ -9,8 +9,10 @@
 // each (CTA, sequence) piece is a "segment". A segment that is a whole
 // sequence writes the final row; any other segment writes a normalised fp32
 // partial and its log2-sum-exp into workspace slot g + b (unique: along the
-// monotone path of (g, b) pieces g + b strictly increases), and the merge
-// kernel combines the pieces of every sequence that spans several CTAs.
+// monotone path of (g, b) pieces g + b strictly increases). The merge kernel,
+// launched right behind the decode kernel (programmatic dependent launch),
+// combines the pieces of every sequence that spans several CTAs in share
+// order, so results do not depend on scheduling.
 #pragma once
 
 #include "common.cuh"
@@ -35,7 +37,7 @@ struct DecodeArgs {
   float scale_log2;  // scale * log2(e)
   int G;             // CTAs per kv head
   // workspace
-  int64_t* ws_prefix;  // [B + 1] tile prefix (written by CTA (0, 0))
+  int64_t* ws_prefix;  // [B + 1] tile prefix (written by the first CTA of kv head 0)
   float* ws_lse;       // [Hkv, G + B, n_rep] log2-sum-exp of partials
   float* ws_o;         // [Hkv, G + B, n_rep, D] normalised partials
   // pools (generic kernel reads them directly; fused write stores into them)
@@ -68,12 +70,18 @@ __device__ __forceinline__ int share_of(int64_t t, int64_t total, int G) {
   return static_cast<int>(((t + 1) * G + total - 1) / total - 1);
 }
 
+// Shares actually used: never more CTAs than tiles, so no share is empty.
+__device__ __forceinline__ int shares_used(int64_t total, int G) {
+  return total < G ? static_cast<int>(total) : G;
+}
+
 struct RangeInfo {
   int64_t total;    // T
   int64_t start;    // first tile of this CTA
   int64_t end;      // one past the last tile
   int64_t p_first;  // prefix of b_first
   int b_first;      // sequence holding tile `start`
+  int G;            // shares used (<= DecodeArgs::G)
 };
 
 // Block-wide exclusive scan of one int64 per thread (NT threads, NT % 32 == 0).
@@ -101,12 +109,13 @@ __device__ __forceinline__ int64_t block_excl_scan(int64_t v, int64_t* sm,
   return before + x - v;
 }
 
-// Find this CTA's share. All NT threads must call it. CTA (0, 0) also
-// publishes the tile prefix to the workspace and writes the rows of
-// sequences with no context (no CTA streams them).
+// Find this CTA's share. All NT threads must call it. The CTA streams kv
+// heads [kv0, kv0 + nkv). The first CTA of kv head 0 publishes the tile
+// prefix to the workspace for the merge kernel; CTAs with g == 0 write the
+// rows of sequences with no context (no CTA streams them).
 template <int NT, typename T>
-__device__ void find_share(const DecodeArgs& a, int g, int kvh, RangeInfo* ri,
-                           int64_t* sm_scan) {
+__device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
+                           RangeInfo* ri, int64_t* sm_scan) {
   const int tid = threadIdx.x;
   // pass 1: total tiles (and context validation)
   int64_t mine = 0;
@@ -117,18 +126,20 @@ __device__ void find_share(const DecodeArgs& a, int g, int kvh, RangeInfo* ri,
   }
   int64_t total = 0;
   block_excl_scan<NT>(mine, sm_scan, &total);
-  const int64_t start = share_start(g, total, a.G);
-  const int64_t end = share_start(g + 1, total, a.G);
+  const int G = shares_used(total, a.G);
+  const int64_t start = g < G ? share_start(g, total, G) : total;
+  const int64_t end = g < G ? share_start(g + 1, total, G) : total;
   if (tid == 0) {
     ri->total = total;
     ri->start = start;
     ri->end = end;
     ri->b_first = -1;
     ri->p_first = 0;
+    ri->G = G;
   }
   __syncthreads();
   // pass 2: prefix of every sequence; locate `start`
-  const bool publish = (g == 0 && kvh == 0 && a.ws_prefix != nullptr);
+  const bool publish = (g == 0 && kv0 == 0);
   int64_t running = 0;
   for (int base = 0; base < a.B; base += NT) {
     const int b = base + tid;
@@ -142,9 +153,9 @@ __device__ void find_share(const DecodeArgs& a, int g, int kvh, RangeInfo* ri,
         ri->p_first = p;
       }
       if (n == 0 && g == 0) {
-        // empty context: zero row (and lse = -inf) for this kv head's group
-        for (int i = 0; i < a.n_rep * a.D; ++i) {
-          const int h = kvh * a.n_rep + i / a.D, d = i % a.D;
+        // empty context: zero rows (and lse = -inf) of this CTA's heads
+        for (int i = 0; i < nkv * a.n_rep * a.D; ++i) {
+          const int h = kv0 * a.n_rep + i / a.D, d = i % a.D;
           if (a.lse_mode) {
             a.lse_o[(static_cast<int64_t>(b) * a.H + h) * a.D + d] = 0.f;
             if (d == 0) a.lse_out[static_cast<int64_t>(b) * a.H + h] = -INFINITY;
@@ -182,6 +193,25 @@ __device__ __forceinline__ void write_segment_value(const DecodeArgs& a,
     a.ws_o[(slot * a.n_rep + n) * a.D + d] = val;
     if (d == 0) a.ws_lse[slot * a.n_rep + n] = lse2;
   }
+}
+
+// Shares [glo, glo + parts) hold the pieces of a sequence with tile prefix
+// pb and nb tiles.
+__device__ __forceinline__ void piece_range(int64_t pb, int64_t nb, int64_t total, int G,
+                                            int* glo, int* parts) {
+  const int lo = share_of(pb, total, G);
+  *glo = lo;
+  *parts = share_of(pb + nb - 1, total, G) - lo + 1;
+}
+
+// Programmatic dependent launch: let the dependent (merge) grid start
+// launching now / wait until the prerequisite (decode) grid has finished and
+// its memory is visible. Both are no-ops without a dependent launch.
+__device__ __forceinline__ void launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 }  // namespace irb

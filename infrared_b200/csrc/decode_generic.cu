@@ -1,9 +1,9 @@
 // Paged decode attention on CUDA cores for every dtype/shape the TMA kernel
 // does not take (fp32 pools, GQA groups of 9-16, block sizes other than 8 or a
-// multiple of 16), plus the two log-sum-exp merge kernels.
+// multiple of 16), plus the log-sum-exp merge of partials from several GPUs.
 //
 // The generic kernel uses the same balanced tile shares and segment outputs
-// as the TMA kernel (decode_common.cuh) so the split merge serves both. A CTA
+// as the TMA kernel (decode_common.cuh), so one split merge serves both. A CTA
 // of 128 threads walks its tiles in order: it stages the 16 K and V rows of a
 // tile in shared memory (gathered row by row through the block table),
 // computes the 16 x group scores with fp32 dot products, updates the
@@ -34,7 +34,8 @@ __global__ void __launch_bounds__(kGenThreads)
 
   const int kvh = blockIdx.x, g = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  find_share<kGenThreads, T>(a, g, kvh, &ri, sm_scan);
+  find_share<kGenThreads, T>(a, g, kvh, 1, &ri, sm_scan);
+  launch_dependents();
   const int64_t start = ri.start, end = ri.end;
   if (start >= end) return;
 
@@ -168,38 +169,49 @@ __global__ void __launch_bounds__(kGenThreads)
   }
 }
 
+// Combine the pieces of the split sequences: CTA (kv head x query head in
+// group, sequence), one thread per head-dim column. Every piece's loads are
+// independent, so the merge of a sequence costs about one L2 round trip.
 template <typename T>
-__global__ void split_merge_kernel(const DecodeArgs a) {
-  const int b = blockIdx.x, kvh = blockIdx.y;
+__global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
+  wait_prerequisites();  // the decode grid's pieces and prefix are complete
+  __shared__ float red[2][4];
+  const int kvh = blockIdx.x / a.n_rep, n = blockIdx.x % a.n_rep, b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t pb = a.ws_prefix[b];
   const int64_t nb = a.ws_prefix[b + 1] - pb;
   const int64_t total = a.ws_prefix[a.B];
-  if (nb <= 0) return;
-  const int glo = share_of(pb, total, a.G);
-  const int ghi = share_of(pb + nb - 1, total, a.G);
-  if (glo == ghi) return;  // written whole by one CTA
-  const int64_t base = static_cast<int64_t>(kvh) * (a.G + a.B) + b;
-  for (int idx = threadIdx.x; idx < a.n_rep * a.D; idx += blockDim.x) {
-    const int n = idx / a.D, d = idx % a.D;
-    float M = -INFINITY;
-    for (int g = glo; g <= ghi; ++g) {
-      if (share_start(g, total, a.G) == share_start(g + 1, total, a.G)) continue;
-      M = fmaxf(M, a.ws_lse[(base + g) * a.n_rep + n]);
-    }
-    float val = 0.f, lse2 = -INFINITY;
-    if (M != -INFINITY) {
-      float lsum = 0.f, osum = 0.f;
-      for (int g = glo; g <= ghi; ++g) {
-        if (share_start(g, total, a.G) == share_start(g + 1, total, a.G)) continue;
-        const int64_t sl = base + g;
-        const float w = ex2(a.ws_lse[sl * a.n_rep + n] - M);
-        lsum += w;
-        osum += w * a.ws_o[(sl * a.n_rep + n) * a.D + d];
-      }
-      val = osum / lsum;
-      lse2 = M + log2f(lsum);
-    }
-    write_segment_value<T>(a, kvh, 0, b, true, n, d, val, lse2);
+  if (nb <= 0) return;  // empty context: written by the decode kernel
+  const int G = shares_used(total, a.G);
+  const int glo = share_of(pb, total, G);
+  const int parts = share_of(pb + nb - 1, total, G) - glo + 1;
+  if (parts == 1) return;  // written whole by one CTA
+  const int64_t base = static_cast<int64_t>(kvh) * (a.G + a.B) + glo + b;
+  const float* lse = a.ws_lse + base * a.n_rep + n;  // stride n_rep per part
+  float mx = -INFINITY;
+  for (int i = tid; i < parts; i += blockDim.x) mx = fmaxf(mx, lse[i * a.n_rep]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[0][warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+  float sum = 0.f;
+  if (mx != -INFINITY)
+    for (int i = tid; i < parts; i += blockDim.x) sum += ex2(lse[i * a.n_rep] - mx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (lane == 0) red[1][warp] = sum;
+  __syncthreads();
+  sum = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+  const float inv = sum > 0.f ? 1.f / sum : 0.f;
+  const float lse2 = sum > 0.f ? mx + log2f(sum) : -INFINITY;
+  const float* o = a.ws_o + (base * a.n_rep + n) * a.D;  // stride n_rep * D per part
+  const int64_t ostride = static_cast<int64_t>(a.n_rep) * a.D;
+  for (int d = tid; d < a.D; d += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < parts; ++i) acc += ex2(lse[i * a.n_rep] - mx) * o[i * ostride + d];
+    write_segment_value<T>(a, kvh, 0, b, true, n, d, mx == -INFINITY ? 0.f : acc * inv, lse2);
   }
 }
 
@@ -268,13 +280,22 @@ int decode_generic_occupancy(int dtype, int D) {
 }
 
 int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
-  dim3 grid(a.B, a.Hkv);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.Hkv * a.n_rep, a.B);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   switch (dtype) {
-    case IR_DTYPE_F32: split_merge_kernel<float><<<grid, 128, 0, s>>>(a); break;
-    case IR_DTYPE_BF16: split_merge_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(a); break;
-    default: split_merge_kernel<__half><<<grid, 128, 0, s>>>(a); break;
+    case IR_DTYPE_F32: e = cudaLaunchKernelEx(&cfg, split_merge_kernel<float>, a); break;
+    case IR_DTYPE_BF16: e = cudaLaunchKernelEx(&cfg, split_merge_kernel<__nv_bfloat16>, a); break;
+    default: e = cudaLaunchKernelEx(&cfg, split_merge_kernel<__half>, a); break;
   }
-  return static_cast<int>(cudaGetLastError());
+  return static_cast<int>(e);
 }
 
 int launch_lse_merge(void* out, int64_t out_stride, const float* o_parts,

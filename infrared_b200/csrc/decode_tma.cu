@@ -1,24 +1,30 @@
 // Paged decode attention for 16-bit pools: TMA-fed, warp-specialised.
 //
-// One CTA streams one share of the 16-token tiles of one kv head (see
-// decode_common.cuh). Warp 0 is the producer: its lanes resolve 32 tiles at a
-// time (sequence walk + block-table lookup), then lane 0 issues, per tile,
-// TMA tensor copies of the K and V rows ([16 rows x 128 B] boxes with the
-// 128-byte swizzle, so the ldmatrix reads below are conflict free) into a
-// ring of NS stages guarded by full/empty mbarriers. Warps 1-4 consume tiles
-// round robin. Per tile a consumer warp computes, for every query head of
-// the GQA group at once (padded to 8 columns):
+// A CTA owns a group of HG kv heads and one share of the 16-token tiles of
+// every sequence (decode_common.cuh). Warp 0 is the producer: its lanes
+// resolve 32 tiles at a time (sequence walk + block-table lookup), then lane
+// 0 issues, per tile, one TMA tensor copy for K and one for V that move the
+// tile's rows for all HG heads at once (HG x 16 rows x D x 2 B = 16 KB for
+// HG = 4, D = 128 — one contiguous piece of a block). The tensor map views a
+// pool row as [head][half][64 elements] with dimensions ordered
+// (element, slot, half, head), so the box lands in shared memory as one
+// 2 KB region per (head, 64-column half) of 16 rows x 128 B with the 128-byte
+// swizzle, which makes the ldmatrix reads below conflict free. Stages are
+// guarded by full/empty mbarriers.
+//
+// Warps 1..HG are consumers, one per kv head; each sees every tile. For its
+// head, per tile, it computes for the whole GQA group at once (padded to 8
+// columns):
 //   S^T[16 tok x 8 heads] = K[16 x D] . Q^T[D x 8]    (D/16 mma.m16n8k16)
 //   online softmax over the 16 tokens per head (exp2 on the SFU, fp32)
 //   O^T[D x 8]           += V^T[D x 16] . P^T[16 x 8]  (D/16 mma.m16n8k16)
 // with P^T moved into B-operand layout by two movmatrix transposes, so each
 // K/V element is read from HBM once for the whole group. The tensor-core
-// instructions here are the warp-level mma.sync form: the path is bound by
-// HBM bandwidth, and mma.sync only removes the FMA/convert instruction issue
-// that would otherwise cap a CUDA-core GEMV at ~7 FMAs per loaded element.
-// At the end of each segment the four consumer warps combine their running
-// (max, sum, accumulator) states through shared memory (log-sum-exp) and
-// write the final row or a workspace partial.
+// instructions are the warp-level mma.sync form: the path is bound by HBM
+// bandwidth, and mma.sync only removes the FMA/convert issue that would
+// otherwise cap a CUDA-core GEMV at ~7 FMAs per loaded element. A warp writes
+// its segment's row (or workspace piece) itself when the sequence changes;
+// no cross-warp combine is needed.
 #include "decode_common.cuh"
 #include "kernels.h"
 
@@ -26,8 +32,6 @@ namespace irb {
 
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kThreads = 32 * (1 + kConsumerWarps);
 constexpr unsigned kFull = 0xffffffffu;
 
 struct __align__(16) ItemDesc {
@@ -36,61 +40,68 @@ struct __align__(16) ItemDesc {
   int seg;
   int packed;  // n_valid in bits 0-7, flags above
 };
-constexpr int kFlagValid = 1 << 8;    // copies were issued (block ids valid)
-constexpr int kFlagSeqEnd = 1 << 9;   // last tile of the sequence
-constexpr int kFlagWhole = 1 << 10;   // the segment is the whole sequence
-constexpr int kFlagEnd = 1 << 11;     // end-of-stream marker
+constexpr int kFlagValid = 1 << 8;     // copies were issued (block ids valid)
+constexpr int kFlagSeqEnd = 1 << 9;    // last tile of the sequence
+constexpr int kFlagWhole = 1 << 10;    // the segment is the whole sequence
+constexpr int kFlagEnd = 1 << 11;      // end-of-stream marker
+constexpr int kFlagSegStart = 1 << 12; // first tile of a segment
 
-template <int D, int NS>
+// R = rows per TMA box: 16, or 8 for 8-token blocks (two boxes per tile).
+template <int D, int HG, int NS, int R>
 struct Layout {
-  static constexpr int kHalf = kTile * 128;           // 16 rows x 128 B
-  static constexpr int kHalves = D / 64;              // 64-element column halves
-  static constexpr int kStage = 2 * kHalves * kHalf;  // K + V of one tile
-  static constexpr int kCombStride = D * 8 + 16;      // floats per warp
-  static constexpr int off_comb = NS * kStage;
-  static constexpr int off_desc = off_comb + kConsumerWarps * kCombStride * 4;
+  static constexpr int kHalves = D / 64;
+  static constexpr int kRegion = R * 128;                 // one (head, half) box slice
+  static constexpr int kBox = HG * kHalves * kRegion;     // one box, K or V
+  static constexpr int kSide = kBox * (kTile / R);        // K (or V) of one tile
+  static constexpr int kStage = 2 * kSide;
+  static constexpr int off_desc = NS * kStage;
   static constexpr int off_bar = off_desc + NS * 16;
-  static constexpr int off_misc = off_bar + (2 * NS + 2) * 8;
-  static constexpr int kBytes = off_misc + 256;
+  static constexpr int off_misc = off_bar + 2 * NS * 8;
+  static constexpr int kBytes = off_misc + 128;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
+  // byte offset of row `tok` (0..15) of (head, half) inside one side
+  static __device__ __forceinline__ int row_off(int head, int half, int tok) {
+    return (tok / R) * kBox + ((head * kHalves + half) * R + tok % R) * 128;
+  }
 };
 
-template <typename T, int D, int NS, bool BS8>
-__global__ void __launch_bounds__(kThreads)
+struct TmaParams {
+  int one_box;  // 1: one 4-D box per side; 0: one 3-D box per (head, half)
+};
+
+template <typename T, int D, int HG, int NS, int R>
+__global__ void __launch_bounds__(32 * (HG + 1), 1)
     decode_tma_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv,
-                      const DecodeArgs a) {
-  using L = Layout<D, NS>;
+                      const DecodeArgs a, const TmaParams tp) {
+  using L = Layout<D, HG, NS, R>;
+  constexpr int NT = 32 * (HG + 1);
   constexpr int KS = D / 16;  // k-steps of QK, m-tiles of PV
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int kvh = blockIdx.x, g = blockIdx.y;
+  const int hg = blockIdx.x, g = blockIdx.y;
+  const int kv0 = hg * HG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::off_bar);
   uint64_t* empty = full + NS;
-  uint64_t* flush_full = empty + NS;
-  uint64_t* flush_done = flush_full + 1;
   RangeInfo* ri = reinterpret_cast<RangeInfo*>(smem + L::off_misc);
-  int* seg_b = reinterpret_cast<int*>(smem + L::off_misc + 64);
-  int* seg_whole = seg_b + 2;
-  int64_t* sm_scan = reinterpret_cast<int64_t*>(smem + L::off_misc + 128);
+  int64_t* sm_scan = reinterpret_cast<int64_t*>(smem + L::off_misc + 64);
   ItemDesc* desc = reinterpret_cast<ItemDesc*>(smem + L::off_desc);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], HG);
     }
-    mbar_init(flush_full, kConsumerWarps);
-    mbar_init(flush_done, kConsumerWarps);
     fence_mbar_init();
   }
   if (threadIdx.x == 32) {
     prefetch_tensormap(&tmk);
     prefetch_tensormap(&tmv);
   }
-  find_share<kThreads, T>(a, g, kvh, ri, sm_scan);  // includes __syncthreads
+  find_share<NT, T>(a, g, kv0, HG, ri, sm_scan);  // includes __syncthreads
+  launch_dependents();
   const int64_t start = ri->start, end = ri->end;
   if (start >= end) return;
 
@@ -124,7 +135,7 @@ __global__ void __launch_bounds__(kThreads)
         const int nvalid = min(kTile, ctx - tok0);
         const int32_t* btr = a.block_tables + lb * a.bt_stride;
         bool ok;
-        if (BS8) {
+        if (R == 8) {
           const int blk = tok0 >> 3;
           const int id0 = btr[blk];
           ok = id0 >= 0 && id0 < a.num_blocks;
@@ -143,8 +154,8 @@ __global__ void __launch_bounds__(kThreads)
         if (!ok) set_err(a.err, IR_DEVERR_BLOCK_ID);
         seg_start = (tt == start) || (j == 0);
         const bool whole = (lp >= start) && (lp + ln <= end);
-        packed = nvalid | (ok ? kFlagValid : 0) |
-                 (j == ln - 1 ? kFlagSeqEnd : 0) | (whole ? kFlagWhole : 0);
+        packed = nvalid | (ok ? kFlagValid : 0) | (j == ln - 1 ? kFlagSeqEnd : 0) |
+                 (whole ? kFlagWhole : 0) | (seg_start ? kFlagSegStart : 0);
       }
       const unsigned starts = __ballot_sync(kFull, active && seg_start);
       const unsigned le_mask = (lane == 31) ? kFull : ((2u << lane) - 1u);
@@ -169,35 +180,26 @@ __global__ void __launch_bounds__(kThreads)
         const int64_t kr1 = __shfl_sync(kFull, row1, k);
         if (lane == 0) {
           desc[slot] = ItemDesc{kb, ktok, kseg, kpk};
-          uint8_t* st = smem + slot * L::kStage;
-          uint8_t* kd = st;
-          uint8_t* vd = st + L::kHalves * L::kHalf;
+          uint8_t* kd = smem + slot * L::kStage;
+          uint8_t* vd = kd + L::kSide;
           if (kpk & kFlagValid) {
-            if (BS8) {
-              const uint32_t boxes = kr1 >= 0 ? 2u : 1u;
-              mbar_arrive_expect_tx(&full[slot],
-                                    boxes * 2u * L::kHalves * (8u * 128u));
+            const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
+            mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox * 2 * L::kBox));
+            for (int bx = 0; bx < nbox; ++bx) {
+              const int row = static_cast<int>(bx == 0 ? kr0 : kr1);
+              if (tp.one_box) {
+                tma_load_4d(kd + bx * L::kBox, &tmk, &full[slot], 0, row, 0, kv0);
+                tma_load_4d(vd + bx * L::kBox, &tmv, &full[slot], 0, row, 0, kv0);
+              } else {
 #pragma unroll
-              for (int h = 0; h < L::kHalves; ++h) {
-                tma_load_3d(kd + h * L::kHalf, &tmk, &full[slot], 64 * h, kvh,
-                            static_cast<int>(kr0));
-                tma_load_3d(vd + h * L::kHalf, &tmv, &full[slot], 64 * h, kvh,
-                            static_cast<int>(kr0));
-                if (kr1 >= 0) {
-                  tma_load_3d(kd + h * L::kHalf + 8 * 128, &tmk, &full[slot],
-                              64 * h, kvh, static_cast<int>(kr1));
-                  tma_load_3d(vd + h * L::kHalf + 8 * 128, &tmv, &full[slot],
-                              64 * h, kvh, static_cast<int>(kr1));
+                for (int h = 0; h < HG; ++h) {
+#pragma unroll
+                  for (int hf = 0; hf < L::kHalves; ++hf) {
+                    const int off = bx * L::kBox + (h * L::kHalves + hf) * L::kRegion;
+                    tma_load_3d(kd + off, &tmk, &full[slot], 64 * hf, kv0 + h, row);
+                    tma_load_3d(vd + off, &tmv, &full[slot], 64 * hf, kv0 + h, row);
+                  }
                 }
-              }
-            } else {
-              mbar_arrive_expect_tx(&full[slot], L::kStage);
-#pragma unroll
-              for (int h = 0; h < L::kHalves; ++h) {
-                tma_load_3d(kd + h * L::kHalf, &tmk, &full[slot], 64 * h, kvh,
-                            static_cast<int>(kr0));
-                tma_load_3d(vd + h * L::kHalf, &tmv, &full[slot], 64 * h, kvh,
-                            static_cast<int>(kr0));
               }
             }
           } else {
@@ -215,33 +217,36 @@ __global__ void __launch_bounds__(kThreads)
       t += nact;
     }
     if (!abort) {
-      for (int k = 0; k < kConsumerWarps; ++k) {
-        const uint32_t slot = item % NS;
-        const uint32_t par = ((item / NS) & 1u) ^ 1u;
-        int ok_wait = 1;
-        if (lane == 0) ok_wait = mbar_wait_bounded(&empty[slot], par) ? 1 : 0;
-        ok_wait = __shfl_sync(kFull, ok_wait, 0);
-        if (!ok_wait) {
-          if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
-          break;
-        }
-        if (lane == 0) {
+      const uint32_t slot = item % NS;
+      const uint32_t par = ((item / NS) & 1u) ^ 1u;
+      if (lane == 0) {
+        if (mbar_wait_bounded(&empty[slot], par)) {
           desc[slot] = ItemDesc{0, 0, seg_base, kFlagEnd};
           mbar_arrive(&full[slot]);
+        } else {
+          set_err(a.err, IR_DEVERR_TIMEOUT);
         }
-        ++item;
       }
     }
     return;
   }
 
   // -------------------------------------------------------------- consumers
-  const int cw = warp - 1;
-  const int ct = cw * 32 + lane;  // 0..127
-  float* comb_all = reinterpret_cast<float*>(smem + L::off_comb);
-  float* comb = comb_all + cw * L::kCombStride;
-  const int grp = lane >> 2;       // token row / head column of fragments
-  const int qd = (lane & 3) * 2;   // column pair inside fragments
+  const int head = warp - 1;  // 0..HG-1
+  const int kvh = kv0 + head;
+  const int grp = lane >> 2;      // token row / head column of fragments
+  const int qd = (lane & 3) * 2;  // column pair inside fragments
+  // per-lane row offsets (bytes, within one side) of the ldmatrix reads
+  const int ktok = (lane & 7) + ((lane >> 3) & 1) * 8;  // K: non-transposed
+  const int kcsel = lane >> 4;
+  const int vtok = (lane & 7) + (lane >> 4) * 8;         // V: transposed
+  const int vcsel = (lane >> 3) & 1;
+  int koff[L::kHalves], voff[L::kHalves];
+#pragma unroll
+  for (int hf = 0; hf < L::kHalves; ++hf) {
+    koff[hf] = L::row_off(head, hf, ktok);
+    voff[hf] = L::row_off(head, hf, vtok);
+  }
 
   float acc[KS][4];
   float m[2], l[2];
@@ -253,12 +258,11 @@ __global__ void __launch_bounds__(kThreads)
   }
   m[0] = m[1] = -INFINITY;
   l[0] = l[1] = 0.f;
-  int cur_seg = 0, cur_b = -1;
-  uint32_t flushes = 0;
-  bool abort = false;
+  int cur_b = -1, seg_b = -1;
+  bool seg_whole = false, have_seg = false;
 
-  // Combine the four warps' states of segment cur_seg and write it out.
-  auto flush = [&]() -> bool {
+  // Write this warp's finished segment: the final row or a workspace piece.
+  auto flush = [&]() {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       l[j] += __shfl_xor_sync(kFull, l[j], 4);
@@ -266,86 +270,44 @@ __global__ void __launch_bounds__(kThreads)
       l[j] += __shfl_xor_sync(kFull, l[j], 16);
     }
 #pragma unroll
-    for (int i = 0; i < KS; ++i) {
-      const int d0 = 16 * i + grp;
-      *reinterpret_cast<float2*>(&comb[d0 * 8 + qd]) =
-          make_float2(acc[i][0], acc[i][1]);
-      *reinterpret_cast<float2*>(&comb[(d0 + 8) * 8 + qd]) =
-          make_float2(acc[i][2], acc[i][3]);
-    }
-    if (lane < 4) {
-      comb[D * 8 + qd] = m[0];
-      comb[D * 8 + qd + 1] = m[1];
-      comb[D * 8 + 8 + qd] = l[0];
-      comb[D * 8 + 8 + qd + 1] = l[1];
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(flush_full);
-    bool ok = mbar_wait_bounded(flush_full, flushes & 1u);
-    if (__any_sync(kFull, !ok)) {
-      if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
-      return false;
-    }
-    const int sb = seg_b[cur_seg & 1];
-    const bool whole = seg_whole[cur_seg & 1] != 0;
-    for (int idx = ct; idx < a.n_rep * D; idx += 32 * kConsumerWarps) {
-      const int n = idx / D, d = idx - n * D;
-      float mw[kConsumerWarps], M = -INFINITY;
+    for (int j = 0; j < 2; ++j) {
+      const int n = qd + j;
+      if (n < a.n_rep) {
+        const bool empty_seg = (m[j] == -INFINITY);
+        const float inv = empty_seg ? 0.f : 1.f / l[j];
+        const float lse2 = empty_seg ? -INFINITY : m[j] + log2f(l[j]);
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        mw[w] = comb_all[w * L::kCombStride + D * 8 + n];
-        M = fmaxf(M, mw[w]);
-      }
-      float val = 0.f, lse2 = -INFINITY;
-      if (M != -INFINITY) {
-        float lsum = 0.f, osum = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-          const float wt = ex2(mw[w] - M);
-          lsum += wt * comb_all[w * L::kCombStride + D * 8 + 8 + n];
-          osum += wt * comb_all[w * L::kCombStride + d * 8 + n];
+        for (int i = 0; i < KS; ++i) {
+          const int d0 = 16 * i + grp;
+          write_segment_value<T>(a, kvh, g, seg_b, seg_whole, n, d0, acc[i][j] * inv, lse2);
+          write_segment_value<T>(a, kvh, g, seg_b, seg_whole, n, d0 + 8,
+                                 acc[i][j + 2] * inv, lse2);
         }
-        val = osum / lsum;
-        lse2 = M + log2f(lsum);
       }
-      write_segment_value<T>(a, kvh, g, sb, whole, n, d, val, lse2);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(flush_done);
-    ok = mbar_wait_bounded(flush_done, flushes & 1u);
-    if (__any_sync(kFull, !ok)) {
-      if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
-      return false;
-    }
-    ++flushes;
 #pragma unroll
     for (int i = 0; i < KS; ++i)
       acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     m[0] = m[1] = -INFINITY;
     l[0] = l[1] = 0.f;
-    return true;
   };
 
-  for (uint32_t item = cw;; item += kConsumerWarps) {
+  for (uint32_t item = 0;; ++item) {
     const uint32_t slot = item % NS, par = (item / NS) & 1u;
     const bool ok = mbar_wait_bounded(&full[slot], par);
     if (__any_sync(kFull, !ok)) {
       if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
-      abort = true;
       break;
     }
     const ItemDesc dsc = desc[slot];
     const int pk = dsc.packed;
-    while (cur_seg < dsc.seg && !abort) {
-      abort = !flush();
-      ++cur_seg;
-    }
-    if (abort || (pk & kFlagEnd)) break;
-
+    if ((pk & (kFlagSegStart | kFlagEnd)) && have_seg) flush();
+    if (pk & kFlagEnd) break;
     const int b = dsc.b;
-    if (lane == 0) {
-      seg_b[cur_seg & 1] = b;
-      seg_whole[cur_seg & 1] = (pk & kFlagWhole) ? 1 : 0;
+    if (pk & kFlagSegStart) {
+      have_seg = true;
+      seg_b = b;
+      seg_whole = (pk & kFlagWhole) != 0;
     }
     if (b != cur_b) {
       cur_b = b;
@@ -362,19 +324,19 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
     const int nvalid = (pk & kFlagValid) ? (pk & 0xff) : 0;
-    uint8_t* st = smem + slot * L::kStage;
-    uint8_t* vst = st + L::kHalves * L::kHalf;
-    const uint32_t kb = smem_u32(st);
-    const uint32_t vb = kb + L::kHalves * L::kHalf;
+    uint8_t* kst = smem + slot * L::kStage;
+    uint8_t* vst = kst + L::kSide;
+    const uint32_t kb = smem_u32(kst);
+    const uint32_t vb = kb + L::kSide;
     bool wrote = false;
     if (nvalid > 0) {
       if (nvalid < kTile) {
-        // rows past the context: zero V so 0 * garbage cannot make NaN
+        // rows past the context: zero this head's V so 0 * garbage cannot make NaN
         const int per_row = L::kHalves * 8;
         for (int idx = lane; idx < (kTile - nvalid) * per_row; idx += 32) {
           const int r = nvalid + idx / per_row, rem = idx % per_row;
-          *reinterpret_cast<uint4*>(vst + (rem >> 3) * L::kHalf + r * 128 +
-                                    (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(vst + L::row_off(head, rem >> 3, r) + (rem & 7) * 16) =
+              make_uint4(0, 0, 0, 0);
         }
         wrote = true;
       }
@@ -394,10 +356,9 @@ __global__ void __launch_bounds__(kThreads)
           const T* src = reinterpret_cast<const T*>(is_v ? a.v_new : a.k_new) +
                          b * a.kv_stride + static_cast<int64_t>(kvh) * D + c * 8;
           const uint4 val = *reinterpret_cast<const uint4*>(src);
-          uint8_t* base = is_v ? vst : st;
-          const int cc = c & 7;
-          *reinterpret_cast<uint4*>(base + (c >> 3) * L::kHalf + r * 128 +
-                                    ((cc ^ (r & 7)) << 4)) = val;
+          uint8_t* base = is_v ? vst : kst;
+          *reinterpret_cast<uint4*>(base + L::row_off(head, c >> 3, r) +
+                                    (((c & 7) ^ (r & 7)) << 4)) = val;
           if (slot_w >= 0 && slot_w < a.num_slots) {
             T* dst = const_cast<T*>(reinterpret_cast<const T*>(is_v ? a.v_pool : a.k_pool)) +
                      (slot_w * a.Hkv + kvh) * D + c * 8;
@@ -410,18 +371,13 @@ __global__ void __launch_bounds__(kThreads)
 
       // S^T = K . Q^T : 16 tokens x 8 head columns
       float s[4] = {0.f, 0.f, 0.f, 0.f};
-      {
-        const int tok = (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int csel = lane >> 4;
 #pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-          const int chunk = (ks & 3) * 2 + csel;
-          const uint32_t addr = kb + (ks >> 2) * L::kHalf + tok * 128 +
-                                ((chunk ^ (tok & 7)) << 4);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4(addr, a0, a1, a2, a3);
-          mma_16816<T>(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
-        }
+      for (int ks = 0; ks < KS; ++ks) {
+        const int chunk = (ks & 3) * 2 + kcsel;
+        const uint32_t addr = kb + koff[ks >> 2] + ((chunk ^ (ktok & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(addr, a0, a1, a2, a3);
+        mma_16816<T>(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
       }
       // online softmax over this tile's tokens, per head column
       const bool v0 = grp < nvalid, v1 = grp + 8 < nvalid;
@@ -450,19 +406,13 @@ __global__ void __launch_bounds__(kThreads)
       const uint32_t pb0 = movmatrix_trans(pack2<T>(p[0], p[1]));
       const uint32_t pb1 = movmatrix_trans(pack2<T>(p[2], p[3]));
       // O^T += V^T . P^T
-      {
-        const int mi = lane >> 3;
-        const int tok = (lane & 7) + (mi >> 1) * 8;
-        const int csel = mi & 1;
 #pragma unroll
-        for (int i = 0; i < KS; ++i) {
-          const int chunk = (i & 3) * 2 + csel;
-          const uint32_t addr = vb + (i >> 2) * L::kHalf + tok * 128 +
-                                ((chunk ^ (tok & 7)) << 4);
-          uint32_t a0, a1, a2, a3;
-          ldsm_x4_trans(addr, a0, a1, a2, a3);
-          mma_16816<T>(acc[i], a0, a1, a2, a3, pb0, pb1);
-        }
+      for (int i = 0; i < KS; ++i) {
+        const int chunk = (i & 3) * 2 + vcsel;
+        const uint32_t addr = vb + voff[i >> 2] + ((chunk ^ (vtok & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(addr, a0, a1, a2, a3);
+        mma_16816<T>(acc[i], a0, a1, a2, a3, pb0, pb1);
       }
     }
     if (wrote) fence_proxy_async_shared();
@@ -471,70 +421,85 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-template <typename T, int D, int NS, bool BS8>
-int launch_one(const CUtensorMap& tmk, const CUtensorMap& tmv,
-               const DecodeArgs& a, cudaStream_t stream) {
-  using L = Layout<D, NS>;
-  auto kern = decode_tma_kernel<T, D, NS, BS8>;
+constexpr int kStages = 3;  // 2 CTAs per SM at HG = 4, D = 128
+
+template <typename T, int D, int HG, int R>
+int launch_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+             const TmaParams& tp, cudaStream_t stream) {
+  using L = Layout<D, HG, kStages, R>;
   static_assert(L::kAlloc <= 227 * 1024, "shared memory budget");
-  cudaError_t e = cudaFuncSetAttribute(
-      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+  auto kern = decode_tma_kernel<T, D, HG, kStages, R>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       L::kAlloc);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(a.Hkv, a.G);
-  kern<<<grid, kThreads, L::kAlloc, stream>>>(tmk, tmv, a);
+  dim3 grid(a.Hkv / HG, a.G);
+  kern<<<grid, 32 * (HG + 1), L::kAlloc, stream>>>(tmk, tmv, a, tp);
   return static_cast<int>(cudaGetLastError());
 }
 
-template <typename T, int D, int NS, bool BS8>
-int occupancy_one() {
-  using L = Layout<D, NS>;
-  auto kern = decode_tma_kernel<T, D, NS, BS8>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           L::kAlloc) != cudaSuccess)
+template <typename T, int D, int HG, int R>
+int occupancy_t() {
+  using L = Layout<D, HG, kStages, R>;
+  auto kern = decode_tma_kernel<T, D, HG, kStages, R>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
+      cudaSuccess)
     return 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads,
-                                                    L::kAlloc) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 32 * (HG + 1), L::kAlloc) !=
+      cudaSuccess)
     return 1;
   return n > 0 ? n : 1;
 }
 
-constexpr int kStages = 8;  // multiple of kConsumerWarps (slot reuse stays in one warp)
-static_assert(kStages % kConsumerWarps == 0, "stage ring must align with warps");
+// Dispatch over (D, HG, R) for one dtype; op 0 = launch, 1 = occupancy.
+template <typename T, int D, int HG>
+int by_rows(int op, int R, const CUtensorMap* tmk, const CUtensorMap* tmv,
+            const DecodeArgs* a, const TmaParams* tp, cudaStream_t s) {
+  if (R == 8)
+    return op ? occupancy_t<T, D, HG, 8>() : launch_t<T, D, HG, 8>(*tmk, *tmv, *a, *tp, s);
+  return op ? occupancy_t<T, D, HG, 16>() : launch_t<T, D, HG, 16>(*tmk, *tmv, *a, *tp, s);
+}
 
-template <typename T>
-int dispatch_launch(const CUtensorMap& tmk, const CUtensorMap& tmv,
-                    const DecodeArgs& a, cudaStream_t s) {
-  const bool bs8 = a.bs == 8;
-  if (a.D == 128)
-    return bs8 ? launch_one<T, 128, kStages, true>(tmk, tmv, a, s)
-               : launch_one<T, 128, kStages, false>(tmk, tmv, a, s);
-  return bs8 ? launch_one<T, 64, kStages, true>(tmk, tmv, a, s)
-             : launch_one<T, 64, kStages, false>(tmk, tmv, a, s);
+template <typename T, int D>
+int by_group(int op, int HG, int R, const CUtensorMap* tmk, const CUtensorMap* tmv,
+             const DecodeArgs* a, const TmaParams* tp, cudaStream_t s) {
+  switch (HG) {
+    case 1: return by_rows<T, D, 1>(op, R, tmk, tmv, a, tp, s);
+    case 2: return by_rows<T, D, 2>(op, R, tmk, tmv, a, tp, s);
+    case 4: return by_rows<T, D, 4>(op, R, tmk, tmv, a, tp, s);
+    default: return by_rows<T, D, 8>(op, R, tmk, tmv, a, tp, s);
+  }
 }
 
 template <typename T>
-int dispatch_occupancy(int D, bool bs8) {
-  if (D == 128)
-    return bs8 ? occupancy_one<T, 128, kStages, true>()
-               : occupancy_one<T, 128, kStages, false>();
-  return bs8 ? occupancy_one<T, 64, kStages, true>()
-             : occupancy_one<T, 64, kStages, false>();
+int by_dim(int op, int D, int HG, int R, const CUtensorMap* tmk, const CUtensorMap* tmv,
+           const DecodeArgs* a, const TmaParams* tp, cudaStream_t s) {
+  return D == 128 ? by_group<T, 128>(op, HG, R, tmk, tmv, a, tp, s)
+                  : by_group<T, 64>(op, HG, R, tmk, tmv, a, tp, s);
 }
 
 }  // namespace
 
-int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv,
-                      const DecodeArgs& a, int dtype, cudaStream_t stream) {
-  if (dtype == IR_DTYPE_BF16)
-    return dispatch_launch<__nv_bfloat16>(tmk, tmv, a, stream);
-  return dispatch_launch<__half>(tmk, tmv, a, stream);
+int tma_head_group(int num_kv_heads) {
+  for (int hg : {8, 4, 2, 1})
+    if (num_kv_heads % hg == 0) return hg;
+  return 1;
 }
 
-int decode_tma_occupancy(int dtype, int D, int bs) {
+int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
+                      int dtype, int one_box, cudaStream_t stream) {
+  const TmaParams tp{one_box};
+  const int HG = tma_head_group(a.Hkv), R = a.bs == 8 ? 8 : 16;
   if (dtype == IR_DTYPE_BF16)
-    return dispatch_occupancy<__nv_bfloat16>(D, bs == 8);
-  return dispatch_occupancy<__half>(D, bs == 8);
+    return by_dim<__nv_bfloat16>(0, a.D, HG, R, &tmk, &tmv, &a, &tp, stream);
+  return by_dim<__half>(0, a.D, HG, R, &tmk, &tmv, &a, &tp, stream);
+}
+
+int decode_tma_occupancy(int dtype, int D, int Hkv, int bs) {
+  const int HG = tma_head_group(Hkv), R = bs == 8 ? 8 : 16;
+  if (dtype == IR_DTYPE_BF16)
+    return by_dim<__nv_bfloat16>(1, D, HG, R, nullptr, nullptr, nullptr, nullptr, nullptr);
+  return by_dim<__half>(1, D, HG, R, nullptr, nullptr, nullptr, nullptr, nullptr);
 }
 
 }  // namespace irb

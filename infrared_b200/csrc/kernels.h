@@ -10,16 +10,22 @@ namespace irb {
 
 struct DecodeArgs;
 
-// decode_tma.cu: 16-bit pools, D in {64, 128}, group <= 8, bs == 8 or bs % 16 == 0
+// decode_tma.cu: 16-bit pools, D in {64, 128}, group <= 8, bs == 8 or bs % 16 == 0.
+// One CTA covers tma_head_group(Hkv) kv heads; one_box selects the 4-D
+// (one copy per tile side) or the 3-D (one copy per head and half) map.
+int tma_head_group(int num_kv_heads);
 int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv,
-                      const DecodeArgs& a, int dtype, cudaStream_t stream);
-int decode_tma_occupancy(int dtype, int D, int bs);
+                      const DecodeArgs& a, int dtype, int one_box,
+                      cudaStream_t stream);
+int decode_tma_occupancy(int dtype, int D, int Hkv, int bs);
 
 // decode_generic.cu: any dtype, D in {64, 128}, group <= 16, any block size
 int launch_decode_generic(const DecodeArgs& a, int dtype, cudaStream_t stream);
 int decode_generic_occupancy(int dtype, int D);
 
-// merges of split sequences (decode_generic.cu)
+// merges (decode_generic.cu): the pieces of sequences split across CTAs
+// (programmatic dependent launch behind the decode kernel), and partials of
+// KV ranges computed elsewhere (e.g. other GPUs)
 int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t stream);
 int launch_lse_merge(void* out, int64_t out_stride, const float* o_parts,
                      const float* lse_parts, int P, int B, int H, int D,

@@ -253,13 +253,17 @@ def decode_plan(q, k_pool, block_tables, block_size, scale=1.0):
     return path.value, g.value, lib.ir_paged_decode_workspace_size(s)
 
 
-def _ws(s: DecodeShape, dev: int, ws: torch.Tensor | None):
-    nbytes = _lib.load().ir_paged_decode_workspace_size(s)
+def _ws(s: DecodeShape, dev: int, ws: torch.Tensor | None) -> torch.Tensor:
+    """The call's workspace: the caller's, or the cached per-device one."""
+    lib = _lib.load()
+    nbytes = lib.ir_paged_decode_workspace_size(s)
     if nbytes == 0:
-        check(_lib.load().ir_paged_decode_plan(s, None, None))
+        check(lib.ir_paged_decode_plan(s, None, None))
     if ws is None:
         ws = workspace(nbytes, dev)
-    return ws, nbytes
+    elif ws.numel() < nbytes:
+        raise ValueError(f"workspace of {ws.numel()} bytes < {nbytes} needed")
+    return ws
 
 
 def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
@@ -280,7 +284,7 @@ def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
             out.stride(1) != q.shape[2]:
         raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
     s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
-    ws, nbytes = _ws(s, dev, ws)
+    ws = _ws(s, dev, ws)
     check(_lib.load().ir_paged_decode(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
@@ -316,7 +320,7 @@ def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
     s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
-    ws, nbytes = _ws(s, dev, ws)
+    ws = _ws(s, dev, ws)
     check(_lib.load().ir_paged_decode_write(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
@@ -341,7 +345,7 @@ def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor
             and lse.dtype == torch.float32):
         raise ValueError("o and lse must be contiguous fp32")
     s = _shape(q, k_pool, block_tables, block_size, scale, h * d)
-    ws, nbytes = _ws(s, dev, ws)
+    ws = _ws(s, dev, ws)
     check(_lib.load().ir_paged_decode_lse(
         o.data_ptr(), lse.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),

@@ -77,11 +77,12 @@ def test_tma_and_cuda_core_paths_agree(name):
     assert ops.decode_plan(q, kp, bt, w.block_size)[0] == 2
     want = oracle_decode(w, *[host_f32(t) for t in (q, kp, vp)])
     outs = {}
-    for path in (1, 2):
+    for path in (1, 2, 3):   # CUDA cores, TMA one copy per tile, TMA per (head, half)
         ops.set_decode_path(path)
         outs[path] = host_f32(irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size))
         assert_close_bf16(outs[path], want)
     assert np.abs(outs[1] - outs[2]).max() < 2e-2
+    assert np.array_equal(outs[2], outs[3])
 
 
 # ----------------------------------------------------------- sweeps
@@ -417,3 +418,23 @@ def test_cuda_graph_capture_and_replay():
         pool.v.copy_(pool_ref_v)
         eager = step(newq, k, v, ws, gs, mask)
         assert torch.equal(out_static, eager)
+
+
+def test_workspace_reuse_across_shapes():
+    """Split sequences are merged from pieces in the workspace; the workspace
+    needs no initialisation and one buffer serves calls of any shape."""
+    w = wl.custom(45, 16, 28, 4, 128, 16, 100, 3000, "bfloat16")
+    q, kp, vp, _, _ = dev_values(wl.numpy_values(w, 4), torch.bfloat16)
+    bt, ctx, _ = dev_meta(w)
+    _, ctas, nbytes = ops.decode_plan(q, kp, bt, 16, w.scale)
+    assert ctas > w.batch   # sequences really are split across CTAs
+    ws = torch.full((nbytes,), 0x7f, dtype=torch.uint8, device=DEV)   # garbage on purpose
+    outs = [irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16, ws=ws) for _ in range(3)]
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    assert_close_bf16(host_f32(outs[0]), oracle_decode(w, *[host_f32(t) for t in (q, kp, vp)]))
+    # a smaller batch after a larger one reuses the workspace (its tiles are
+    # shared out differently, so it agrees within tolerance)
+    small = irb.paged_decode(q[:3], kp, vp, bt[:3], ctx[:3], w.scale, 16, ws=ws)
+    assert_close_bf16(host_f32(small), host_f32(outs[0][:3]))
+    with pytest.raises(ValueError, match="workspace"):
+        irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16, ws=ws[:256])
