@@ -61,6 +61,8 @@ def parse_args():
     p.add_argument("--soak", type=float, default=1.5,
                    help="seconds of untimed replays before timing (clock sampling)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--batch", type=int, default=0,
+                   help="override the workload's per-GPU batch (c2/c3/c4)")
     p.add_argument("--decode-path", type=int, default=0,
                    help="kernel override (ir_set_decode_path): 0 auto, 1 CUDA-core, "
                         "2 TMA, 3 TMA with one copy per head and half")
@@ -198,9 +200,11 @@ def dist_info():
     return world, rank, local
 
 
-def make_workload(name, rank):
+def make_workload(name, rank, batch=0):
     from infrared_b200 import workloads as wl
 
+    if batch:
+        return wl.CONFIGS[name](seed=rank, batch=batch)
     return wl.CONFIGS[name](seed=rank)
 
 
@@ -219,7 +223,7 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     ops.set_decode_path(args.decode_path)
-    w = make_workload(args.config, rank)
+    w = make_workload(args.config, rank, args.batch)
     fused = args.config == "c3"
     bt = torch.from_numpy(w.block_tables).to(dev)
     ctx = torch.from_numpy(w.context_lens).to(dev)

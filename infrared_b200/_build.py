@@ -46,22 +46,27 @@ def up_to_date() -> bool:
     return all(f.stat().st_mtime <= t for f in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and up_to_date():
+def build(force: bool = False, verbose: bool = False, out: Path | None = None,
+          defines: tuple[str, ...] = ()) -> Path:
+    """Compile the library (to ``out`` with extra ``-D`` defines for tuning
+    variants; the default build goes next to this file)."""
+    dst = Path(out) if out is not None else LIB
+    if out is None and not defines and not force and up_to_date():
         return LIB
     cmd = [
         nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo",
         "-Xcompiler", "-fPIC,-O3", "-shared", "-cudart", "static",
         "--expt-relaxed-constexpr", "-I", str(INCLUDE),
-        "-o", str(LIB) + ".tmp",
+        *[f"-D{d}" for d in defines],
+        "-o", str(dst) + ".tmp",
         *[str(CSRC / s) for s in SOURCES],
     ]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True, cwd=str(CSRC))
-    os.replace(str(LIB) + ".tmp", LIB)
-    return LIB
+    os.replace(str(dst) + ".tmp", dst)
+    return dst
 
 
 if __name__ == "__main__":

@@ -13,7 +13,11 @@ from ctypes import (POINTER, c_char_p, c_float, c_int, c_int32, c_int64,
                     c_size_t, c_void_p)
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().with_name("libinfrared_b200.so")
+import os
+
+# INFRARED_B200_LIB points at another build of the library (tuning variants).
+LIB_PATH = Path(os.environ.get("INFRARED_B200_LIB") or
+                Path(__file__).resolve().with_name("libinfrared_b200.so"))
 
 IR_DTYPE_F32, IR_DTYPE_BF16, IR_DTYPE_F16 = 0, 1, 2
 IR_OK, IR_ERR_INVALID_ARG, IR_ERR_UNSUPPORTED, IR_ERR_CUDA, IR_ERR_WORKSPACE = range(5)

@@ -170,14 +170,18 @@ __global__ void __launch_bounds__(kGenThreads)
 }
 
 // Combine the pieces of the split sequences: CTA (kv head x query head in
-// group, sequence), one thread per head-dim column. Every piece's loads are
-// independent, so the merge of a sequence costs about one L2 round trip.
+// group, sequence) of 4 warps; warp w folds pieces w, w+4, ... with an online
+// log-sum-exp, each lane owning 4 consecutive head-dim columns (16-byte
+// loads), then the 4 warp states are combined through shared memory. The
+// pieces' loads are independent, so a merge costs a few L2 round trips even
+// when a sequence spans dozens of CTAs.
 template <typename T>
 __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   wait_prerequisites();  // the decode grid's pieces and prefix are complete
-  __shared__ float red[2][4];
+  __shared__ float4 s_acc[4][32];
+  __shared__ float s_m[4], s_s[4];
   const int kvh = blockIdx.x / a.n_rep, n = blockIdx.x % a.n_rep, b = blockIdx.y;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t pb = a.ws_prefix[b];
   const int64_t nb = a.ws_prefix[b + 1] - pb;
   const int64_t total = a.ws_prefix[a.B];
@@ -187,32 +191,56 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   const int parts = share_of(pb + nb - 1, total, G) - glo + 1;
   if (parts == 1) return;  // written whole by one CTA
   const int64_t base = static_cast<int64_t>(kvh) * (a.G + a.B) + glo + b;
-  const float* lse = a.ws_lse + base * a.n_rep + n;  // stride n_rep per part
-  float mx = -INFINITY;
-  for (int i = tid; i < parts; i += blockDim.x) mx = fmaxf(mx, lse[i * a.n_rep]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) red[0][warp] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
-  float sum = 0.f;
-  if (mx != -INFINITY)
-    for (int i = tid; i < parts; i += blockDim.x) sum += ex2(lse[i * a.n_rep] - mx);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-  if (lane == 0) red[1][warp] = sum;
-  __syncthreads();
-  sum = red[1][0] + red[1][1] + red[1][2] + red[1][3];
-  const float inv = sum > 0.f ? 1.f / sum : 0.f;
-  const float lse2 = sum > 0.f ? mx + log2f(sum) : -INFINITY;
-  const float* o = a.ws_o + (base * a.n_rep + n) * a.D;  // stride n_rep * D per part
+  const float* lse = a.ws_lse + base * a.n_rep + n;       // stride n_rep per piece
+  const float* o = a.ws_o + (base * a.n_rep + n) * a.D;   // stride n_rep * D per piece
   const int64_t ostride = static_cast<int64_t>(a.n_rep) * a.D;
-  for (int d = tid; d < a.D; d += blockDim.x) {
-    float acc = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < parts; ++i) acc += ex2(lse[i * a.n_rep] - mx) * o[i * ostride + d];
-    write_segment_value<T>(a, kvh, 0, b, true, n, d, mx == -INFINITY ? 0.f : acc * inv, lse2);
+  const bool active = lane * 4 < a.D;
+  float M = -INFINITY, S = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int i = warp; i < parts; i += 4) {
+    const float li = lse[i * a.n_rep];
+    const float4 oi = active ? *reinterpret_cast<const float4*>(o + i * ostride + lane * 4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (li == -INFINITY) continue;
+    const float Mn = fmaxf(M, li);
+    const float c = ex2(M - Mn), w = ex2(li - Mn);  // ex2(-inf) = 0 on the first piece
+    S = S * c + w;
+    acc.x = acc.x * c + w * oi.x;
+    acc.y = acc.y * c + w * oi.y;
+    acc.z = acc.z * c + w * oi.z;
+    acc.w = acc.w * c + w * oi.w;
+    M = Mn;
   }
+  s_acc[warp][lane] = acc;
+  if (lane == 0) {
+    s_m[warp] = M;
+    s_s[warp] = S;
+  }
+  __syncthreads();
+  if (warp != 0) return;
+  float Mt = fmaxf(fmaxf(s_m[0], s_m[1]), fmaxf(s_m[2], s_m[3]));
+  float St = 0.f;
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    if (s_s[w] == 0.f) continue;
+    const float c = ex2(s_m[w] - Mt);
+    const float4 x = s_acc[w][lane];
+    St += c * s_s[w];
+    r.x += c * x.x;
+    r.y += c * x.y;
+    r.z += c * x.z;
+    r.w += c * x.w;
+  }
+  if (!active) return;
+  const bool empty = St == 0.f;
+  const float inv = empty ? 0.f : 1.f / St;
+  const float lse2 = empty ? -INFINITY : Mt + log2f(St);
+  const float v[4] = {r.x * inv, r.y * inv, r.z * inv, r.w * inv};
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    write_segment_value<T>(a, kvh, 0, b, true, n, lane * 4 + k, v[k], lse2);
 }
 
 template <typename T>
@@ -282,7 +310,7 @@ int decode_generic_occupancy(int dtype, int D) {
 int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv * a.n_rep, a.B);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(128);  // 4 warps; split_merge_kernel assumes exactly 4
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -57,7 +57,11 @@ struct Layout {
   static constexpr int off_desc = NS * kStage;
   static constexpr int off_bar = off_desc + NS * 16;
   static constexpr int off_misc = off_bar + 2 * NS * 8;
-  static constexpr int kBytes = off_misc + 128;
+  // per consumer warp: [8 heads][D + 4] fp32 output staging + 8 lse values
+  static constexpr int kFlushStride = D + 4;  // padding spreads the 4 column lanes over banks
+  static constexpr int kFlushFloats = 8 * kFlushStride + 8;
+  static constexpr int off_flush = off_misc + 128;
+  static constexpr int kBytes = off_flush + HG * kFlushFloats * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
   // byte offset of row `tok` (0..15) of (head, half) inside one side
   static __device__ __forceinline__ int row_off(int head, int half, int tok) {
@@ -261,7 +265,11 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   int cur_b = -1, seg_b = -1;
   bool seg_whole = false, have_seg = false;
 
+  float* fbuf = reinterpret_cast<float*>(smem + L::off_flush) + head * L::kFlushFloats;
+
   // Write this warp's finished segment: the final row or a workspace piece.
+  // The normalised fragments go through shared memory so that the global
+  // writes are whole 16-byte pieces of contiguous head rows.
   auto flush = [&]() {
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
@@ -271,20 +279,56 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
     }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const int n = qd + j;
-      if (n < a.n_rep) {
-        const bool empty_seg = (m[j] == -INFINITY);
-        const float inv = empty_seg ? 0.f : 1.f / l[j];
-        const float lse2 = empty_seg ? -INFINITY : m[j] + log2f(l[j]);
+      const bool empty_seg = (m[j] == -INFINITY);
+      const float inv = empty_seg ? 0.f : 1.f / l[j];
+      float* row = fbuf + (qd + j) * L::kFlushStride;
 #pragma unroll
-        for (int i = 0; i < KS; ++i) {
-          const int d0 = 16 * i + grp;
-          write_segment_value<T>(a, kvh, g, seg_b, seg_whole, n, d0, acc[i][j] * inv, lse2);
-          write_segment_value<T>(a, kvh, g, seg_b, seg_whole, n, d0 + 8,
-                                 acc[i][j + 2] * inv, lse2);
-        }
+      for (int i = 0; i < KS; ++i) {
+        row[16 * i + grp] = acc[i][j] * inv;
+        row[16 * i + grp + 8] = acc[i][j + 2] * inv;
       }
+      if (grp == 0) fbuf[8 * L::kFlushStride + qd + j] = empty_seg ? -INFINITY : m[j] + log2f(l[j]);
     }
+    __syncwarp();
+    const int nr = a.n_rep;
+    const float* lse2 = fbuf + 8 * L::kFlushStride;
+    if (seg_whole && !a.lse_mode) {
+      // final rows in T: 16-byte pieces of 8 elements
+      constexpr int kPer = D / 8;
+      T* dst = reinterpret_cast<T*>(a.out) + seg_b * a.out_stride +
+               static_cast<int64_t>(kvh * nr) * D;
+      for (int c = lane; c < nr * kPer; c += 32) {
+        const int n = c / kPer, d = (c % kPer) * 8;
+        const float4 x = *reinterpret_cast<const float4*>(fbuf + n * L::kFlushStride + d);
+        const float4 y = *reinterpret_cast<const float4*>(fbuf + n * L::kFlushStride + d + 4);
+        uint4 v;
+        v.x = pack2<T>(x.x, x.y);
+        v.y = pack2<T>(x.z, x.w);
+        v.z = pack2<T>(y.x, y.y);
+        v.w = pack2<T>(y.z, y.w);
+        *reinterpret_cast<uint4*>(dst + n * D + d) = v;
+      }
+    } else {
+      // fp32 rows: the LSE-mode output or a workspace piece
+      float* dst;
+      float* ldst;
+      if (seg_whole) {
+        dst = a.lse_o + (static_cast<int64_t>(seg_b) * a.H + kvh * nr) * D;
+        ldst = a.lse_out + static_cast<int64_t>(seg_b) * a.H + kvh * nr;
+      } else {
+        const int64_t slot = static_cast<int64_t>(kvh) * (a.G + a.B) + g + seg_b;
+        dst = a.ws_o + slot * nr * D;
+        ldst = a.ws_lse + slot * nr;
+      }
+      constexpr int kPer = D / 4;
+      for (int c = lane; c < nr * kPer; c += 32) {
+        const int n = c / kPer, d = (c % kPer) * 4;
+        *reinterpret_cast<float4*>(dst + n * D + d) =
+            *reinterpret_cast<const float4*>(fbuf + n * L::kFlushStride + d);
+      }
+      if (lane < nr) ldst[lane] = seg_whole ? lse2[lane] * kLn2 : lse2[lane];
+    }
+    __syncwarp();
 #pragma unroll
     for (int i = 0; i < KS; ++i)
       acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -369,16 +413,22 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
       }
       __syncwarp();
 
-      // S^T = K . Q^T : 16 tokens x 8 head columns
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      // S^T = K . Q^T : 16 tokens x 8 head columns (two accumulators halve
+      // the dependent MMA chain)
+      float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         const int chunk = (ks & 3) * 2 + kcsel;
         const uint32_t addr = kb + koff[ks >> 2] + ((chunk ^ (ktok & 7)) << 4);
         uint32_t a0, a1, a2, a3;
         ldsm_x4(addr, a0, a1, a2, a3);
-        mma_16816<T>(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+        if (ks & 1)
+          mma_16816<T>(s2, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+        else
+          mma_16816<T>(s, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
       }
+#pragma unroll
+      for (int r = 0; r < 4; ++r) s[r] += s2[r];
       // online softmax over this tile's tokens, per head column
       const bool v0 = grp < nvalid, v1 = grp + 8 < nvalid;
       float p[4];
@@ -421,14 +471,29 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   }
 }
 
-constexpr int kStages = 3;  // 2 CTAs per SM at HG = 4, D = 128
+// Stage ring depth: as many tiles as fit in one CTA's shared memory next to
+// the flush buffers (one CTA per SM; measured faster on B200 than two CTAs
+// with half the stages each). IRB_TMA_STAGES caps it for tuning builds.
+#ifndef IRB_TMA_STAGES
+#define IRB_TMA_STAGES 16
+#endif
+template <int D, int HG, int R>
+constexpr int stages_for() {
+  constexpr int stage = 2 * HG * (D / 64) * kTile * 128;  // K + V of one tile
+  constexpr int flush = HG * (8 * (D + 4) + 8) * 4;
+  constexpr int budget = 227 * 1024 - 1024 - 512 - flush;   // align slack, misc
+  constexpr int fit = budget / (stage + 48);                // + desc and barriers
+  constexpr int n = fit < IRB_TMA_STAGES ? fit : IRB_TMA_STAGES;
+  return n < 2 ? 2 : n;
+}
 
 template <typename T, int D, int HG, int R>
 int launch_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
              const TmaParams& tp, cudaStream_t stream) {
-  using L = Layout<D, HG, kStages, R>;
+  constexpr int NS = stages_for<D, HG, R>();
+  using L = Layout<D, HG, NS, R>;
   static_assert(L::kAlloc <= 227 * 1024, "shared memory budget");
-  auto kern = decode_tma_kernel<T, D, HG, kStages, R>;
+  auto kern = decode_tma_kernel<T, D, HG, NS, R>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        L::kAlloc);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -439,8 +504,9 @@ int launch_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a
 
 template <typename T, int D, int HG, int R>
 int occupancy_t() {
-  using L = Layout<D, HG, kStages, R>;
-  auto kern = decode_tma_kernel<T, D, HG, kStages, R>;
+  constexpr int NS = stages_for<D, HG, R>();
+  using L = Layout<D, HG, NS, R>;
+  auto kern = decode_tma_kernel<T, D, HG, NS, R>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc) !=
       cudaSuccess)
     return 1;

@@ -144,7 +144,7 @@ def c1(seed: int = 0) -> Workload:
 
 def c2(seed: int = 0, batch: int = 64) -> Workload:
     rng = np.random.default_rng(seed)
-    bs, nb = 16, 32768
+    bs, nb = 16, max(32768, batch * 256)
     ctx = rng.integers(512, 4097, size=batch).astype(np.int32)
     bt, info = assign_blocks(rng, ctx, bs, nb, max_blocks=4096 // bs)
     return Workload("c2", batch, 28, 4, 128, bs, nb, "bfloat16", 128 ** -0.5, 0.5, ctx, bt,
@@ -153,7 +153,7 @@ def c2(seed: int = 0, batch: int = 64) -> Workload:
 
 def c3(seed: int = 0, batch: int = 256) -> Workload:
     rng = np.random.default_rng(seed)
-    bs, nb = 16, 32768
+    bs, nb = 16, max(32768, batch * 128)
     ctx = rng.integers(128, 2049, size=batch).astype(np.int32)
     bt, info = assign_blocks(rng, ctx, bs, nb, max_blocks=2048 // bs, shared_frac=0.3)
     return Workload("c3", batch, 28, 4, 128, bs, nb, "bfloat16", 128 ** -0.5, 0.5, ctx, bt,
