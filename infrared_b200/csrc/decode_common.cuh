@@ -117,6 +117,52 @@ template <int NT, typename T>
 __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
                            RangeInfo* ri, int64_t* sm_scan) {
   const int tid = threadIdx.x;
+  const bool publish = (g == 0 && kv0 == 0);
+  auto empty_rows = [&](int b) {
+    // empty context: zero rows (and lse = -inf) of this CTA's heads
+    for (int i = 0; i < nkv * a.n_rep * a.D; ++i) {
+      const int h = kv0 * a.n_rep + i / a.D, d = i % a.D;
+      if (a.lse_mode) {
+        a.lse_o[(static_cast<int64_t>(b) * a.H + h) * a.D + d] = 0.f;
+        if (d == 0) a.lse_out[static_cast<int64_t>(b) * a.H + h] = -INFINITY;
+      } else {
+        reinterpret_cast<T*>(a.out)[b * a.out_stride + h * a.D + d] = DT<T>::from_f(0.f);
+      }
+    }
+  };
+  if (tid == 0) ri->b_first = -1;
+  if (a.B <= NT) {
+    // one pass: every thread owns one sequence
+    const int b = tid;
+    int n = 0;
+    if (b < a.B) {
+      const int c = a.context_lens[b];
+      if (c < 0 || c > a.max_blocks * a.bs) set_err(a.err, IR_DEVERR_CONTEXT_LEN);
+      n = tiles_of(a, b);
+    }
+    int64_t total = 0;
+    const int64_t p = block_excl_scan<NT>(n, sm_scan, &total);  // synchronises
+    const int G = shares_used(total, a.G);
+    const int64_t start = g < G ? share_start(g, total, G) : total;
+    const int64_t end = g < G ? share_start(g + 1, total, G) : total;
+    if (b < a.B) {
+      if (publish) a.ws_prefix[b] = p;
+      if (n > 0 && p <= start && start < p + n) {
+        ri->b_first = b;
+        ri->p_first = p;
+      }
+      if (n == 0 && g == 0) empty_rows(b);
+    }
+    if (tid == 0) {
+      ri->total = total;
+      ri->start = start;
+      ri->end = end;
+      ri->G = G;
+      if (publish) a.ws_prefix[a.B] = total;
+    }
+    __syncthreads();
+    return;
+  }
   // pass 1: total tiles (and context validation)
   int64_t mine = 0;
   for (int b = tid; b < a.B; b += NT) {
@@ -129,17 +175,7 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
   const int G = shares_used(total, a.G);
   const int64_t start = g < G ? share_start(g, total, G) : total;
   const int64_t end = g < G ? share_start(g + 1, total, G) : total;
-  if (tid == 0) {
-    ri->total = total;
-    ri->start = start;
-    ri->end = end;
-    ri->b_first = -1;
-    ri->p_first = 0;
-    ri->G = G;
-  }
-  __syncthreads();
   // pass 2: prefix of every sequence; locate `start`
-  const bool publish = (g == 0 && kv0 == 0);
   int64_t running = 0;
   for (int base = 0; base < a.B; base += NT) {
     const int b = base + tid;
@@ -152,23 +188,17 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
         ri->b_first = b;
         ri->p_first = p;
       }
-      if (n == 0 && g == 0) {
-        // empty context: zero rows (and lse = -inf) of this CTA's heads
-        for (int i = 0; i < nkv * a.n_rep * a.D; ++i) {
-          const int h = kv0 * a.n_rep + i / a.D, d = i % a.D;
-          if (a.lse_mode) {
-            a.lse_o[(static_cast<int64_t>(b) * a.H + h) * a.D + d] = 0.f;
-            if (d == 0) a.lse_out[static_cast<int64_t>(b) * a.H + h] = -INFINITY;
-          } else {
-            reinterpret_cast<T*>(a.out)[b * a.out_stride + h * a.D + d] =
-                DT<T>::from_f(0.f);
-          }
-        }
-      }
+      if (n == 0 && g == 0) empty_rows(b);
     }
     running += chunk_total;
   }
-  if (publish && tid == 0) a.ws_prefix[a.B] = total;
+  if (tid == 0) {
+    ri->total = total;
+    ri->start = start;
+    ri->end = end;
+    ri->G = G;
+    if (publish) a.ws_prefix[a.B] = total;
+  }
   __syncthreads();
 }
 

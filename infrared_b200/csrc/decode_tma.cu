@@ -55,13 +55,16 @@ struct Layout {
   static constexpr int kSide = kBox * (kTile / R);        // K (or V) of one tile
   static constexpr int kStage = 2 * kSide;
   static constexpr int off_desc = NS * kStage;
-  static constexpr int off_bar = off_desc + NS * 16;
-  static constexpr int off_misc = off_bar + 2 * NS * 8;
+  static constexpr int off_bar = off_desc + NS * 16;  // full[NS], empty[NS], qfree[2]
+  static constexpr int off_misc = off_bar + (2 * NS + 2) * 8;
   // per consumer warp: [8 heads][D + 4] fp32 output staging + 8 lse values
   static constexpr int kFlushStride = D + 4;  // padding spreads the 4 column lanes over banks
   static constexpr int kFlushFloats = 8 * kFlushStride + 8;
   static constexpr int off_flush = off_misc + 128;
-  static constexpr int kBytes = off_flush + HG * kFlushFloats * 4;
+  // q rows of the current and next segment: [2][HG * 8 heads][D] of T
+  static constexpr int kQBuf = HG * 8 * D * 2;
+  static constexpr int off_q = (off_flush + HG * kFlushFloats * 4 + 127) / 128 * 128;
+  static constexpr int kBytes = off_q + 2 * kQBuf;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
   // byte offset of row `tok` (0..15) of (head, half) inside one side
   static __device__ __forceinline__ int row_off(int head, int half, int tok) {
@@ -71,6 +74,7 @@ struct Layout {
 
 struct TmaParams {
   int one_box;  // 1: one 4-D box per side; 0: one 3-D box per (head, half)
+  int q_bulk;   // 1: the producer stages each segment's q rows in shared memory
 };
 
 template <typename T, int D, int HG, int NS, int R>
@@ -89,6 +93,7 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::off_bar);
   uint64_t* empty = full + NS;
+  uint64_t* qfree = empty + NS;  // [2]: consumers are done reading a q buffer
   RangeInfo* ri = reinterpret_cast<RangeInfo*>(smem + L::off_misc);
   int64_t* sm_scan = reinterpret_cast<int64_t*>(smem + L::off_misc + 64);
   ItemDesc* desc = reinterpret_cast<ItemDesc*>(smem + L::off_desc);
@@ -98,6 +103,8 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], HG);
     }
+    mbar_init(&qfree[0], HG);
+    mbar_init(&qfree[1], HG);
     fence_mbar_init();
   }
   if (threadIdx.x == 32) {
@@ -182,13 +189,37 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
         const int kpk = __shfl_sync(kFull, packed, k);
         const int64_t kr0 = __shfl_sync(kFull, row0, k);
         const int64_t kr1 = __shfl_sync(kFull, row1, k);
+        // a segment's first tile also brings the segment's q rows (buffer
+        // seg & 1), once the consumers have loaded segment seg - 2's q
+        const bool with_q = tp.q_bulk && (kpk & kFlagSegStart);
+        if (with_q && kseg >= 2) {
+          int okq = 1;
+          if (lane == 0)
+            okq = mbar_wait_bounded(&qfree[kseg & 1], ((kseg >> 1) + 1) & 1) ? 1 : 0;
+          if (!__shfl_sync(kFull, okq, 0)) {
+            if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
+            abort = true;
+            break;
+          }
+        }
         if (lane == 0) {
           desc[slot] = ItemDesc{kb, ktok, kseg, kpk};
           uint8_t* kd = smem + slot * L::kStage;
           uint8_t* vd = kd + L::kSide;
-          if (kpk & kFlagValid) {
-            const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
-            mbar_arrive_expect_tx(&full[slot], static_cast<uint32_t>(nbox * 2 * L::kBox));
+          const uint32_t qbytes = with_q ? static_cast<uint32_t>(HG * a.n_rep * D * 2) : 0u;
+          const bool valid = (kpk & kFlagValid) != 0;
+          const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
+          const uint32_t tbytes = valid ? static_cast<uint32_t>(nbox * 2 * L::kBox) : 0u;
+          if (valid || with_q)
+            mbar_arrive_expect_tx(&full[slot], tbytes + qbytes);
+          else
+            mbar_arrive(&full[slot]);  // invalid tile: nothing to wait for
+          if (with_q) {
+            const T* qsrc = reinterpret_cast<const T*>(a.q) + kb * a.q_stride +
+                            static_cast<int64_t>(kv0 * a.n_rep) * D;
+            bulk_load(smem + L::off_q + (kseg & 1) * L::kQBuf, qsrc, qbytes, &full[slot]);
+          }
+          if (valid) {
             for (int bx = 0; bx < nbox; ++bx) {
               const int row = static_cast<int>(bx == 0 ? kr0 : kr1);
               if (tp.one_box) {
@@ -206,8 +237,6 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
                 }
               }
             }
-          } else {
-            mbar_arrive(&full[slot]);
           }
         }
         ++item;
@@ -262,7 +291,7 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   }
   m[0] = m[1] = -INFINITY;
   l[0] = l[1] = 0.f;
-  int cur_b = -1, seg_b = -1;
+  int seg_b = -1;
   bool seg_whole = false, have_seg = false;
 
   float* fbuf = reinterpret_cast<float*>(smem + L::off_flush) + head * L::kFlushFloats;
@@ -352,11 +381,12 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
       have_seg = true;
       seg_b = b;
       seg_whole = (pk & kFlagWhole) != 0;
-    }
-    if (b != cur_b) {
-      cur_b = b;
-      const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_stride +
-                      static_cast<int64_t>(kvh * a.n_rep) * D;
+      // this segment's q as B fragments: from the staged rows, else global
+      const T* qrow = tp.q_bulk
+          ? reinterpret_cast<const T*>(smem + L::off_q + (dsc.seg & 1) * L::kQBuf) +
+                head * a.n_rep * D
+          : reinterpret_cast<const T*>(a.q) + b * a.q_stride +
+                static_cast<int64_t>(kvh * a.n_rep) * D;
 #pragma unroll
       for (int ks = 0; ks < KS; ++ks) {
         if (grp < a.n_rep) {
@@ -365,6 +395,10 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
         } else {
           qf[ks][0] = qf[ks][1] = 0u;
         }
+      }
+      if (tp.q_bulk) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&qfree[dsc.seg & 1]);
       }
     }
     const int nvalid = (pk & kFlagValid) ? (pk & 0xff) : 0;
@@ -481,7 +515,8 @@ template <int D, int HG, int R>
 constexpr int stages_for() {
   constexpr int stage = 2 * HG * (D / 64) * kTile * 128;  // K + V of one tile
   constexpr int flush = HG * (8 * (D + 4) + 8) * 4;
-  constexpr int budget = 227 * 1024 - 1024 - 512 - flush;   // align slack, misc
+  constexpr int qbuf = 2 * HG * 8 * D * 2;
+  constexpr int budget = 227 * 1024 - 1024 - 640 - flush - qbuf;  // align slack, misc
   constexpr int fit = budget / (stage + 48);                // + desc and barriers
   constexpr int n = fit < IRB_TMA_STAGES ? fit : IRB_TMA_STAGES;
   return n < 2 ? 2 : n;
@@ -554,7 +589,11 @@ int tma_head_group(int num_kv_heads) {
 
 int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
                       int dtype, int one_box, cudaStream_t stream) {
-  const TmaParams tp{one_box};
+  // q rows of a head group move as one bulk copy when 16-byte aligned
+  const int64_t grp_elems = static_cast<int64_t>(a.n_rep) * a.D;
+  const bool q_ok = (reinterpret_cast<uintptr_t>(a.q) % 16 == 0) && (a.q_stride * 2) % 16 == 0 &&
+                    (grp_elems * 2) % 16 == 0;
+  const TmaParams tp{one_box, q_ok ? 1 : 0};
   const int HG = tma_head_group(a.Hkv), R = a.bs == 8 ? 8 : 16;
   if (dtype == IR_DTYPE_BF16)
     return by_dim<__nv_bfloat16>(0, a.D, HG, R, &tmk, &tmv, &a, &tp, stream);
