@@ -1,0 +1,98 @@
+"""Install the B200 kernels behind infrared's own paged-attention seam.
+
+infrared's ``Attention.forward`` calls ``paged_attention(q, k, v, paged,
+mask, layer_idx, scale, n_rep)`` (infrared/model/triton_attention.py:81-107),
+which first scatters this step's K/V with ``paged.pool.write`` and then, when
+``_should_use_triton(q, paged.use_triton)`` says so, reads the history with
+``_paged_attention_triton``; otherwise it runs the naive gather path. Both
+names are module globals looked up at call time, and ``PagedKVPool.write``
+is a class attribute (infrared/cache/paged_kv_cache.py:48), so replacing
+those three routes the engine's decode steps — eager
+(infrared/engine/paged_engine.py:290-332) and CUDA-graph
+(infrared/engine/cuda_graph.py:231-287) — to this package without editing
+infrared:
+
+* ``PagedKVPool.write`` on CUDA tensors -> ``ir_cache_write``;
+* ``_should_use_triton`` -> True for CUDA decode calls (``Sq == 1``) with
+  ``head_dim`` 64 or 128 in fp32 / bf16 / fp16 and ``use_triton`` set;
+  prefill and mixed varlen batches (``Sq > 1``) keep infrared's own path;
+* ``_paged_attention_triton`` -> ``ir_derive_block_metadata`` (once per
+  forward) + ``ir_paged_decode``.
+
+The replacement read path trusts the engine's decode metadata: the mask is a
+prefix of zeros and ``gather_slots`` lists whole blocks; a call that breaks
+either is reported by the device error flag (``check_device_errors``).
+"""
+
+from __future__ import annotations
+
+import importlib
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .attention import block_metadata
+
+_SUPPORTED = (torch.float32, torch.bfloat16, torch.float16)
+
+
+def should_use_b200(q: torch.Tensor, want: bool) -> bool:
+    """Gate with the reference's signature (triton_attention.py:68-76)."""
+    return (bool(want) and q.is_cuda and q.dim() == 4 and q.shape[1] == 1
+            and q.shape[-1] in (64, 128) and q.dtype in _SUPPORTED)
+
+
+def paged_attention_b200(q: torch.Tensor, paged, mask: torch.Tensor, layer_idx: int,
+                         scale: float, n_rep: int) -> torch.Tensor:
+    """Read path with the signature of ``_paged_attention_triton``
+    (triton_attention.py:310-318): the pool already holds this step's K/V."""
+    b, sq, h, d = q.shape
+    pool = paged.pool
+    bt, ctx = block_metadata(paged, mask)
+    out = torch.empty((b, sq, h, d), dtype=q.dtype, device=q.device)
+    ops.paged_decode(q.reshape(b, h, d), pool.k[layer_idx], pool.v[layer_idx], bt, ctx,
+                     scale, pool.block_size, out=out.view(b, h, d))
+    return out
+
+
+def _make_write(original):
+    def write(self, layer_idx, k, v, slots):
+        if k.is_cuda and k.dtype in _SUPPORTED and self.k.dtype == k.dtype:
+            ops.cache_write(k, v, self.k[layer_idx], self.v[layer_idx], slots)
+        else:
+            original(self, layer_idx, k, v, slots)
+    write.__doc__ = "PagedKVPool.write on the B200 cache-write kernel (CUDA tensors)."
+    return write
+
+
+@dataclass
+class Installed:
+    """Handle of an installation; ``uninstall()`` restores infrared's functions."""
+
+    triton_attention: object
+    pool_cls: object
+    saved: dict
+
+    def uninstall(self) -> None:
+        self.triton_attention._should_use_triton = self.saved["gate"]
+        self.triton_attention._paged_attention_triton = self.saved["read"]
+        self.pool_cls.write = self.saved["write"]
+
+
+def install(triton_attention=None, paged_kv_cache=None) -> Installed:
+    """Route infrared's paged decode attention to the B200 kernels.
+
+    ``triton_attention`` / ``paged_kv_cache`` default to the installed
+    ``infrared.model.triton_attention`` and ``infrared.cache.paged_kv_cache``
+    modules (any modules with the same names and call contract work).
+    """
+    ta = triton_attention or importlib.import_module("infrared.model.triton_attention")
+    pk = paged_kv_cache or importlib.import_module("infrared.cache.paged_kv_cache")
+    pool_cls = pk.PagedKVPool
+    saved = {"gate": ta._should_use_triton, "read": ta._paged_attention_triton,
+             "write": pool_cls.write}
+    ta._should_use_triton = should_use_b200
+    ta._paged_attention_triton = paged_attention_b200
+    pool_cls.write = _make_write(saved["write"])
+    return Installed(ta, pool_cls, saved)

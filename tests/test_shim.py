@@ -1,0 +1,176 @@
+"""The shim that installs the B200 kernels behind infrared's own seam.
+
+CPU part: with infrared importable (its checkout at INFRARED_REF, default
+/root/reference; skipped elsewhere), installing the shim leaves every CPU
+call on infrared's naive path, bit for bit, and uninstalling restores the
+original functions. GPU part: the same shim installed into a stand-in seam
+with infrared's call contract (a dispatcher that writes through
+``pool.write`` and then asks ``_should_use_triton`` whether to call
+``_paged_attention_triton``), checked against the oracle.
+"""
+
+import os
+import sys
+import types
+
+import numpy as np
+import pytest
+import torch
+
+from infrared_b200 import shim
+from infrared_b200 import workloads as wl
+from oracle import paged_attention_np as orc
+
+REF = os.environ.get("INFRARED_REF", "/root/reference")
+
+
+@pytest.fixture
+def infrared():
+    if not os.path.isdir(os.path.join(REF, "infrared")):
+        pytest.skip("infrared reference checkout not available")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import infrared.cache.paged_kv_cache as pk
+    import infrared.model.triton_attention as ta
+
+    return ta, pk
+
+
+def test_install_uninstall_restores(infrared):
+    ta, pk = infrared
+    before = (ta._should_use_triton, ta._paged_attention_triton, pk.PagedKVPool.write)
+    h = shim.install(ta, pk)
+    assert ta._should_use_triton is shim.should_use_b200
+    assert ta._paged_attention_triton is shim.paged_attention_b200
+    assert pk.PagedKVPool.write is not before[2]
+    h.uninstall()
+    assert (ta._should_use_triton, ta._paged_attention_triton, pk.PagedKVPool.write) == before
+
+
+def test_cpu_calls_stay_on_reference_path(infrared):
+    """With the shim installed, infrared's CPU decode gives its own result."""
+    ta, pk = infrared
+    w = wl.custom(3, 4, 14, 2, 64, 16, 5, 90, "float32")
+    q, kp, vp, kn, vn = wl.numpy_values(w, 2)
+    t = int(w.context_lens.max())
+    gs = torch.from_numpy(orc.gather_slots_from_tables(w.block_tables, w.context_lens, 16, t))
+    mask = torch.from_numpy(orc.decode_mask(w.context_lens, t))
+
+    def run():
+        pool = pk.PagedKVPool(1, w.num_blocks, 16, 2, 64, torch.float32)
+        pool.k[0].copy_(torch.from_numpy(kp))
+        pool.v[0].copy_(torch.from_numpy(vp))
+        ctx = pk.PagedContext(pool, torch.from_numpy(w.slot_mapping), gs, use_triton=True)
+        out = ta.paged_attention(torch.from_numpy(q)[:, None], torch.from_numpy(kn)[:, None],
+                                 torch.from_numpy(vn)[:, None], ctx, mask, 0, w.scale, w.n_rep)
+        return out, pool
+
+    ref_out, ref_pool = run()
+    h = shim.install(ta, pk)
+    try:
+        out, pool = run()
+    finally:
+        h.uninstall()
+    assert torch.equal(out, ref_out)
+    assert torch.equal(pool.k, ref_pool.k) and torch.equal(pool.v, ref_pool.v)
+
+
+def test_gate_rejects_cpu_prefill_and_opt_out():
+    q = torch.zeros(2, 1, 28, 128)
+    assert not shim.should_use_b200(q, True)                          # CPU
+    assert not shim.should_use_b200(torch.zeros(1, 3, 28, 128), True)  # Sq > 1
+
+
+# ---------------------------------------------------------------- GPU, stand-in seam
+
+
+def _stand_in_seam():
+    """Modules with infrared's seam contract (names and call order), written here."""
+    pk = types.ModuleType("stand_in_paged_kv_cache")
+
+    class PagedKVPool:
+        def __init__(self, layers, blocks, bs, hkv, d, dtype, device):
+            self.block_size = bs
+            self.k = torch.zeros(layers, blocks * bs, hkv, d, dtype=dtype, device=device)
+            self.v = torch.zeros_like(self.k)
+
+        def write(self, layer_idx, k, v, slots):
+            self.k[layer_idx, slots] = k
+            self.v[layer_idx, slots] = v
+
+    pk.PagedKVPool = PagedKVPool
+    ta = types.ModuleType("stand_in_triton_attention")
+    calls = {"b200": 0, "naive": 0}
+
+    def _should_use_triton(q, want):
+        return False
+
+    def _paged_attention_triton(q, paged, mask, layer_idx, scale, n_rep):
+        raise AssertionError("not installed")
+
+    def _naive(q, paged, mask, layer_idx, scale, n_rep):
+        calls["naive"] += 1
+        kk = paged.pool.k[layer_idx][paged.gather_slots].float()
+        vv = paged.pool.v[layer_idx][paged.gather_slots].float()
+        kk = kk.repeat_interleave(n_rep, dim=2)
+        vv = vv.repeat_interleave(n_rep, dim=2)
+        s = torch.einsum("bqhd,bkhd->bhqk", q.float(), kk) * scale + mask.float()
+        return torch.einsum("bhqk,bkhd->bqhd", s.softmax(-1), vv).to(q.dtype)
+
+    def paged_attention(q, k, v, paged, mask, layer_idx, scale, n_rep):
+        h, d = k.shape[-2], k.shape[-1]
+        paged.pool.write(layer_idx, k.reshape(-1, h, d), v.reshape(-1, h, d), paged.write_slots)
+        if ta._should_use_triton(q, paged.use_triton):
+            calls["b200"] += 1
+            return ta._paged_attention_triton(q, paged, mask, layer_idx, scale, n_rep)
+        return _naive(q, paged, mask, layer_idx, scale, n_rep)
+
+    ta._should_use_triton = _should_use_triton
+    ta._paged_attention_triton = _paged_attention_triton
+    ta.paged_attention = paged_attention
+    return ta, pk, calls
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_shim_routes_decode_to_b200(dtype):
+    from infrared_b200 import PagedContext, check_device_errors
+
+    ta, pk, calls = _stand_in_seam()
+    h = shim.install(ta, pk)
+    try:
+        w = wl.custom(9, 6, 28, 4, 128, 16, 10, 400, "float32", shared_frac=0.3)
+        q, kp, vp, kn, vn = [torch.from_numpy(x).cuda().to(dtype) for x in wl.numpy_values(w, 4)]
+        pool = pk.PagedKVPool(2, w.num_blocks, 16, 4, 128, dtype, "cuda")
+        pool.k[1].copy_(kp)
+        pool.v[1].copy_(vp)
+        t = int(w.context_lens.max())
+        gs = torch.from_numpy(orc.gather_slots_from_tables(w.block_tables, w.context_lens, 16,
+                                                           t)).cuda()
+        mask = torch.from_numpy(orc.decode_mask(w.context_lens, t)).cuda().to(dtype)
+        ctx = PagedContext(pool, torch.from_numpy(w.slot_mapping).cuda(), gs, use_triton=True)
+        out = ta.paged_attention(q[:, None], kn[:, None], vn[:, None], ctx, mask, 1, w.scale,
+                                 w.n_rep)
+        assert calls["b200"] == 1 and calls["naive"] == 0
+        assert torch.equal(pool.k[1][ctx.write_slots], kn)   # written by ir_cache_write
+        host = [x.float().cpu().numpy() for x in (q, kp, vp, kn, vn)]
+        kp2, vp2 = host[1][None].copy(), host[2][None].copy()
+        orc.pool_write(kp2, vp2, 0, host[3], host[4], w.slot_mapping)
+        want = orc.decode_from_tables(host[0], kp2, vp2, 0, w.block_tables, w.context_lens, 16,
+                                      w.scale, w.n_rep)
+        tol = 1e-5 if dtype == torch.float32 else 2e-2
+        np.testing.assert_allclose(out[:, 0].float().cpu().numpy(), want, atol=tol,
+                                   rtol=0 if dtype == torch.float32 else tol)
+        # a prefill call (Sq = 2) stays on the seam's own path
+        q2 = q[:1, None].expand(-1, 2, -1, -1).contiguous()
+        k2 = kn[:1, None].expand(-1, 2, -1, -1).contiguous()
+        slots2 = torch.tensor([0, 1], device="cuda")
+        mask2 = torch.zeros(1, 1, 2, 2, device="cuda", dtype=dtype)
+        mask2[0, 0, 0, 1] = torch.finfo(dtype).min
+        ta.paged_attention(q2, k2, k2, PagedContext(pool, slots2, slots2[None], use_triton=True),
+                           mask2, 1, w.scale, w.n_rep)
+        assert calls["b200"] == 1 and calls["naive"] == 1
+        check_device_errors()
+    finally:
+        h.uninstall()
