@@ -203,6 +203,39 @@ int ir_paged_decode_lse(float* o, float* lse, const void* q,
                         size_t workspace_bytes, int32_t* err_flag,
                         ir_stream_t stream);
 
+/* Largest workspace ir_paged_decode_noalloc can serve (bytes). */
+#define IR_NOALLOC_WORKSPACE_BYTES (8u << 20)
+
+/*
+ * ir_paged_decode for callers that cannot allocate device memory. No
+ * counterpart in the reference (its path allocates through PyTorch).
+ *
+ * Some hosts own every device byte themselves and forbid allocation calls on
+ * their serving path: an engine that hands out a fixed memory budget at
+ * start-up, a plugin loaded into another runtime's process, or a foreign-
+ * language binding with no access to a device allocator. They cannot supply
+ * the workspace ir_paged_decode asks for. This entry point takes the same
+ * inputs and outputs but keeps its scratch (partial results of sequences
+ * split across SMs) in an 8 MiB array that is part of the library itself
+ * (IR_NOALLOC_WORKSPACE_BYTES; every GPU that loads the library holds it
+ * until the process exits). It calls no cudaMalloc or cudaFree.
+ *
+ * - The first call on a device looks up the array's device address with
+ *   that device current (this may load the library's GPU code), so make that
+ *   first call before capturing a CUDA graph.
+ * - Shapes whose scratch (ir_paged_decode_workspace_size) exceeds
+ *   IR_NOALLOC_WORKSPACE_BYTES are rejected with IR_ERR_WORKSPACE.
+ * - All calls on a device share the one array and it keeps whatever the
+ *   last call left in it; nothing in it needs to start at zero. Calls that
+ *   may run at the same time on the GPU (different streams without ordering
+ *   between them) race on it and give wrong results: order them.
+ */
+int ir_paged_decode_noalloc(void* out, const void* q, const void* k_pool,
+                            const void* v_pool, const int32_t* block_tables,
+                            const int32_t* context_lens,
+                            const ir_decode_shape* shape, int32_t* err_flag,
+                            ir_stream_t stream);
+
 /*
  * Combine P partials: out[b, h, :] = sum_p w_p o_parts[p, b, h, :] with
  * w_p = exp(lse_parts[p, b, h] - LSE), LSE = log sum_p exp(lse_parts[p]).

@@ -21,6 +21,7 @@ LIB_PATH = Path(os.environ.get("INFRARED_B200_LIB") or
 
 IR_DTYPE_F32, IR_DTYPE_BF16, IR_DTYPE_F16 = 0, 1, 2
 IR_OK, IR_ERR_INVALID_ARG, IR_ERR_UNSUPPORTED, IR_ERR_CUDA, IR_ERR_WORKSPACE = range(5)
+IR_NOALLOC_WORKSPACE_BYTES = 8 << 20
 
 DEVERR_BITS = {
     0x1: "BLOCK_ID",
@@ -92,6 +93,9 @@ _SIGNATURES = {
                                     c_size_t, c_void_p, c_void_p]),
     "ir_lse_merge": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int, c_int,
                              c_int, c_int, c_void_p]),
+    "ir_paged_decode_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, POINTER(DecodeShape), c_void_p,
+                                        c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -346,6 +346,35 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
   return cuda_status(e, "merge kernel launch");
 }
 
+// Scratch of ir_paged_decode_noalloc: part of the library image, so the
+// entry point allocates nothing. Host code must not pass the symbol itself
+// to a kernel (on the host it names a host-side shadow, not device memory);
+// it passes the device address found with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_ws[IR_NOALLOC_WORKSPACE_BYTES];
+
+std::mutex g_noalloc_mu;
+std::map<int, void*> g_noalloc_ptr;  // device -> address of g_noalloc_ws
+
+// Device address of g_noalloc_ws on the current device (looked up once per
+// device, with that device current).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(static_cast<int>(e), "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  auto it = g_noalloc_ptr.find(dev);
+  if (it == g_noalloc_ptr.end()) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_ws);
+    if (e != cudaSuccess || p == nullptr)
+      return cuda_status(e != cudaSuccess ? static_cast<int>(e) : 1,
+                         "cudaGetSymbolAddress(no-alloc scratch)");
+    it = g_noalloc_ptr.emplace(dev, p).first;
+  }
+  *out = it->second;
+  return IR_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -485,6 +514,28 @@ int ir_paged_decode_lse(float* o, float* lse, const void* q,
   return decode_impl(Mode::kLse, nullptr, o, lse, q, k_pool, v_pool, nullptr,
                      nullptr, 0, nullptr, block_tables, context_lens, shape,
                      workspace, workspace_bytes, err_flag, stream);
+}
+
+int ir_paged_decode_noalloc(void* out, const void* q, const void* k_pool,
+                            const void* v_pool, const int32_t* block_tables,
+                            const int32_t* context_lens,
+                            const ir_decode_shape* shape, int32_t* err_flag,
+                            ir_stream_t stream) {
+  Plan plan;
+  int rc = make_plan(shape, &plan);
+  if (rc) return rc;
+  if (plan.bytes > IR_NOALLOC_WORKSPACE_BYTES)
+    return fail(IR_ERR_WORKSPACE,
+                "shape needs " + std::to_string(plan.bytes) +
+                    " bytes of scratch; ir_paged_decode_noalloc holds at most " +
+                    std::to_string(IR_NOALLOC_WORKSPACE_BYTES) +
+                    " (use ir_paged_decode with a caller workspace)");
+  void* ws = nullptr;
+  rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  return decode_impl(Mode::kFinal, out, nullptr, nullptr, q, k_pool, v_pool,
+                     nullptr, nullptr, 0, nullptr, block_tables, context_lens,
+                     shape, ws, IR_NOALLOC_WORKSPACE_BYTES, err_flag, stream);
 }
 
 int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
