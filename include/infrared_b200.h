@@ -239,12 +239,17 @@ int ir_paged_decode_noalloc(void* out, const void* q, const void* k_pool,
 /*
  * Combine P partials: out[b, h, :] = sum_p w_p o_parts[p, b, h, :] with
  * w_p = exp(lse_parts[p, b, h] - LSE), LSE = log sum_p exp(lse_parts[p]).
- * o_parts [P, B, H, D] fp32, lse_parts [P, B, H] fp32 contiguous; out is
- * [B, H, D] of `dtype` with sequence stride out_stride. Rows whose partials
- * are all -inf become zero. No reference counterpart (see above).
+ * Part p of o_parts starts at o_parts + p * o_part_stride and is [B, H, D]
+ * fp32 contiguous; part p of lse_parts starts at lse_parts + p *
+ * lse_part_stride and is [B, H] (strides in elements: B*H*D and B*H for
+ * stacked arrays, or the packed row of an all-gather). out is [B, H, D] of
+ * `dtype` with sequence stride out_stride. Rows whose partials are all -inf
+ * become zero. No reference counterpart (the reference defers split-KV,
+ * infrared docs/research/t4-triton-cudagraph-api.md:130).
  */
 int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
-                 const float* lse_parts, int num_parts, int batch,
+                 int64_t o_part_stride, const float* lse_parts,
+                 int64_t lse_part_stride, int num_parts, int batch,
                  int num_heads, int head_dim, int dtype, ir_stream_t stream);
 
 #ifdef __cplusplus

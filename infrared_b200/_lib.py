@@ -91,8 +91,8 @@ _SIGNATURES = {
     "ir_paged_decode_lse": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, POINTER(DecodeShape), c_void_p,
                                     c_size_t, c_void_p, c_void_p]),
-    "ir_lse_merge": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int, c_int,
-                             c_int, c_int, c_void_p]),
+    "ir_lse_merge": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int,
+                             c_int, c_int, c_int, c_int, c_void_p]),
     "ir_paged_decode_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, POINTER(DecodeShape), c_void_p,
                                         c_void_p]),

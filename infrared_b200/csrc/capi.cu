@@ -539,19 +539,24 @@ int ir_paged_decode_noalloc(void* out, const void* q, const void* k_pool,
 }
 
 int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
-                 const float* lse_parts, int num_parts, int batch,
+                 int64_t o_part_stride, const float* lse_parts,
+                 int64_t lse_part_stride, int num_parts, int batch,
                  int num_heads, int head_dim, int dtype, ir_stream_t stream) {
   if (elem_bytes(dtype) == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
   if (num_parts <= 0 || batch < 0 || num_heads <= 0 || head_dim <= 0)
     return fail(IR_ERR_INVALID_ARG, "bad sizes");
   if (batch == 0) return IR_OK;
+  const int64_t rows = static_cast<int64_t>(batch) * num_heads;
   if (out_stride < static_cast<int64_t>(num_heads) * head_dim)
     return fail(IR_ERR_INVALID_ARG, "out_stride < H*D");
+  if (num_parts > 1 && (o_part_stride < rows * head_dim || lse_part_stride < rows))
+    return fail(IR_ERR_INVALID_ARG, "part strides smaller than one part");
   if (!out || !o_parts || !lse_parts) return fail(IR_ERR_INVALID_ARG, "null pointer");
   if (batch > 2147483647 || num_heads > 65535)
     return fail(IR_ERR_UNSUPPORTED, "grid too large");
-  int e = irb::launch_lse_merge(out, out_stride, o_parts, lse_parts, num_parts,
-                                batch, num_heads, head_dim, dtype, stream);
+  int e = irb::launch_lse_merge(out, out_stride, o_parts, o_part_stride, lse_parts,
+                                lse_part_stride, num_parts, batch, num_heads, head_dim,
+                                dtype, stream);
   return cuda_status(e, "lse merge launch");
 }
 

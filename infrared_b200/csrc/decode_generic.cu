@@ -244,24 +244,23 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
 }
 
 template <typename T>
-__global__ void lse_merge_kernel(T* out, int64_t out_stride,
-                                 const float* o_parts, const float* lse_parts,
-                                 int P, int B, int H, int D) {
+__global__ void lse_merge_kernel(T* out, int64_t out_stride, const float* o_parts,
+                                 int64_t o_part_stride, const float* lse_parts,
+                                 int64_t lse_part_stride, int P, int B, int H, int D) {
   const int b = blockIdx.x, h = blockIdx.y;
   const int64_t row = static_cast<int64_t>(b) * H + h;
-  const int64_t pstride = static_cast<int64_t>(B) * H;
   float M = -INFINITY;
-  for (int p = 0; p < P; ++p) M = fmaxf(M, lse_parts[p * pstride + row]);
+  for (int p = 0; p < P; ++p) M = fmaxf(M, lse_parts[p * lse_part_stride + row]);
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float val = 0.f;
     if (M != -INFINITY) {
       float lsum = 0.f, osum = 0.f;
       for (int p = 0; p < P; ++p) {
-        const float lp = lse_parts[p * pstride + row];
+        const float lp = lse_parts[p * lse_part_stride + row];
         if (lp == -INFINITY) continue;
         const float w = ex2((lp - M) * kLog2e);
         lsum += w;
-        osum += w * o_parts[(p * pstride + row) * D + d];
+        osum += w * o_parts[p * o_part_stride + row * D + d];
       }
       val = osum / lsum;
     }
@@ -327,22 +326,26 @@ int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
 }
 
 int launch_lse_merge(void* out, int64_t out_stride, const float* o_parts,
-                     const float* lse_parts, int P, int B, int H, int D,
+                     int64_t o_part_stride, const float* lse_parts,
+                     int64_t lse_part_stride, int P, int B, int H, int D,
                      int dtype, cudaStream_t s) {
   dim3 grid(B, H);
   const int threads = D >= 128 ? 128 : 64;
   switch (dtype) {
     case IR_DTYPE_F32:
       lse_merge_kernel<float><<<grid, threads, 0, s>>>(
-          static_cast<float*>(out), out_stride, o_parts, lse_parts, P, B, H, D);
+          static_cast<float*>(out), out_stride, o_parts, o_part_stride, lse_parts,
+          lse_part_stride, P, B, H, D);
       break;
     case IR_DTYPE_BF16:
       lse_merge_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
-          static_cast<__nv_bfloat16*>(out), out_stride, o_parts, lse_parts, P, B, H, D);
+          static_cast<__nv_bfloat16*>(out), out_stride, o_parts, o_part_stride, lse_parts,
+          lse_part_stride, P, B, H, D);
       break;
     default:
       lse_merge_kernel<__half><<<grid, threads, 0, s>>>(
-          static_cast<__half*>(out), out_stride, o_parts, lse_parts, P, B, H, D);
+          static_cast<__half*>(out), out_stride, o_parts, o_part_stride, lse_parts,
+          lse_part_stride, P, B, H, D);
       break;
   }
   return static_cast<int>(cudaGetLastError());

@@ -28,7 +28,8 @@ int decode_generic_occupancy(int dtype, int D);
 // KV ranges computed elsewhere (e.g. other GPUs)
 int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t stream);
 int launch_lse_merge(void* out, int64_t out_stride, const float* o_parts,
-                     const float* lse_parts, int P, int B, int H, int D,
+                     int64_t o_part_stride, const float* lse_parts,
+                     int64_t lse_part_stride, int P, int B, int H, int D,
                      int dtype, cudaStream_t stream);
 
 // cache_ops.cu

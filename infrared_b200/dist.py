@@ -98,9 +98,9 @@ def chunked_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     gathered = torch.empty(world * packed.numel(), dtype=torch.float32, device=q.device)
     dist.all_gather_into_tensor(gathered, packed, group=group)
     gathered = gathered.view(world, packed.numel())
-    o_parts = gathered[:, : b * h * d].reshape(world, b, h, d)
-    lse_parts = gathered[:, b * h * d:].reshape(world, b, h)
-    return merge_fn(o_parts.contiguous(), lse_parts.contiguous(), out_dtype or q.dtype)
+    o_parts = gathered[:, : b * h * d].unflatten(1, (b, h, d))   # views, no copy
+    lse_parts = gathered[:, b * h * d:].unflatten(1, (b, h))
+    return merge_fn(o_parts, lse_parts, out_dtype or q.dtype)
 
 
 def max_over_ranks(value: float, device=None, group=None) -> float:

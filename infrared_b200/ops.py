@@ -356,19 +356,24 @@ def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor
 def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor,
               dtype: torch.dtype = torch.float32,
               out: torch.Tensor | None = None) -> torch.Tensor:
-    """Combine ``o_parts [P, B, H, D]`` / ``lse_parts [P, B, H]`` (fp32) -> ``[B, H, D]``."""
+    """Combine ``o_parts [P, B, H, D]`` / ``lse_parts [P, B, H]`` (fp32) -> ``[B, H, D]``.
+
+    Each part must be contiguous; the parts may sit at any stride (e.g. the
+    rows of a packed all-gather buffer)."""
     dev = _dev_index(o_parts)
     if o_parts.dim() != 4 or lse_parts.shape != o_parts.shape[:3]:
         raise ValueError("o_parts must be [P, B, H, D] and lse_parts [P, B, H]")
     if o_parts.dtype != torch.float32 or lse_parts.dtype != torch.float32:
         raise ValueError("partials must be fp32")
-    o_parts, lse_parts = o_parts.contiguous(), lse_parts.contiguous()
     p, b, h, d = o_parts.shape
+    if not (o_parts[0].is_contiguous() and lse_parts[0].is_contiguous()):
+        o_parts, lse_parts = o_parts.contiguous(), lse_parts.contiguous()
     if out is None:
         out = torch.empty((b, h, d), dtype=dtype, device=o_parts.device)
     if out.stride(2) != 1 or out.stride(1) != d:
         raise ValueError("out rows must be [H, D] contiguous")
     check(_lib.load().ir_lse_merge(
-        out.data_ptr(), out.stride(0), o_parts.data_ptr(), lse_parts.data_ptr(), p, b, h, d,
-        dtype_code(out.dtype), _stream(dev)))
+        out.data_ptr(), out.stride(0), o_parts.data_ptr(), o_parts.stride(0),
+        lse_parts.data_ptr(), lse_parts.stride(0), p, b, h, d, dtype_code(out.dtype),
+        _stream(dev)))
     return out

@@ -51,7 +51,7 @@ def test_argument_errors_need_no_gpu():
     assert rc == _lib.IR_ERR_INVALID_ARG and b"dtype" in lib.ir_last_error()
     rc = lib.ir_cache_write(None, None, 0, 0, None, None, None, 4, 2, 64, 16, 1, None, None)
     assert rc == _lib.IR_ERR_INVALID_ARG
-    rc = lib.ir_lse_merge(None, 0, None, None, 0, 1, 1, 64, 1, None)
+    rc = lib.ir_lse_merge(None, 0, None, 0, None, 0, 0, 1, 1, 64, 1, None)
     assert rc == _lib.IR_ERR_INVALID_ARG
     assert lib.ir_set_decode_path(5) == _lib.IR_ERR_INVALID_ARG
     rc = lib.ir_derive_block_metadata(None, 0, None, 0, 9, 1, 4, 16, None, 0, None, None, None)

@@ -167,6 +167,13 @@ def test_c4_long_context_and_kv_chunk_merge():
         merged = irb.lse_merge(torch.stack(os_), torch.stack(ls_), torch.bfloat16)
         assert_close_bf16(host_f32(merged), want)
         assert np.abs(host_f32(merged) - host_f32(full)).max() < 2e-2
+        # the packed layout of an all-gather ([P, B*H*D + B*H]) merges in place
+        n_o = os_[0].numel()
+        packed = torch.cat([torch.cat([o.reshape(-1), l.reshape(-1)])[None]
+                            for o, l in zip(os_, ls_)])
+        o_view = packed[:, :n_o].unflatten(1, os_[0].shape)
+        l_view = packed[:, n_o:].unflatten(1, ls_[0].shape)
+        assert torch.equal(irb.lse_merge(o_view, l_view, torch.bfloat16), merged)
 
 
 def test_lse_outputs_match_oracle_partials():
