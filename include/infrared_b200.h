@@ -91,6 +91,27 @@ int ir_cache_gather(void* out, const void* pool, const int64_t* slots,
                     ir_stream_t stream);
 
 /*
+ * Fixed-shape inputs of a CUDA-graph decode step, built on the device.
+ * Replaces the per-element Python loops of build_decode_static_inputs
+ * (infrared/engine/cuda_graph.py:105-155) with the same outputs, bit for bit:
+ * for row i < bucket, sequence j = (i < batch ? i : 0) (pad rows repeat
+ * row 0), with ctx = num_cached[j] + 1 and slot(p) =
+ * block_tables[j, p / block_size] * block_size + p % block_size:
+ *   ids[i] = last_tokens[j]; positions[i] = num_cached[j];
+ *   write_slots[i] = slot(num_cached[j]);
+ *   gather_slots[i, p] = p < ctx ? slot(p) : 0                  (int64 [bucket, t_max])
+ *   mask[i, 0, 0, p]  = p < ctx ? 0 : finfo(mask_dtype).min      ([bucket, 1, 1, t_max])
+ * block_tables is int32 [batch, >= ceil(t_max / block_size)] with row stride
+ * bt_stride; the caller guarantees ctx <= t_max (the reference raises).
+ */
+int ir_build_decode_inputs(const int32_t* block_tables, int64_t bt_stride,
+                           const int32_t* num_cached, const int64_t* last_tokens,
+                           int batch, int bucket, int64_t t_max, int block_size,
+                           int64_t* ids, int64_t* positions, int64_t* write_slots,
+                           int64_t* gather_slots, void* mask, int mask_dtype,
+                           ir_stream_t stream);
+
+/*
  * Turn the reference seam's per-forward metadata into block form.
  * gather_slots [B, T] int64 (row stride gs_stride) and the additive decode
  * mask [B, 1, 1, T] (row stride mask_stride, dtype mask_dtype) as built by
@@ -149,6 +170,13 @@ int ir_paged_decode_plan(const ir_decode_shape* shape, int* path,
  * not eligible then fail with IR_ERR_UNSUPPORTED), 3 = the TMA kernel with
  * one tensor copy per (kv head, 64-column half) instead of one per tile. */
 int ir_set_decode_path(int path);
+
+/* Test hook of the failure path (no reference counterpart): the next launch
+ * of the TMA decode kernel makes its first CTA wait for 16 bytes that no copy
+ * delivers. Its bounded waits run out after about two seconds, the kernel
+ * sets IR_DEVERR_TIMEOUT and returns (that call's output is undefined); the
+ * context stays usable. Nothing faults, traps or hangs. */
+int ir_debug_stall_next_decode(void);
 
 /*
  * Decode attention of one query token per sequence over its paged history:

@@ -71,6 +71,7 @@ _SIGNATURES = {
     "ir_last_error": (c_char_p, []),
     "ir_deverr_name": (c_char_p, [c_int]),
     "ir_set_decode_path": (c_int, [c_int]),
+    "ir_debug_stall_next_decode": (c_int, []),
     "ir_paged_decode_plan": (c_int, [POINTER(DecodeShape), POINTER(c_int), POINTER(c_int)]),
     "ir_paged_decode_workspace_size": (c_size_t, [POINTER(DecodeShape)]),
     "ir_cache_write": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
@@ -78,6 +79,9 @@ _SIGNATURES = {
                                c_void_p, c_void_p]),
     "ir_cache_gather": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
                                 c_int64, c_int, c_void_p, c_void_p]),
+    "ir_build_decode_inputs": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int,
+                                       c_int64, c_int, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_void_p, c_int, c_void_p]),
     "ir_derive_block_metadata": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int,
                                          c_int, c_int64, c_int, c_void_p, c_int64,
                                          c_void_p, c_void_p, c_void_p]),

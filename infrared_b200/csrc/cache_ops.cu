@@ -119,6 +119,38 @@ __global__ void derive_metadata_kernel(const int64_t* __restrict__ gs,
   if (bad) set_err(err, IR_DEVERR_NOT_BLOCKED);
 }
 
+// Fixed-shape decode inputs for a CUDA-graph bucket, one row per block.x:
+// row i describes sequence j = (i < batch ? i : 0) (pad rows repeat row 0).
+__global__ void build_decode_inputs_kernel(const int32_t* __restrict__ bt, int64_t bt_stride,
+                                           const int32_t* __restrict__ num_cached,
+                                           const int64_t* __restrict__ last_tokens,
+                                           int batch, int64_t t_max, int bs,
+                                           int64_t* __restrict__ ids,
+                                           int64_t* __restrict__ positions,
+                                           int64_t* __restrict__ write_slots,
+                                           int64_t* __restrict__ gather_slots, void* mask,
+                                           int mask_bytes, uint32_t min_bits) {
+  const int i = blockIdx.x;
+  const int j = i < batch ? i : 0;
+  const int32_t* row = bt + j * bt_stride;
+  const int64_t nc = num_cached[j];
+  const int64_t ctx = nc + 1;
+  const int64_t t = static_cast<int64_t>(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (t == 0) {
+    ids[i] = last_tokens[j];
+    positions[i] = nc;
+    write_slots[i] = static_cast<int64_t>(row[nc / bs]) * bs + nc % bs;
+  }
+  if (t >= t_max) return;
+  const bool valid = t < ctx;
+  gather_slots[i * t_max + t] = valid ? static_cast<int64_t>(row[t / bs]) * bs + t % bs : 0;
+  if (mask_bytes == 4)
+    reinterpret_cast<uint32_t*>(mask)[i * t_max + t] = valid ? 0u : min_bits;
+  else
+    reinterpret_cast<uint16_t*>(mask)[i * t_max + t] =
+        static_cast<uint16_t>(valid ? 0u : min_bits);
+}
+
 int grid_for(int64_t work, int threads) {
   return static_cast<int>((work + threads - 1) / threads);
 }
@@ -182,6 +214,21 @@ int launch_cache_gather(void* out, const void* pool, const int64_t* slots,
         static_cast<uint16_t*>(out), static_cast<const uint16_t*>(pool), slots, n,
         row_elems, num_slots, err);
   }
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_build_decode_inputs(const int32_t* bt, int64_t bt_stride,
+                               const int32_t* num_cached, const int64_t* last_tokens,
+                               int batch, int bucket, int64_t t_max, int bs, int64_t* ids,
+                               int64_t* positions, int64_t* write_slots,
+                               int64_t* gather_slots, void* mask, int mask_bytes,
+                               uint32_t min_bits, cudaStream_t stream) {
+  if (bucket == 0) return 0;
+  dim3 grid(bucket, static_cast<unsigned>((t_max + 255) / 256));
+  build_decode_inputs_kernel<<<grid, 256, 0, stream>>>(bt, bt_stride, num_cached, last_tokens,
+                                                       batch, t_max, bs, ids, positions,
+                                                       write_slots, gather_slots, mask,
+                                                       mask_bytes, min_bits);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -47,6 +47,7 @@ std::mutex g_mu;
 std::map<std::pair<int, int>, int> g_cache;  // (device, key) -> value
 int g_forced_path = 0;
 int g_one_box = 1;
+int g_stall_next = 0;  // test hook: the next TMA decode launch times out on purpose
 
 int cached(int key, int (*compute)(int), int arg, int* out) {
   int dev = 0;
@@ -337,7 +338,13 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
           make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads, s->head_dim,
                         s->dtype, rows)))
       return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-    e = irb::launch_decode_tma(tmk, tmv, a, s->dtype, one_box, stream);
+    int stall = 0;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      stall = g_stall_next;
+      g_stall_next = 0;
+    }
+    e = irb::launch_decode_tma(tmk, tmv, a, s->dtype, one_box, stall, stream);
   } else {
     e = irb::launch_decode_generic(a, s->dtype, stream);
   }
@@ -399,6 +406,12 @@ int ir_set_decode_path(int path) {
   return IR_OK;
 }
 
+int ir_debug_stall_next_decode(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_stall_next = 1;
+  return IR_OK;
+}
+
 int ir_paged_decode_plan(const ir_decode_shape* shape, int* path,
                          int* ctas_per_kv_head) {
   Plan p;
@@ -454,6 +467,34 @@ int ir_cache_gather(void* out, const void* pool, const int64_t* slots,
                                    static_cast<int>(row), num_slots, eb,
                                    err_flag, stream);
   return cuda_status(e, "cache gather launch");
+}
+
+int ir_build_decode_inputs(const int32_t* block_tables, int64_t bt_stride,
+                           const int32_t* num_cached, const int64_t* last_tokens,
+                           int batch, int bucket, int64_t t_max, int block_size,
+                           int64_t* ids, int64_t* positions, int64_t* write_slots,
+                           int64_t* gather_slots, void* mask, int mask_dtype,
+                           ir_stream_t stream) {
+  const int eb = elem_bytes(mask_dtype);
+  if (eb == 0) return fail(IR_ERR_INVALID_ARG, "bad mask dtype");
+  if (batch <= 0 || batch > bucket)
+    return fail(IR_ERR_INVALID_ARG, "need 0 < batch <= bucket");
+  if (t_max <= 0 || block_size <= 0 || bt_stride <= 0)
+    return fail(IR_ERR_INVALID_ARG, "bad sizes");
+  if (bucket > 2147483647 || (t_max + 255) / 256 > 65535)
+    return fail(IR_ERR_UNSUPPORTED, "grid too large");
+  if (!block_tables || !num_cached || !last_tokens || !ids || !positions || !write_slots ||
+      !gather_slots || !mask)
+    return fail(IR_ERR_INVALID_ARG, "null pointer");
+  // finfo(dtype).min bit patterns: fp32 -3.4028235e38, bf16 -3.3895e38, fp16 -65504
+  const uint32_t min_bits = mask_dtype == IR_DTYPE_F32    ? 0xff7fffffu
+                            : mask_dtype == IR_DTYPE_BF16 ? 0xff7fu
+                                                          : 0xfbffu;
+  int e = irb::launch_build_decode_inputs(block_tables, bt_stride, num_cached, last_tokens,
+                                          batch, bucket, t_max, block_size, ids, positions,
+                                          write_slots, gather_slots, mask, eb, min_bits,
+                                          stream);
+  return cuda_status(e, "decode-inputs launch");
 }
 
 int ir_derive_block_metadata(const int64_t* gather_slots, int64_t gs_stride,

@@ -75,6 +75,7 @@ struct Layout {
 struct TmaParams {
   int one_box;  // 1: one 4-D box per side; 0: one 3-D box per (head, half)
   int q_bulk;   // 1: the producer stages each segment's q rows in shared memory
+  int stall;    // test hook: CTA (0, 0) expects bytes that never come (wait runs out)
 };
 
 template <typename T, int D, int HG, int NS, int R>
@@ -210,8 +211,9 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
           const bool valid = (kpk & kFlagValid) != 0;
           const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
           const uint32_t tbytes = valid ? static_cast<uint32_t>(nbox * 2 * L::kBox) : 0u;
+          const uint32_t never = (tp.stall && item == 0 && g == 0 && hg == 0) ? 16u : 0u;
           if (valid || with_q)
-            mbar_arrive_expect_tx(&full[slot], tbytes + qbytes);
+            mbar_arrive_expect_tx(&full[slot], tbytes + qbytes + never);
           else
             mbar_arrive(&full[slot]);  // invalid tile: nothing to wait for
           if (with_q) {
@@ -588,12 +590,12 @@ int tma_head_group(int num_kv_heads) {
 }
 
 int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a,
-                      int dtype, int one_box, cudaStream_t stream) {
+                      int dtype, int one_box, int stall, cudaStream_t stream) {
   // q rows of a head group move as one bulk copy when 16-byte aligned
   const int64_t grp_elems = static_cast<int64_t>(a.n_rep) * a.D;
   const bool q_ok = (reinterpret_cast<uintptr_t>(a.q) % 16 == 0) && (a.q_stride * 2) % 16 == 0 &&
                     (grp_elems * 2) % 16 == 0;
-  const TmaParams tp{one_box, q_ok ? 1 : 0};
+  const TmaParams tp{one_box, q_ok ? 1 : 0, stall};
   const int HG = tma_head_group(a.Hkv), R = a.bs == 8 ? 8 : 16;
   if (dtype == IR_DTYPE_BF16)
     return by_dim<__nv_bfloat16>(0, a.D, HG, R, &tmk, &tmv, &a, &tp, stream);

@@ -15,7 +15,7 @@ struct DecodeArgs;
 // (one copy per tile side) or the 3-D (one copy per head and half) map.
 int tma_head_group(int num_kv_heads);
 int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv,
-                      const DecodeArgs& a, int dtype, int one_box,
+                      const DecodeArgs& a, int dtype, int one_box, int stall,
                       cudaStream_t stream);
 int decode_tma_occupancy(int dtype, int D, int Hkv, int bs);
 
@@ -41,6 +41,12 @@ int launch_cache_write(const void* k, const void* v, int64_t k_stride,
 int launch_cache_gather(void* out, const void* pool, const int64_t* slots,
                         int64_t n, int row_elems, int64_t num_slots,
                         int elem_bytes, int32_t* err, cudaStream_t stream);
+int launch_build_decode_inputs(const int32_t* bt, int64_t bt_stride,
+                               const int32_t* num_cached, const int64_t* last_tokens,
+                               int batch, int bucket, int64_t t_max, int bs, int64_t* ids,
+                               int64_t* positions, int64_t* write_slots,
+                               int64_t* gather_slots, void* mask, int mask_bytes,
+                               uint32_t min_bits, cudaStream_t stream);
 int launch_derive_metadata(const int64_t* gs, int64_t gs_stride,
                            const void* mask, int64_t mask_stride,
                            int mask_elem_bytes, int B, int64_t T, int bs,

@@ -17,7 +17,11 @@ infrared:
   ``head_dim`` 64 or 128 in fp32 / bf16 / fp16 and ``use_triton`` set;
   prefill and mixed varlen batches (``Sq > 1``) keep infrared's own path;
 * ``_paged_attention_triton`` -> ``ir_derive_block_metadata`` (once per
-  forward) + ``ir_paged_decode``.
+  forward) + ``ir_paged_decode``;
+* (optional, ``graph_inputs=True``) ``cuda_graph.build_decode_static_inputs``
+  (infrared/engine/cuda_graph.py:105-155, a module global read by
+  ``CudaGraphDecoder.decode`` at :211) -> ``ir_build_decode_inputs`` for CUDA
+  devices, which removes the per-element Python loop of every graph step.
 
 The replacement read path trusts the engine's decode metadata: the mask is a
 prefix of zeros and ``gather_slots`` lists whole blocks; a call that breaks
@@ -66,6 +70,20 @@ def _make_write(original):
     return write
 
 
+def _make_graph_inputs(original, decode_inputs_cls):
+    from .graph_inputs import build_decode_static_inputs as on_device
+
+    def build(block_tables, num_cached, last_tokens, bucket_b, t_max, block_size, device,
+              dtype):
+        if torch.device(device).type == "cuda":
+            return on_device(block_tables, num_cached, last_tokens, bucket_b, t_max,
+                             block_size, device, dtype, decode_inputs_cls)
+        return original(block_tables, num_cached, last_tokens, bucket_b, t_max, block_size,
+                        device, dtype)
+    build.__doc__ = "build_decode_static_inputs on the device (ir_build_decode_inputs)."
+    return build
+
+
 @dataclass
 class Installed:
     """Handle of an installation; ``uninstall()`` restores infrared's functions."""
@@ -73,26 +91,39 @@ class Installed:
     triton_attention: object
     pool_cls: object
     saved: dict
+    cuda_graph: object = None
 
     def uninstall(self) -> None:
         self.triton_attention._should_use_triton = self.saved["gate"]
         self.triton_attention._paged_attention_triton = self.saved["read"]
         self.pool_cls.write = self.saved["write"]
+        if self.cuda_graph is not None:
+            self.cuda_graph.build_decode_static_inputs = self.saved["graph_inputs"]
 
 
-def install(triton_attention=None, paged_kv_cache=None) -> Installed:
+def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
+            graph_inputs: bool = True) -> Installed:
     """Route infrared's paged decode attention to the B200 kernels.
 
-    ``triton_attention`` / ``paged_kv_cache`` default to the installed
-    ``infrared.model.triton_attention`` and ``infrared.cache.paged_kv_cache``
-    modules (any modules with the same names and call contract work).
+    ``triton_attention`` / ``paged_kv_cache`` / ``cuda_graph`` default to the
+    installed ``infrared.model.triton_attention``, ``infrared.cache.paged_kv_cache``
+    and ``infrared.engine.cuda_graph`` modules (any modules with the same names
+    and call contract work); ``graph_inputs=False`` leaves infrared's graph-input
+    builder alone.
     """
     ta = triton_attention or importlib.import_module("infrared.model.triton_attention")
     pk = paged_kv_cache or importlib.import_module("infrared.cache.paged_kv_cache")
+    cg = None
+    if graph_inputs:
+        cg = cuda_graph or importlib.import_module("infrared.engine.cuda_graph")
     pool_cls = pk.PagedKVPool
     saved = {"gate": ta._should_use_triton, "read": ta._paged_attention_triton,
              "write": pool_cls.write}
     ta._should_use_triton = should_use_b200
     ta._paged_attention_triton = paged_attention_b200
     pool_cls.write = _make_write(saved["write"])
-    return Installed(ta, pool_cls, saved)
+    if cg is not None:
+        saved["graph_inputs"] = cg.build_decode_static_inputs
+        cg.build_decode_static_inputs = _make_graph_inputs(saved["graph_inputs"],
+                                                           cg.DecodeInputs)
+    return Installed(ta, pool_cls, saved, cg)

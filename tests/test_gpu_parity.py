@@ -445,3 +445,64 @@ def test_workspace_reuse_across_shapes():
     assert_close_bf16(host_f32(small), host_f32(outs[0][:3]))
     with pytest.raises(ValueError, match="workspace"):
         irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16, ws=ws[:256])
+
+
+
+# ----------------------------------------------------------- graph-input builder
+
+
+@pytest.mark.parametrize("name", sorted(cases.GRAPH_CASES))
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_graph_inputs_match_reference_bit_exact(golden, name, dtype):
+    """ir_build_decode_inputs == infrared's build_decode_static_inputs (golden outputs)."""
+    from infrared_b200.graph_inputs import build_decode_static_inputs
+
+    tables, num_cached, last, bucket, t_max, bs = cases.graph_case_args(name)
+    got = build_decode_static_inputs(tables, num_cached, last, bucket, t_max, bs, DEV, dtype)
+    for key in ("ids", "positions", "write_slots", "gather_slots"):
+        np.testing.assert_array_equal(got.__getattribute__(key).cpu().numpy(),
+                                      golden[f"{name}/{key}"])
+    want_mask = torch.from_numpy(golden[f"{name}/mask"]).to(dtype)
+    want_mask[want_mask != 0] = torch.finfo(dtype).min
+    assert torch.equal(got.mask.cpu(), want_mask)
+
+
+def test_graph_inputs_errors_and_known_answers():
+    from infrared_b200.graph_inputs import build_decode_static_inputs
+
+    inp = build_decode_static_inputs([[0, 1], [2]], [5, 2], [7, 9], 4, 16, 4, DEV,
+                                     torch.float32)
+    assert inp.write_slots[:2].tolist() == [5, 10]
+    assert torch.equal(inp.gather_slots[2], inp.gather_slots[0])
+    with pytest.raises(ValueError, match="exceeds t_max"):
+        build_decode_static_inputs([[0]], [10], [1], 1, 8, 8, DEV, torch.float32)
+    with pytest.raises(ValueError, match="bucket_b"):
+        build_decode_static_inputs([[0]], [1], [1], 0, 8, 8, DEV, torch.float32)
+
+
+
+# ----------------------------------------------------------- failure path
+
+
+def test_bounded_wait_runs_out_and_context_survives():
+    """A decode whose pipeline barrier never completes (the test hook expects
+    bytes no copy delivers) gives up after its wait limit, reports TIMEOUT
+    through the error flag, and the next decode on the same context is right."""
+    import time
+
+    from infrared_b200 import _lib
+
+    w = wl.custom(46, 4, 28, 4, 128, 16, 100, 400, "bfloat16")
+    q, kp, vp, _, _ = dev_values(wl.numpy_values(w, 3), torch.bfloat16)
+    bt, ctx, _ = dev_meta(w)
+    irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16)
+    torch.cuda.synchronize()
+    assert _lib.load().ir_debug_stall_next_decode() == 0
+    t0 = time.perf_counter()
+    irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 30
+    with pytest.raises(irb.DeviceError, match="TIMEOUT"):
+        ops.check_device_errors()
+    out = irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16)
+    assert_close_bf16(host_f32(out), oracle_decode(w, *[host_f32(t) for t in (q, kp, vp)]))

@@ -31,25 +31,42 @@ def infrared():
     if REF not in sys.path:
         sys.path.insert(0, REF)
     import infrared.cache.paged_kv_cache as pk
+    import infrared.engine.cuda_graph as cg
     import infrared.model.triton_attention as ta
 
-    return ta, pk
+    return ta, pk, cg
 
 
 def test_install_uninstall_restores(infrared):
-    ta, pk = infrared
-    before = (ta._should_use_triton, ta._paged_attention_triton, pk.PagedKVPool.write)
-    h = shim.install(ta, pk)
+    ta, pk, cg = infrared
+    before = (ta._should_use_triton, ta._paged_attention_triton, pk.PagedKVPool.write,
+              cg.build_decode_static_inputs)
+    h = shim.install(ta, pk, cg)
     assert ta._should_use_triton is shim.should_use_b200
     assert ta._paged_attention_triton is shim.paged_attention_b200
     assert pk.PagedKVPool.write is not before[2]
+    assert cg.build_decode_static_inputs is not before[3]
     h.uninstall()
-    assert (ta._should_use_triton, ta._paged_attention_triton, pk.PagedKVPool.write) == before
+    assert (ta._should_use_triton, ta._paged_attention_triton, pk.PagedKVPool.write,
+            cg.build_decode_static_inputs) == before
+
+
+def test_cpu_graph_inputs_stay_on_reference_path(infrared):
+    ta, pk, cg = infrared
+    args = ([[0, 1], [2]], [5, 2], [7, 9], 4, 16, 4, "cpu", torch.float32)
+    ref = cg.build_decode_static_inputs(*args)
+    h = shim.install(ta, pk, cg)
+    try:
+        got = cg.build_decode_static_inputs(*args)
+    finally:
+        h.uninstall()
+    for f in ("ids", "positions", "write_slots", "gather_slots", "mask"):
+        assert torch.equal(getattr(got, f), getattr(ref, f))
 
 
 def test_cpu_calls_stay_on_reference_path(infrared):
     """With the shim installed, infrared's CPU decode gives its own result."""
-    ta, pk = infrared
+    ta, pk, cg = infrared
     w = wl.custom(3, 4, 14, 2, 64, 16, 5, 90, "float32")
     q, kp, vp, kn, vn = wl.numpy_values(w, 2)
     t = int(w.context_lens.max())
@@ -66,7 +83,7 @@ def test_cpu_calls_stay_on_reference_path(infrared):
         return out, pool
 
     ref_out, ref_pool = run()
-    h = shim.install(ta, pk)
+    h = shim.install(ta, pk, cg)
     try:
         out, pool = run()
     finally:
@@ -138,7 +155,7 @@ def test_shim_routes_decode_to_b200(dtype):
     from infrared_b200 import PagedContext, check_device_errors
 
     ta, pk, calls = _stand_in_seam()
-    h = shim.install(ta, pk)
+    h = shim.install(ta, pk, graph_inputs=False)
     try:
         w = wl.custom(9, 6, 28, 4, 128, 16, 10, 400, "float32", shared_frac=0.3)
         q, kp, vp, kn, vn = [torch.from_numpy(x).cuda().to(dtype) for x in wl.numpy_values(w, 4)]
