@@ -20,7 +20,9 @@ divided by the slowest rank's time.
 * ``e2e``: the same metric through the public Python API
   (``infrared_b200.paged_decode``) with host buffers: every step copies q,
   block tables and context lengths from pinned host memory and reads the
-  output back.
+  output back (inputs packed in one pinned buffer; double-buffered: the next
+  step's copy in and the previous step's copy out overlap this step's kernel
+  on two copy streams; kernels run in order).
 * ``roofline``: the decode call's bytes / its measured duration against the
   measured HBM copy bandwidth in MEASURED_PEAKS.json.
 * ``cpu_baseline`` / ``--impl reference``: the reference's naive CPU path
@@ -243,55 +245,72 @@ def run_ours(args):
             irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size, out=out, ws=ws)
 
     def measure_e2e():
-        """Public API with pinned host buffers; copies inside the timed region."""
-        q_host = sets[0][0].cpu().pin_memory()
-        bt_host = bt.cpu().pin_memory()
-        ctx_host = ctx.cpu().pin_memory()
-        out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-        q_dev = torch.empty_like(sets[0][0])
-        bt_dev, ctx_dev = torch.empty_like(bt), torch.empty_like(ctx)
-        kn_host = sets[0][3].cpu().pin_memory()
-        vn_host = sets[0][4].cpu().pin_memory()
-        sm_host = sm.cpu().pin_memory()
-        kn_dev, vn_dev, sm_dev = (torch.empty_like(sets[0][3]), torch.empty_like(sets[0][4]),
-                                  torch.empty_like(sm))
+        """Public API with pinned host buffers; every step copies its inputs in
+        and its result out. The step's inputs sit in one pinned buffer (one
+        copy in); double-buffered: step i+1's inputs copy in on one copy stream
+        and step i's result copies out on another while kernels run in order."""
+        parts = [sets[0][0], bt, ctx] + ([sets[0][3], sets[0][4], sm] if fused else [])
+        offs, total = [], 0
+        for t in parts:
+            offs.append(total)
+            total += -(-t.numel() * t.element_size() // 256) * 256
+        host_in = torch.empty(total, dtype=torch.uint8).pin_memory()
+        for t, o in zip(parts, offs):
+            nb = t.numel() * t.element_size()
+            host_in[o:o + nb].copy_(t.cpu().reshape(-1).view(torch.uint8))
+
+        def views(buf):
+            return [buf[o:o + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+                    for t, o in zip(parts, offs)]
+
         _, kp0, vp0, _, _ = sets[0]
+        bufs = []
+        for _ in range(2):
+            din = torch.empty(total, dtype=torch.uint8, device=dev)
+            bufs.append({"din": din, "in": views(din), "out": torch.empty_like(out),
+                         "host_out": torch.empty(out.shape, dtype=out.dtype).pin_memory(),
+                         "in_ready": torch.cuda.Event(), "done": torch.cuda.Event()})
+        compute = torch.cuda.current_stream(dev)
+        h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
-        def e2e_step():
-            q_dev.copy_(q_host, non_blocking=True)
-            bt_dev.copy_(bt_host, non_blocking=True)
-            ctx_dev.copy_(ctx_host, non_blocking=True)
+        def e2e_step(i):
+            bf = bufs[i % 2]
+            h2d_s.wait_event(bf["done"])          # step i-2 finished with this buffer
+            with torch.cuda.stream(h2d_s):
+                bf["din"].copy_(host_in, non_blocking=True)
+                bf["in_ready"].record(h2d_s)
+            compute.wait_event(bf["in_ready"])
+            x = bf["in"]
             if fused:
-                kn_dev.copy_(kn_host, non_blocking=True)
-                vn_dev.copy_(vn_host, non_blocking=True)
-                sm_dev.copy_(sm_host, non_blocking=True)
-                o = irb.paged_decode_write(q_dev, kn_dev, vn_dev, kp0, vp0, sm_dev, bt_dev,
-                                           ctx_dev, w.scale, w.block_size, ws=ws)
+                irb.paged_decode_write(x[0], x[3], x[4], kp0, vp0, x[5], x[1], x[2], w.scale,
+                                       w.block_size, out=bf["out"], ws=ws)
             else:
-                o = irb.paged_decode(q_dev, kp0, vp0, bt_dev, ctx_dev, w.scale, w.block_size,
-                                     ws=ws)
-            out_host.copy_(o, non_blocking=True)
+                irb.paged_decode(x[0], kp0, vp0, x[1], x[2], w.scale, w.block_size,
+                                 out=bf["out"], ws=ws)
+            bf["done"].record(compute)
+            d2h_s.wait_event(bf["done"])
+            with torch.cuda.stream(d2h_s):
+                bf["host_out"].copy_(bf["out"], non_blocking=True)
 
-        for _ in range(max(args.warmup, 3)):
-            e2e_step()
+        for i in range(max(args.warmup, 3)):
+            e2e_step(i)
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
-        ev[0].record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        ev[1].record(stream)
+        ev[0].record(compute)
+        h2d_s.wait_event(ev[0])
+        for i in range(args.steps):
+            e2e_step(i)
+        compute.wait_stream(d2h_s)
+        ev[1].record(compute)
         ev[1].synchronize()
         e2e_ms = ev[0].elapsed_time(ev[1])
         if world > 1:
             t = torch.tensor([e2e_ms], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = float(t.item())
-        h2d = (q_host.numel() * q_host.element_size() + bt_host.numel() * 4 +
-               ctx_host.numel() * 4)
-        if fused:
-            h2d += 2 * kn_host.numel() * kn_host.element_size() + sm_host.numel() * 8
-        d2h = out_host.numel() * out_host.element_size()
+        h2d = sum(t.numel() * t.element_size() for t in parts)
+        d2h = out.numel() * out.element_size()
         return e2e_ms, h2d, d2h
 
     stream = torch.cuda.Stream(dev)

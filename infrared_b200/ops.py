@@ -65,6 +65,9 @@ def _index_of(device) -> int:
 def error_flag(device: torch.device | int | None = None) -> torch.Tensor:
     """The per-device int32 error word the kernels OR their error bits into."""
     idx = _index_of(device)
+    t = _err_flags.get(idx)
+    if t is not None:
+        return t
     with _state_lock:
         t = _err_flags.get(idx)
         if t is None:
@@ -93,6 +96,9 @@ def _stream(device_index: int) -> int:
 
 def workspace(nbytes: int, device_index: int) -> torch.Tensor:
     """A cached, growing per-device workspace buffer (256-byte aligned)."""
+    t = _workspaces.get(device_index)
+    if t is not None and t.numel() >= nbytes:
+        return t
     with _state_lock:
         t = _workspaces.get(device_index)
         if t is None or t.numel() < nbytes:
@@ -103,8 +109,10 @@ def workspace(nbytes: int, device_index: int) -> torch.Tensor:
 
 
 def set_decode_path(path: int) -> None:
-    """0 = automatic kernel choice, 1 = CUDA-core kernel, 2 = TMA kernel."""
+    """0 = automatic kernel choice, 1 = CUDA-core kernel, 2 = TMA kernel,
+    3 = TMA kernel with one copy per (kv head, column half)."""
     check(_lib.load().ir_set_decode_path(path))
+    _plans.clear()   # cached workspace sizes depend on the kernel choice
 
 
 # --- pool scatter / gather ----------------------------------------------------
@@ -266,6 +274,21 @@ def _ws(s: DecodeShape, dev: int, ws: torch.Tensor | None) -> torch.Tensor:
     return ws
 
 
+# Validated call plans of paged_decode, keyed by everything the checks look
+# at (shapes, strides, dtypes, devices, block size, scale): a repeated call
+# (every layer of every decode step) skips the checks and the shape build.
+_plans: dict = {}
+
+
+def _decode_key(q, k_pool, v_pool, block_tables, context_lens, out, block_size, scale):
+    return (q.shape, q.stride(), q.dtype, q.device, k_pool.shape, k_pool.stride(),
+            k_pool.dtype, k_pool.device, v_pool.shape, v_pool.stride(), v_pool.dtype,
+            v_pool.device, block_tables.shape, block_tables.stride(), block_tables.dtype,
+            block_tables.device, context_lens.shape, context_lens.stride(),
+            context_lens.dtype, context_lens.device, out.shape, out.stride(), out.dtype,
+            block_size, float(scale))
+
+
 def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                  block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                  block_size: int, out: torch.Tensor | None = None,
@@ -276,15 +299,28 @@ def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     ``block_tables`` int32 ``[B, max_blocks]`` of block ids, ``context_lens``
     int32 ``[B]``. GQA: query head h reads kv head ``h // (H // Hkv)``.
     """
-    _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
-    dev = _dev_index(q)
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
-            out.stride(1) != q.shape[2]:
-        raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
-    s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
-    ws = _ws(s, dev, ws)
+    key = _decode_key(q, k_pool, v_pool, block_tables, context_lens, out, block_size, scale)
+    plan = _plans.get(key)
+    if plan is None:
+        _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+        if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
+                out.stride(1) != q.shape[2] or out.device != q.device:
+            raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
+        s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
+        nbytes = _lib.load().ir_paged_decode_workspace_size(s)
+        if nbytes == 0:
+            check(_lib.load().ir_paged_decode_plan(s, None, None))
+        plan = (s, nbytes, _dev_index(q))
+        if len(_plans) > 512:
+            _plans.clear()
+        _plans[key] = plan
+    s, nbytes, dev = plan
+    if ws is None:
+        ws = workspace(nbytes, dev)
+    elif ws.numel() < nbytes:
+        raise ValueError(f"workspace of {ws.numel()} bytes < {nbytes} needed")
     check(_lib.load().ir_paged_decode(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
