@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(kGenThreads)
 // when a sequence spans dozens of CTAs.
 template <typename T>
 __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
+  launch_dependents();   // the next kernel may start its own prologue now
   wait_prerequisites();  // the decode grid's pieces and prefix are complete
   __shared__ float4 s_acc[4][32];
   __shared__ float s_m[4], s_s[4];

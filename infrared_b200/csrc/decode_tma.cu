@@ -112,6 +112,10 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
     prefetch_tensormap(&tmk);
     prefetch_tensormap(&tmv);
   }
+  // Launched with programmatic dependent launch: everything above overlaps
+  // the previous kernel in the stream; nothing below runs before that kernel
+  // has finished and its writes are visible (no input is read earlier).
+  wait_prerequisites();
   find_share<NT, T>(a, g, kv0, HG, ri, sm_scan);  // includes __syncthreads
   launch_dependents();
   const int64_t start = ri->start, end = ri->end;
@@ -534,9 +538,17 @@ int launch_t(const CUtensorMap& tmk, const CUtensorMap& tmv, const DecodeArgs& a
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        L::kAlloc);
   if (e != cudaSuccess) return static_cast<int>(e);
-  dim3 grid(a.Hkv / HG, a.G);
-  kern<<<grid, 32 * (HG + 1), L::kAlloc, stream>>>(tmk, tmv, a, tp);
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.Hkv / HG, a.G);
+  cfg.blockDim = dim3(32 * (HG + 1));
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kern, tmk, tmv, a, tp));
 }
 
 template <typename T, int D, int HG, int R>
