@@ -2,12 +2,13 @@
 """Paged-decode attention throughput on B200 — one JSON line per run.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c4]
+                    [--config c2|c3|c4|c5]
 
 A step is one decode-attention call (one layer) over one batch of the
 workload: ``c2`` (default) is the Qwen2.5-7B geometry batch of 64 sequences
 with contexts U[512, 4096]; ``c3`` adds the fused K/V cache write over 256
-sequences with shared prefixes; ``c4`` is 4 x 32k contexts. At N GPUs (one
+sequences with shared prefixes; ``c4`` is 4 x 32k contexts; ``c5`` is a
+whole greedy decode step of a random-init Qwen2.5-7B (tok/s). At N GPUs (one
 process per GPU, launched by torchrun) every rank decodes its own batch of
 the workload — the sequences are sharded, there is no collective on the data
 path — so the scaling is weak and ``value`` is the bytes all ranks moved
@@ -56,7 +57,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["c2", "c3", "c4"], default="c2")
+    p.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c2")
     p.add_argument("--sets", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -441,6 +442,11 @@ def run_reference(args):
     world, rank, _ = dist_info()
     if rank != 0:
         return
+    if args.config == "c5":
+        print(json.dumps({"impl": "reference", "unavailable": "c5 is a whole Qwen2.5-7B decode "
+                          "step; the reference's CPU path restated here is the attention path "
+                          "(configs c2/c3/c4)"}), flush=True)
+        return
     w = make_workload(args.config, 0)
     gbs, secs, n = time_cpu_oracle(w, steps=args.steps, warmup=args.warmup)
     per_step = secs / max(n, 1)
@@ -584,10 +590,127 @@ def run_chunked(args):
         print(json.dumps(line), flush=True)
 
 
+def run_model(args):
+    """C5: one greedy decode token of a random-init Qwen2.5-7B for a batch of
+    128 sequences (contexts U[1024, 2048]), attention on the fused cache-write
+    + decode kernel, the rest of the step on library GEMMs; the step is one
+    CUDA graph replayed token after token. At N GPUs every rank holds the
+    weights and decodes its share of the 128 sequences (strong scaling, no
+    collective on the data path)."""
+    import torch
+    import torch.distributed as dist
+
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import model_step as ms
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    global_batch = args.batch or 128
+    ctx_all = ms.random_context_lens(global_batch, 1024, 2048, seed=0)
+    lo, hi = irdist.shard_sequences(ctx_all, world)[rank]
+    warm = max(args.warmup, 3)
+    model = ms.Qwen2DecodeStep(ms.QWEN25_7B, ctx_all[lo:hi], max_new=2 * warm + args.steps + min(args.steps, 100) + 8,
+                               device=dev, seed=rank)
+    w_bytes = model.weight_bytes()
+    for _ in range(warm):                      # eager steps (plans, workspaces, cuBLAS)
+        model.step()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            logits = model.step()
+        for _ in range(warm):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        kv_first = model.kv_bytes_per_step()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        clocks = ClockSampler(local)
+        ev[0].record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev[1].record(stream)
+        ev[1].synchronize()
+        clk = clocks.stop()
+    ms_dev = ev[0].elapsed_time(ev[1])
+    kv_bytes = (kv_first + model.kv_bytes_per_step()) // 2   # contexts grow by one a step
+    ms_job = irdist.max_over_ranks(ms_dev, device=dev) if world > 1 else ms_dev
+    # e2e: the engine's loop -- every step copies ids, positions and block
+    # tables in from pinned host memory, replays and reads the sampled ids back
+    b = model.batch
+    h_ids = torch.empty(b, dtype=torch.int64).pin_memory()
+    h_pos = torch.empty(b, dtype=torch.int64).pin_memory()
+    h_bt = model.block_tables.cpu().pin_memory()
+    h_ids.copy_(model.ids.cpu())
+    h_pos.copy_(model.positions.cpu())
+    e2e_steps = min(args.steps, 100)
+    if model.positions.max().item() + e2e_steps + 1 > model.max_blocks * model.bs:
+        e2e_steps = 0
+    with torch.cuda.stream(stream):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            model.ids.copy_(h_ids, non_blocking=True)
+            model.positions.copy_(h_pos, non_blocking=True)
+            model.block_tables.copy_(h_bt, non_blocking=True)
+            graph.replay()
+            h_ids.copy_(model.ids, non_blocking=True)
+            stream.synchronize()
+            h_pos += 1
+        e2e_s = time.perf_counter() - t0
+    e2e_s = irdist.max_over_ranks(e2e_s, device=dev) if world > 1 else e2e_s
+    del graph, logits
+    peak, peak_kind = measured_peaks()
+    per_step = ms_job / args.steps
+    step_bytes = w_bytes + kv_bytes
+    gbs = step_bytes / (ms_dev / args.steps / 1e3) / 1e9
+    tok_s = global_batch * args.steps / (ms_job / 1e3)
+    line = {
+        "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": warm, "ms_per_step": round(per_step, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init weights N(0,0.02), KV history N(0,0.5), random "
+                "token ids, random block tables (no checkpoint or dataset)",
+        "config": {"workload": "C5: Qwen2.5-7B decode step (28 layers, hidden 3584, 28/4 "
+                               "heads, inter 18944, vocab 152064), ctx U[1024,2048], block "
+                               "16, greedy, one CUDA graph per token",
+                   "global_batch": global_batch, "batch_per_gpu": b,
+                   "parallelism": f"sequence-sharded x{world}, weights replicated",
+                   "l2": "inputs larger than L2: ~14 GB of weights + KV read per step",
+                   "timing": "K graph replays, CUDA events, max over ranks"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_kind": peak_kind, "traffic": None,
+                     "scope": "whole decode step on one GPU: weights + KV history read "
+                              "(rank 0)", "weight_bytes": w_bytes, "kv_bytes": kv_bytes},
+        "e2e": {"value": round(global_batch * e2e_steps / e2e_s, 1) if e2e_steps else None,
+                "unit": "tok/s", "h2d_bytes_per_step": 2 * b * 8 + h_bt.numel() * 4,
+                "d2h_bytes_per_step": b * 8, "steps": e2e_steps},
+        "clocks": clk,
+        "gpu_launches": 2 * ms.QWEN25_7B.layers * args.steps,
+    }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "c5":
+        run_model(args)
     elif args.config == "c4" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_chunked(args)
     else:
