@@ -216,6 +216,31 @@ int ir_paged_decode_write(void* out, const void* q, void* k_pool, void* v_pool,
                           ir_stream_t stream);
 
 /*
+ * ir_paged_decode_write with rotary position embedding applied inside the
+ * kernel: q and k_new are the UN-rotated projections; the kernel rotates q
+ * (in registers) and the new K row (before it is stored in the pool and
+ * used) as infrared's apply_rotary_pos_emb does
+ * (infrared/model/layers.py:79-89: q * cos + rotate_half(q) * sin with the
+ * fp32 cos/sin tables cast to the dtype, each op rounded to the dtype), so
+ * the pool and the output equal rotate-then-ir_paged_decode_write exactly.
+ * rope_cos / rope_sin: fp32 [batch, head_dim] rows with row stride
+ * rope_stride elements (infrared's RotaryEmbedding output at the new
+ * token's position, infrared/model/layers.py:121-136). q, k_new and v_new
+ * may be row views of one fused QKV projection output (q_stride in shape,
+ * kv_stride here). Replaces apply_rotary_pos_emb + write + read of
+ * Attention.forward (infrared/model/layers.py:165-181) in one launch.
+ */
+int ir_paged_decode_rope_write(void* out, const void* q, void* k_pool, void* v_pool,
+                               const void* k_new, const void* v_new,
+                               int64_t kv_stride, const int64_t* slot_mapping,
+                               const float* rope_cos, const float* rope_sin,
+                               int64_t rope_stride, const int32_t* block_tables,
+                               const int32_t* context_lens,
+                               const ir_decode_shape* shape, void* workspace,
+                               size_t workspace_bytes, int32_t* err_flag,
+                               ir_stream_t stream);
+
+/*
  * Decode attention returning the softmax-normalised fp32 output and its
  * log-sum-exp instead of the final row: o [B, H, D] fp32 contiguous,
  * lse [B, H] fp32 natural log (-inf for an empty context, o = 0). These are

@@ -4,9 +4,10 @@ Three hand-written sm_100a CUDA paths behind a C ABI
 (``include/infrared_b200.h``, ``libinfrared_b200.so``):
 
 * ``cache_write`` — scatter of a step's K/V into the paged pool;
-* ``paged_decode`` / ``paged_decode_write`` — GQA decode attention over
-  block tables (optionally fused with the cache write), split across all SMs
-  in equal token shares with a log-sum-exp merge;
+* ``paged_decode`` / ``paged_decode_write`` / ``paged_decode_rope_write`` —
+  GQA decode attention over block tables (optionally fused with the cache
+  write, and with the rotary embedding of q and the new K), split across all
+  SMs in equal token shares with a log-sum-exp merge;
 * ``paged_decode_lse`` + ``lse_merge`` — partials of a KV range and their
   combination, used to spread one long context over several GPUs.
 
@@ -19,11 +20,12 @@ from ._lib import InfraredB200Error, UnsupportedShape
 from .attention import paged_attention
 from .ops import (DeviceError, cache_gather, cache_write, check_device_errors,
                   derive_block_metadata, lse_merge, paged_decode, paged_decode_lse,
-                  paged_decode_write)
+                  paged_decode_rope_write, paged_decode_write)
 from .paged_kv_cache import PagedContext, PagedKVPool
 
 __all__ = [
     "DeviceError", "InfraredB200Error", "PagedContext", "PagedKVPool", "UnsupportedShape",
     "cache_gather", "cache_write", "check_device_errors", "derive_block_metadata",
-    "lse_merge", "paged_attention", "paged_decode", "paged_decode_lse", "paged_decode_write",
+    "lse_merge", "paged_attention", "paged_decode", "paged_decode_lse",
+    "paged_decode_rope_write", "paged_decode_write",
 ]

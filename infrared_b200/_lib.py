@@ -92,6 +92,11 @@ _SIGNATURES = {
                                       c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                                       POINTER(DecodeShape), c_void_p, c_size_t,
                                       c_void_p, c_void_p]),
+    "ir_paged_decode_rope_write": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                           c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                                           c_int64, c_void_p, c_void_p,
+                                           POINTER(DecodeShape), c_void_p, c_size_t,
+                                           c_void_p, c_void_p]),
     "ir_paged_decode_lse": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, POINTER(DecodeShape), c_void_p,
                                     c_size_t, c_void_p, c_void_p]),

@@ -249,7 +249,8 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
                 const int64_t* slot_mapping, const int32_t* block_tables,
                 const int32_t* context_lens, const ir_decode_shape* s,
                 void* workspace, size_t workspace_bytes, int32_t* err,
-                cudaStream_t stream) {
+                cudaStream_t stream, const float* rope_cos = nullptr,
+                const float* rope_sin = nullptr, int64_t rope_stride = 0) {
   Plan plan;
   int rc = make_plan(s, &plan);
   if (rc) return rc;
@@ -263,6 +264,10 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
     return fail(IR_ERR_INVALID_ARG, "null k_new / v_new / slot_mapping");
   if (mode == Mode::kWrite && kv_stride < static_cast<int64_t>(s->num_kv_heads) * s->head_dim)
     return fail(IR_ERR_INVALID_ARG, "kv_stride < Hkv*D");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return fail(IR_ERR_INVALID_ARG, "rope_cos and rope_sin must both be given");
+  if (rope_cos && (rope_stride < s->head_dim || !aligned(rope_cos, 4) || !aligned(rope_sin, 4)))
+    return fail(IR_ERR_INVALID_ARG, "rope tables: stride < head_dim or not 4-byte aligned");
   if (!workspace || workspace_bytes < plan.bytes)
     return fail(IR_ERR_WORKSPACE, "workspace smaller than ir_paged_decode_workspace_size");
   if (!aligned(workspace, 256))
@@ -318,6 +323,9 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
   a.v_new = mode == Mode::kWrite ? v_new : nullptr;
   a.kv_stride = kv_stride;
   a.slot_mapping = slot_mapping;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.rope_stride = rope_stride;
   a.err = err;
 
   int e;
@@ -543,6 +551,22 @@ int ir_paged_decode_write(void* out, const void* q, void* k_pool, void* v_pool,
                      k_new, v_new, kv_stride, slot_mapping, block_tables,
                      context_lens, shape, workspace, workspace_bytes, err_flag,
                      stream);
+}
+
+int ir_paged_decode_rope_write(void* out, const void* q, void* k_pool, void* v_pool,
+                               const void* k_new, const void* v_new,
+                               int64_t kv_stride, const int64_t* slot_mapping,
+                               const float* rope_cos, const float* rope_sin,
+                               int64_t rope_stride, const int32_t* block_tables,
+                               const int32_t* context_lens,
+                               const ir_decode_shape* shape, void* workspace,
+                               size_t workspace_bytes, int32_t* err_flag,
+                               ir_stream_t stream) {
+  if (!rope_cos || !rope_sin) return fail(IR_ERR_INVALID_ARG, "null rope_cos / rope_sin");
+  return decode_impl(Mode::kWrite, out, nullptr, nullptr, q, k_pool, v_pool,
+                     k_new, v_new, kv_stride, slot_mapping, block_tables,
+                     context_lens, shape, workspace, workspace_bytes, err_flag,
+                     stream, rope_cos, rope_sin, rope_stride);
 }
 
 int ir_paged_decode_lse(float* o, float* lse, const void* q,

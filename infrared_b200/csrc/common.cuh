@@ -235,4 +235,32 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<__half2*>(&v));
+}
+
+// ---------------------------------------------------------------- RoPE
+
+// One element of x * cos + rotate_half(x) * sin evaluated the way PyTorch
+// evaluates that expression on tensors of dtype T: the fp32 cos/sin tables
+// are first cast to T, then each product and the sum is a separate
+// elementwise op computed in fp32 and rounded to T (no fused multiply-add).
+// rotate_half maps element d < D/2 to -x[d + D/2] and d >= D/2 to x[d - D/2];
+// `partner` is that other element and `upper` says which half d is in.
+template <typename T>
+__device__ __forceinline__ float rope_elem(float x, float partner, float c, float s,
+                                           bool upper) {
+  const float ct = DT<T>::to_f(DT<T>::from_f(c));
+  const float st = DT<T>::to_f(DT<T>::from_f(s));
+  const float a = DT<T>::to_f(DT<T>::from_f(__fmul_rn(x, ct)));
+  const float b = DT<T>::to_f(DT<T>::from_f(__fmul_rn(upper ? partner : -partner, st)));
+  return DT<T>::to_f(DT<T>::from_f(__fadd_rn(a, b)));
+}
+
 }  // namespace irb

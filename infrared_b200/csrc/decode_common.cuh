@@ -48,6 +48,11 @@ struct DecodeArgs {
   const void* v_new;
   int64_t kv_stride;
   const int64_t* slot_mapping;
+  // RoPE applied to q and to the new token's K inside the kernel (null: the
+  // inputs are already rotated): fp32 cos/sin rows [B, D] with rope_stride
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t rope_stride;
   int32_t* err;
 };
 

@@ -63,8 +63,16 @@ __global__ void __launch_bounds__(kGenThreads)
         cur_b = b;
         const T* qrow = reinterpret_cast<const T*>(a.q) + b * a.q_stride +
                         static_cast<int64_t>(kvh * a.n_rep) * D;
-        for (int i = tid; i < a.n_rep * D; i += kGenThreads)
-          q_s[i / D][i % D] = DT<T>::to_f(qrow[i]);
+        for (int i = tid; i < a.n_rep * D; i += kGenThreads) {
+          float x = DT<T>::to_f(qrow[i]);
+          if (a.rope_cos != nullptr) {
+            const int c = i % D, pc = (c + D / 2) % D;
+            const int64_t r = b * a.rope_stride + c;
+            x = rope_elem<T>(x, DT<T>::to_f(qrow[i - c + pc]), a.rope_cos[r], a.rope_sin[r],
+                             c >= D / 2);
+          }
+          q_s[i / D][i % D] = x;
+        }
       }
       if (tid < kMaxGroup) {
         m_s[tid] = -INFINITY;
@@ -84,8 +92,14 @@ __global__ void __launch_bounds__(kGenThreads)
         if (a.k_new != nullptr && pos == ctx - 1) {
           // fused cache write: the new token's K/V come from the inputs
           const int64_t src = b * a.kv_stride + static_cast<int64_t>(kvh) * D + c;
-          const T kn = reinterpret_cast<const T*>(a.k_new)[src];
+          T kn = reinterpret_cast<const T*>(a.k_new)[src];
           const T vn = reinterpret_cast<const T*>(a.v_new)[src];
+          if (a.rope_cos != nullptr) {
+            const T kp = reinterpret_cast<const T*>(a.k_new)[src - c + (c + D / 2) % D];
+            const int64_t r = b * a.rope_stride + c;
+            kn = DT<T>::from_f(rope_elem<T>(DT<T>::to_f(kn), DT<T>::to_f(kp), a.rope_cos[r],
+                                            a.rope_sin[r], c >= D / 2));
+          }
           kv = DT<T>::to_f(kn);
           vv = DT<T>::to_f(vn);
           const int64_t sw = a.slot_mapping[b];

@@ -76,6 +76,7 @@ struct TmaParams {
   int one_box;  // 1: one 4-D box per side; 0: one 3-D box per (head, half)
   int q_bulk;   // 1: the producer stages each segment's q rows in shared memory
   int stall;    // test hook: CTA (0, 0) expects bytes that never come (wait runs out)
+  int rope_smem;  // 1: the segment's RoPE cos/sin rows travel behind its q rows
 };
 
 template <typename T, int D, int HG, int NS, int R>
@@ -211,7 +212,8 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
           desc[slot] = ItemDesc{kb, ktok, kseg, kpk};
           uint8_t* kd = smem + slot * L::kStage;
           uint8_t* vd = kd + L::kSide;
-          const uint32_t qbytes = with_q ? static_cast<uint32_t>(HG * a.n_rep * D * 2) : 0u;
+          const uint32_t qrows = static_cast<uint32_t>(HG * a.n_rep * D * 2);
+          const uint32_t qbytes = with_q ? qrows + (tp.rope_smem ? D * 8u : 0u) : 0u;
           const bool valid = (kpk & kFlagValid) != 0;
           const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
           const uint32_t tbytes = valid ? static_cast<uint32_t>(nbox * 2 * L::kBox) : 0u;
@@ -223,7 +225,13 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
           if (with_q) {
             const T* qsrc = reinterpret_cast<const T*>(a.q) + kb * a.q_stride +
                             static_cast<int64_t>(kv0 * a.n_rep) * D;
-            bulk_load(smem + L::off_q + (kseg & 1) * L::kQBuf, qsrc, qbytes, &full[slot]);
+            uint8_t* qdst = smem + L::off_q + (kseg & 1) * L::kQBuf;
+            bulk_load(qdst, qsrc, qrows, &full[slot]);
+            if (tp.rope_smem) {
+              bulk_load(qdst + qrows, a.rope_cos + kb * a.rope_stride, D * 4, &full[slot]);
+              bulk_load(qdst + qrows + D * 4, a.rope_sin + kb * a.rope_stride, D * 4,
+                        &full[slot]);
+            }
           }
           if (valid) {
             for (int bx = 0; bx < nbox; ++bx) {
@@ -402,6 +410,29 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
           qf[ks][0] = qf[ks][1] = 0u;
         }
       }
+      if (a.rope_cos != nullptr && grp < a.n_rep) {
+        // RoPE on the q fragments: element d (column pair qd of k-step ks)
+        // pairs with d + D/2, which this lane holds in k-step ks + KS/2
+        const float* cs = tp.rope_smem
+            ? reinterpret_cast<const float*>(
+                  smem + L::off_q + (dsc.seg & 1) * L::kQBuf + HG * a.n_rep * D * 2)
+            : a.rope_cos + b * a.rope_stride;
+        const float* sn = tp.rope_smem ? cs + D : a.rope_sin + b * a.rope_stride;
+#pragma unroll
+        for (int ks = 0; ks < KS / 2; ++ks) {
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const int d = 16 * ks + 8 * w + qd;
+            const float2 lo = unpack2<T>(qf[ks][w]);
+            const float2 hi = unpack2<T>(qf[ks + KS / 2][w]);
+            const int u = d + D / 2;
+            qf[ks][w] = pack2<T>(rope_elem<T>(lo.x, hi.x, cs[d], sn[d], false),
+                                 rope_elem<T>(lo.y, hi.y, cs[d + 1], sn[d + 1], false));
+            qf[ks + KS / 2][w] = pack2<T>(rope_elem<T>(hi.x, lo.x, cs[u], sn[u], true),
+                                          rope_elem<T>(hi.y, lo.y, cs[u + 1], sn[u + 1], true));
+          }
+        }
+      }
       if (tp.q_bulk) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&qfree[dsc.seg & 1]);
@@ -439,7 +470,23 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
           const int c = is_v ? lane - kChunks : lane;
           const T* src = reinterpret_cast<const T*>(is_v ? a.v_new : a.k_new) +
                          b * a.kv_stride + static_cast<int64_t>(kvh) * D + c * 8;
-          const uint4 val = *reinterpret_cast<const uint4*>(src);
+          uint4 val = *reinterpret_cast<const uint4*>(src);
+          if (!is_v && a.rope_cos != nullptr) {
+            // RoPE on the new K row: chunk c pairs with chunk c ^ (kChunks / 2)
+            const int pc = c ^ (kChunks / 2);
+            const bool upper = c >= kChunks / 2;
+            const uint4 pv = *reinterpret_cast<const uint4*>(src + (pc - c) * 8);
+            const float* cs = a.rope_cos + b * a.rope_stride + c * 8;
+            const float* sn = a.rope_sin + b * a.rope_stride + c * 8;
+            uint32_t* xv = reinterpret_cast<uint32_t*>(&val);
+            const uint32_t* yv = reinterpret_cast<const uint32_t*>(&pv);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 x = unpack2<T>(xv[e]), y = unpack2<T>(yv[e]);
+              xv[e] = pack2<T>(rope_elem<T>(x.x, y.x, cs[2 * e], sn[2 * e], upper),
+                               rope_elem<T>(x.y, y.y, cs[2 * e + 1], sn[2 * e + 1], upper));
+            }
+          }
           uint8_t* base = is_v ? vst : kst;
           *reinterpret_cast<uint4*>(base + L::row_off(head, c >> 3, r) +
                                     (((c & 7) ^ (r & 7)) << 4)) = val;
@@ -607,8 +654,15 @@ int launch_decode_tma(const CUtensorMap& tmk, const CUtensorMap& tmv, const Deco
   const int64_t grp_elems = static_cast<int64_t>(a.n_rep) * a.D;
   const bool q_ok = (reinterpret_cast<uintptr_t>(a.q) % 16 == 0) && (a.q_stride * 2) % 16 == 0 &&
                     (grp_elems * 2) % 16 == 0;
-  const TmaParams tp{one_box, q_ok ? 1 : 0, stall};
   const int HG = tma_head_group(a.Hkv), R = a.bs == 8 ? 8 : 16;
+  // RoPE rows ride in the q buffer's unused tail ([HG][8][D] of 16-bit
+  // elements, HG * n_rep rows used) when 16-byte aligned and it has room
+  const bool rope_smem = q_ok && a.rope_cos != nullptr &&
+                         reinterpret_cast<uintptr_t>(a.rope_cos) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(a.rope_sin) % 16 == 0 &&
+                         (a.rope_stride * 4) % 16 == 0 &&
+                         static_cast<int64_t>(HG) * (8 - a.n_rep) * a.D * 2 >= 8 * a.D;
+  const TmaParams tp{one_box, q_ok ? 1 : 0, stall, rope_smem ? 1 : 0};
   if (dtype == IR_DTYPE_BF16)
     return by_dim<__nv_bfloat16>(0, a.D, HG, R, &tmk, &tmv, &a, &tp, stream);
   return by_dim<__half>(0, a.D, HG, R, &tmk, &tmv, &a, &tp, stream);

@@ -6,10 +6,10 @@ infrared runs its model as ``Qwen2ForCausalLM.forward`` (infrared/model/qwen2.py
 package replaces) -> o projection -> residual -> RMSNorm -> SwiGLU MLP
 (:185-196) -> residual; final norm and lm_head; greedy sampling. This module
 restates that decode step for a whole batch in plain PyTorch (GEMMs and
-elementwise ops are library calls; the attention is ``paged_decode_write`` —
-the fused K/V cache write + GQA decode kernel) with random weights, so the
-attention kernels can be measured inside a real 28-layer decode step under
-CUDA-graph replay. It is a measurement harness for the path, not a model
+elementwise ops are library calls; RoPE, the K/V cache write and the GQA
+decode are one kernel, ``paged_decode_rope_write``, fed with row views of
+the QKV projection output) with random weights, so the attention kernels can
+be measured inside a real 28-layer decode step under CUDA-graph replay. It is a measurement harness for the path, not a model
 implementation to serve with: no prefill (the KV history is synthetic, as in
 the kernel benchmarks) and no tokenizer.
 """
@@ -44,7 +44,14 @@ QWEN25_7B = Qwen2Geometry(152064, 3584, 28, 28, 4, 128, 18944)
 
 class Qwen2DecodeStep:
     """Random-init Qwen2 weights, a paged K/V pool holding a synthetic history
-    for ``batch`` sequences, and ``step()``: one greedy decode token for all."""
+    for ``batch`` sequences, and ``step()``: one greedy decode token for all.
+
+    ``fuse_rope`` (class attribute): True runs RoPE inside the attention
+    kernel; False rotates q/k with PyTorch ops first (infrared's
+    apply_rotary_pos_emb) and calls :meth:`attention` on the rotated rows.
+    """
+
+    fuse_rope = True
 
     def __init__(self, geo: Qwen2Geometry, context_lens, max_new: int, block_size: int = 16,
                  device="cuda", dtype=torch.bfloat16, seed: int = 0, std: float = 0.02):
@@ -107,9 +114,20 @@ class Qwen2DecodeStep:
         return x * cos + rot * sin
 
     def attention(self, layer: int, q, k, v, slots, ctx):
-        """The path under test: write this step's K/V and attend (fused kernel)."""
+        """Write this step's (rotated) K/V and attend: the fused kernel."""
         return ops.paged_decode_write(q, k, v, self.k_pool[layer], self.v_pool[layer], slots,
                                       self.block_tables, ctx, self.scale, self.bs)
+
+    def attend(self, layer: int, q, k, v, slots, ctx, cos, sin):
+        """RoPE + cache write + decode of one layer on un-rotated q/k/v views."""
+        if self.fuse_rope:
+            return ops.paged_decode_rope_write(q, k, v, self.k_pool[layer], self.v_pool[layer],
+                                               slots, self.block_tables, ctx, cos, sin,
+                                               self.scale, self.bs)
+        c = cos.to(self.dtype).unsqueeze(1)
+        s = sin.to(self.dtype).unsqueeze(1)
+        return self.attention(layer, self._rope(q, c, s), self._rope(k, c, s), v.contiguous(),
+                              slots, ctx)
 
     def step(self) -> torch.Tensor:
         """One decode token for every sequence; advances ids / positions in place
@@ -122,8 +140,7 @@ class Qwen2DecodeStep:
                  * self.bs + pos % self.bs)
         freqs = pos.float().unsqueeze(1) * self.inv_freq
         emb = torch.cat((freqs, freqs), dim=-1)
-        cos = emb.cos().to(self.dtype).unsqueeze(1)
-        sin = emb.sin().to(self.dtype).unsqueeze(1)
+        cos, sin = emb.cos(), emb.sin()          # fp32 [B, D], as RotaryEmbedding returns
         x = self.embed[self.ids]
         for l, w in enumerate(self.layers):
             hdn = self._rms(x, w["ln1"])
@@ -131,9 +148,7 @@ class Qwen2DecodeStep:
             q = qkv[:, : hq * d].view(b, hq, d)
             k = qkv[:, hq * d:(hq + hkv) * d].view(b, hkv, d)
             v = qkv[:, (hq + hkv) * d:].view(b, hkv, d)
-            q = self._rope(q, cos, sin).contiguous()
-            k = self._rope(k, cos, sin).contiguous()
-            attn = self.attention(l, q, k, v.contiguous(), slots, ctx)
+            attn = self.attend(l, q, k, v, slots, ctx, cos, sin)
             x = x + attn.view(b, hq * d) @ w["wo"]
             hdn = self._rms(x, w["ln2"])
             gate, up = (hdn @ w["wgu"]).chunk(2, dim=-1)

@@ -365,6 +365,55 @@ def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor
     return out
 
 
+def paged_decode_rope_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                            k_pool: torch.Tensor, v_pool: torch.Tensor,
+                            slot_mapping: torch.Tensor, block_tables: torch.Tensor,
+                            context_lens: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                            scale: float, block_size: int, out: torch.Tensor | None = None,
+                            ws: torch.Tensor | None = None) -> torch.Tensor:
+    """:func:`paged_decode_write` with RoPE applied in the kernel.
+
+    ``q [B, H, D]`` and ``k_new [B, Hkv, D]`` are un-rotated (they may be
+    row views of one QKV projection output); ``cos``/``sin`` are fp32
+    ``[B, D]`` (or ``[B, 1, D]``) tables at the new token's position, as
+    infrared's ``RotaryEmbedding`` returns them (layers.py:121-136). The pool
+    and the output equal ``apply_rotary_pos_emb`` (layers.py:79-89) followed
+    by :func:`paged_decode_write`, bit for bit.
+    """
+    _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+    dev = _dev_index(q)
+    b, hkv, d = q.shape[0], k_pool.shape[1], k_pool.shape[2]
+    k_new = k_new.reshape(b, hkv, d)
+    v_new = v_new.reshape(b, hkv, d)
+    if k_new.stride(0) != v_new.stride(0) or k_new.stride(2) != 1 or k_new.stride(1) != d \
+            or v_new.stride(2) != 1 or v_new.stride(1) != d:
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
+        raise ValueError("k_new/v_new must match q's dtype")
+    cos = cos.reshape(b, d) if cos.dim() != 2 else cos
+    sin = sin.reshape(b, d) if sin.dim() != 2 else sin
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.dtype != torch.float32 or t.device != q.device or t.shape != (b, d) \
+                or t.stride(1) != 1:
+            raise ValueError(f"{name} must be fp32 [B, D] rows on q's device")
+    if cos.stride(0) != sin.stride(0):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    slots = slot_mapping.reshape(-1)
+    if slots.dtype != torch.int64 or not slots.is_contiguous() or slots.numel() != b:
+        raise ValueError("slot_mapping must be contiguous int64 [B]")
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
+    ws = _ws(s, dev, ws)
+    check(_lib.load().ir_paged_decode_rope_write(
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
+        k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
+        slots.data_ptr(), cos.data_ptr(), sin.data_ptr(), cos.stride(0) if b else d,
+        block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
+        error_flag(dev).data_ptr(), _stream(dev)))
+    return out
+
+
 def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                      block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                      block_size: int, o: torch.Tensor | None = None,

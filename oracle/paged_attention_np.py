@@ -157,6 +157,37 @@ def blockwise_attention(q: np.ndarray, k_all: np.ndarray, v_all: np.ndarray,
 # --- decode-step metadata (infrared/engine/paged_engine.py, cuda_graph.py) ---
 
 
+def rope_tables(positions, head_dim: int, theta: float):
+    """fp32 ``(cos, sin)`` of shape ``positions.shape + (head_dim,)``:
+    ``inv_freq = 1 / theta ** (arange(0, D, 2) / D)``, ``emb = cat(f, f)``
+    with ``f = position * inv_freq`` (infrared/model/layers.py:121-136).
+    numpy's cos/sin may differ from torch's in the last bit; parity tests
+    take the tables from the golden fixtures."""
+    inv = (1.0 / (np.float32(theta) ** (np.arange(0, head_dim, 2, dtype=np.float32)
+                                          / np.float32(head_dim)))).astype(np.float32)
+    f = np.asarray(positions, dtype=np.float32)[..., None] * inv
+    emb = np.concatenate([f, f], axis=-1).astype(np.float32)
+    return np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
+
+
+def rotate_half(x: np.ndarray) -> np.ndarray:
+    """``(x1, x2) -> (-x2, x1)`` over the last dim (infrared/model/layers.py:72-76)."""
+    half = x.shape[-1] // 2
+    return np.concatenate([-x[..., half:], x[..., :half]], axis=-1)
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """``x * cos + rotate_half(x) * sin`` in fp32, one op at a time
+    (infrared/model/layers.py:79-89); ``x [B, heads, D]``, ``cos/sin [B, D]``
+    broadcast over the heads."""
+    x = x.astype(np.float32)
+    c = cos.astype(np.float32)[:, None, :]
+    s = sin.astype(np.float32)[:, None, :]
+    a = (x * c).astype(np.float32)
+    b = (rotate_half(x) * s).astype(np.float32)
+    return (a + b).astype(np.float32)
+
+
 def slot_of(block_table, pos: int, block_size: int) -> int:
     """Flat slot of logical position ``pos``.
 

@@ -86,3 +86,7 @@ def graph_case_args(name: str):
 
 
 BLOCKWISE_BLOCKS = (1, 3, 16, 100)
+
+# rotary embedding at the new token's position (position = context_len - 1):
+# case -> theta of infrared's RotaryEmbedding
+ROPE_CASES = {"c1": 1e6, "g7_d128_bs16": 1e4, "g8_d128_bs16": 1e6, "g2_d64_bs16": 1e6}

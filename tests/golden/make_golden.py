@@ -34,7 +34,8 @@ import torch  # noqa: E402
 import cases  # noqa: E402
 from infrared.cache.paged_kv_cache import PagedContext, PagedKVPool  # noqa: E402
 from infrared.engine.cuda_graph import build_decode_static_inputs  # noqa: E402
-from infrared.model.layers import repeat_kv  # noqa: E402
+from infrared.model.layers import (RotaryEmbedding, apply_rotary_pos_emb,  # noqa: E402
+                                   repeat_kv)
 from infrared.model.triton_attention import (  # noqa: E402
     paged_attention, paged_attention_blockwise_reference)
 
@@ -79,6 +80,30 @@ def run_blockwise(out: dict) -> None:
         out[f"blockwise/{bn}"] = res.numpy()[:, 0]
 
 
+def run_rope_case(name: str, theta: float, out: dict) -> None:
+    """RoPE at the new token's position, then the naive path on the rotated
+    q and k (what Attention.forward does, infrared/model/layers.py:160-181)."""
+    w, q, kp, vp, kn, vn = cases.attention_inputs(name)
+    s = cases.seam_tensors(w, q, kp, vp, kn, vn)
+    pos = torch.from_numpy(w.context_lens.astype(np.int64) - 1)[:, None]   # [B, 1]
+    cos, sin = RotaryEmbedding(w.head_dim, theta)(pos)                     # [B, 1, D]
+    q_rot, k_rot = apply_rotary_pos_emb(torch.from_numpy(s["q"]), torch.from_numpy(s["k"]),
+                                        cos, sin)
+    pool = PagedKVPool(1, w.num_blocks, w.block_size, w.num_kv_heads, w.head_dim,
+                       torch.float32)
+    pool.k.copy_(torch.from_numpy(s["pool_k"]))
+    pool.v.copy_(torch.from_numpy(s["pool_v"]))
+    ctx = PagedContext(pool, torch.from_numpy(s["write_slots"]),
+                       torch.from_numpy(s["gather_slots"]), use_triton=False)
+    res = paged_attention(q_rot, k_rot, torch.from_numpy(s["v"]), ctx,
+                          torch.from_numpy(s["mask"]), 0, w.scale, w.n_rep)
+    out[f"rope/{name}/cos"] = cos.numpy()[:, 0]
+    out[f"rope/{name}/sin"] = sin.numpy()[:, 0]
+    out[f"rope/{name}/q_rot"] = q_rot.numpy()[:, 0]
+    out[f"rope/{name}/k_rot"] = k_rot.numpy()[:, 0]
+    out[f"rope/{name}/out"] = res.numpy()[:, 0]
+
+
 def main() -> None:
     torch.manual_seed(0)
     out: dict = {}
@@ -87,6 +112,8 @@ def main() -> None:
     for name in cases.GRAPH_CASES:
         run_graph_case(name, out)
     run_blockwise(out)
+    for name, theta in cases.ROPE_CASES.items():
+        run_rope_case(name, theta, out)
     dst = HERE / "golden.npz"
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(out)} arrays)")

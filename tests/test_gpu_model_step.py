@@ -13,6 +13,8 @@ pytestmark = pytest.mark.gpu
 class _Checked(ms.Qwen2DecodeStep):
     """Runs the kernel, then the fp32 reference on the same pool, per layer."""
 
+    fuse_rope = False
+
     def __init__(self, *a, **kw):
         super().__init__(*a, **kw)
         self.worst = 0.0
@@ -26,6 +28,8 @@ class _Checked(ms.Qwen2DecodeStep):
 
 
 class _Reference(ms.Qwen2DecodeStep):
+    fuse_rope = False
+
     def attention(self, layer, q, k, v, slots, ctx):
         return self.reference_attention(layer, q, k, v, slots, ctx)
 
@@ -79,4 +83,20 @@ def test_step_replays_in_a_cuda_graph():
         assert torch.equal(graphed.ids, eager.ids)
     assert torch.equal(graphed.positions, eager.positions)
     assert torch.equal(graphed.k_pool, eager.k_pool)
+    ops.check_device_errors()
+
+
+class _Unfused(ms.Qwen2DecodeStep):
+    fuse_rope = False
+
+
+def test_fused_rope_step_equals_torch_rope_step():
+    """RoPE inside the kernel == PyTorch RoPE + the write/decode kernel, bit for bit."""
+    ctx = _ctx()
+    fused = ms.Qwen2DecodeStep(ms.tiny_geometry(), ctx, max_new=4, device="cuda", seed=5)
+    plain = _Unfused(ms.tiny_geometry(), ctx, max_new=4, device="cuda", seed=5)
+    for _ in range(3):
+        assert torch.equal(fused.step(), plain.step())
+    assert torch.equal(fused.k_pool, plain.k_pool)
+    assert torch.equal(fused.v_pool, plain.v_pool)
     ops.check_device_errors()

@@ -165,3 +165,25 @@ def test_c2_bytes_match_survey_estimate():
     assert 200e6 < w.algorithmic_bytes() < 400e6
     assert w.algorithmic_bytes() == orc.decode_bytes(w.context_lens, 28, 4, 128, 2,
                                                      w.max_blocks)
+
+
+@pytest.mark.parametrize("name", sorted(cases.ROPE_CASES))
+def test_rope_oracle_matches_reference(golden, name):
+    """apply_rope == infrared's apply_rotary_pos_emb bit for bit (fp32, same
+    tables); rope_tables == RotaryEmbedding up to the last-bit differences of
+    fp32 pow/cos between numpy and torch, amplified by the position (up to
+    300 rad here); attention on the rotated q/k == the reference's output."""
+    w, q, kp, vp, kn, vn = cases.attention_inputs(name)
+    cos, sin = golden[f"rope/{name}/cos"], golden[f"rope/{name}/sin"]
+    q_rot = orc.apply_rope(q, cos, sin)
+    k_rot = orc.apply_rope(kn, cos, sin)
+    np.testing.assert_array_equal(q_rot, golden[f"rope/{name}/q_rot"])
+    np.testing.assert_array_equal(k_rot, golden[f"rope/{name}/k_rot"])
+    c2, s2 = orc.rope_tables(w.context_lens - 1, w.head_dim, cases.ROPE_CASES[name])
+    np.testing.assert_allclose(c2, cos, atol=1e-4, rtol=0)
+    np.testing.assert_allclose(s2, sin, atol=1e-4, rtol=0)
+    kp2, vp2 = kp[None].copy(), vp[None].copy()
+    orc.pool_write(kp2, vp2, 0, k_rot, vn, w.slot_mapping)
+    out = orc.decode_from_tables(q_rot, kp2, vp2, 0, w.block_tables, w.context_lens,
+                                 w.block_size, w.scale, w.n_rep)
+    np.testing.assert_allclose(out, golden[f"rope/{name}/out"], atol=1e-5, rtol=0)
