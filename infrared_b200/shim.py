@@ -21,7 +21,12 @@ infrared:
 * (optional, ``graph_inputs=True``) ``cuda_graph.build_decode_static_inputs``
   (infrared/engine/cuda_graph.py:105-155, a module global read by
   ``CudaGraphDecoder.decode`` at :211) -> ``ir_build_decode_inputs`` for CUDA
-  devices, which removes the per-element Python loop of every graph step.
+  devices, which removes the per-element Python loop of every graph step;
+* (optional, ``fuse_rope=True``) ``layers.Attention.forward``
+  (infrared/model/layers.py:156-182, a class attribute) -> the same
+  projections, then ONE ``ir_paged_decode_rope_write`` that applies RoPE to
+  q and the new K, writes K/V and attends, for paged CUDA decode calls the
+  gate accepts; every other call runs infrared's own forward.
 
 The replacement read path trusts the engine's decode metadata: the mask is a
 prefix of zeros and ``gather_slots`` lists whole blocks; a call that breaks
@@ -70,6 +75,32 @@ def _make_write(original):
     return write
 
 
+def _make_attention_forward(original):
+    def forward(self, x, ctx, layer_idx):
+        paged = ctx.paged
+        b = x.shape[0]
+        # the gate of should_use_b200, applied to the layer's input
+        if (paged is None or not paged.use_triton or x.dim() != 3 or x.shape[1] != 1
+                or not x.is_cuda or x.dtype not in _SUPPORTED
+                or self.head_dim not in (64, 128) or paged.pool.k.dtype != x.dtype
+                or ctx.cos.dtype != torch.float32 or ctx.cos.numel() != b * self.head_dim):
+            return original(self, x, ctx, layer_idx)
+        q = self.q_proj(x).view(b, self.num_heads, self.head_dim)
+        k = self.k_proj(x).view(b, self.num_kv_heads, self.head_dim)
+        v = self.v_proj(x).view(b, self.num_kv_heads, self.head_dim)
+        pool = paged.pool
+        bt, cl = block_metadata(paged, ctx.mask)
+        out = ops.paged_decode_rope_write(q, k, v, pool.k[layer_idx], pool.v[layer_idx],
+                                          paged.write_slots.reshape(-1), bt, cl,
+                                          ctx.cos.reshape(b, self.head_dim),
+                                          ctx.sin.reshape(b, self.head_dim), self.scale,
+                                          pool.block_size)
+        return self.o_proj(out.view(b, 1, self.num_heads * self.head_dim))
+    forward.__doc__ = ("Attention.forward with RoPE + cache write + decode in one kernel "
+                       "for paged CUDA decode calls.")
+    return forward
+
+
 def _make_graph_inputs(original, decode_inputs_cls):
     from .graph_inputs import build_decode_static_inputs as on_device
 
@@ -92,6 +123,7 @@ class Installed:
     pool_cls: object
     saved: dict
     cuda_graph: object = None
+    attention_cls: object = None
 
     def uninstall(self) -> None:
         self.triton_attention._should_use_triton = self.saved["gate"]
@@ -99,17 +131,21 @@ class Installed:
         self.pool_cls.write = self.saved["write"]
         if self.cuda_graph is not None:
             self.cuda_graph.build_decode_static_inputs = self.saved["graph_inputs"]
+        if self.attention_cls is not None:
+            self.attention_cls.forward = self.saved["forward"]
 
 
 def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
-            graph_inputs: bool = True) -> Installed:
+            graph_inputs: bool = True, layers=None, fuse_rope: bool = False) -> Installed:
     """Route infrared's paged decode attention to the B200 kernels.
 
-    ``triton_attention`` / ``paged_kv_cache`` / ``cuda_graph`` default to the
-    installed ``infrared.model.triton_attention``, ``infrared.cache.paged_kv_cache``
-    and ``infrared.engine.cuda_graph`` modules (any modules with the same names
-    and call contract work); ``graph_inputs=False`` leaves infrared's graph-input
-    builder alone.
+    ``triton_attention`` / ``paged_kv_cache`` / ``cuda_graph`` / ``layers``
+    default to the installed ``infrared.model.triton_attention``,
+    ``infrared.cache.paged_kv_cache``, ``infrared.engine.cuda_graph`` and
+    ``infrared.model.layers`` modules (any modules with the same names and call
+    contract work); ``graph_inputs=False`` leaves infrared's graph-input
+    builder alone; ``fuse_rope=True`` also replaces ``Attention.forward`` so
+    that RoPE runs inside the decode kernel.
     """
     ta = triton_attention or importlib.import_module("infrared.model.triton_attention")
     pk = paged_kv_cache or importlib.import_module("infrared.cache.paged_kv_cache")
@@ -126,4 +162,10 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
         saved["graph_inputs"] = cg.build_decode_static_inputs
         cg.build_decode_static_inputs = _make_graph_inputs(saved["graph_inputs"],
                                                            cg.DecodeInputs)
-    return Installed(ta, pool_cls, saved, cg)
+    attn_cls = None
+    if fuse_rope:
+        ly = layers or importlib.import_module("infrared.model.layers")
+        attn_cls = ly.Attention
+        saved["forward"] = attn_cls.forward
+        attn_cls.forward = _make_attention_forward(saved["forward"])
+    return Installed(ta, pool_cls, saved, cg, attn_cls)

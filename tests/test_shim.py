@@ -191,3 +191,140 @@ def test_shim_routes_decode_to_b200(dtype):
         check_device_errors()
     finally:
         h.uninstall()
+
+
+# ---------------------------------------------------------------- RoPE-fused forward
+
+
+@pytest.fixture
+def infrared_layers(infrared):
+    import infrared.model.layers as ly
+
+    return ly
+
+
+def test_fuse_rope_install_and_cpu_fallback(infrared, infrared_layers):
+    """install(fuse_rope=True) swaps Attention.forward; a CPU paged decode call
+    still runs infrared's own forward bit for bit; uninstall restores it."""
+    from infrared.model.config import Qwen2Config
+
+    ta, pk, cg = infrared
+    ly = infrared_layers
+    cfg = Qwen2Config(vocab_size=64, hidden_size=128, intermediate_size=256,
+                      num_hidden_layers=1, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=32, rms_norm_eps=1e-6, rope_theta=1e6,
+                      max_position_embeddings=512, tie_word_embeddings=False,
+                      bos_token_id=0)
+    torch.manual_seed(0)
+    attn = ly.Attention(cfg)
+    w = wl.custom(4, 3, 4, 2, 32, 16, 3, 40, "float32")
+    kp, vp = wl.numpy_values(w, 1)[1:3]
+    t = int(w.context_lens.max())
+    gs = torch.from_numpy(orc.gather_slots_from_tables(w.block_tables, w.context_lens, 16, t))
+    mask = torch.from_numpy(orc.decode_mask(w.context_lens, t))
+    cos, sin = ly.RotaryEmbedding(32, 1e6)(torch.from_numpy(w.context_lens - 1)[:, None])
+    x = torch.randn(3, 1, 128)
+
+    def run():
+        pool = pk.PagedKVPool(1, w.num_blocks, 16, 2, 32, torch.float32)
+        pool.k[0].copy_(torch.from_numpy(kp))
+        pool.v[0].copy_(torch.from_numpy(vp))
+        paged = pk.PagedContext(pool, torch.from_numpy(w.slot_mapping), gs, use_triton=True)
+        ctx = ly.ForwardContext(cos=cos, sin=sin, mask=mask, kv_cache=None, start_col=0,
+                                paged=paged)
+        with torch.no_grad():
+            return attn(x, ctx, 0), pool
+
+    before = ly.Attention.forward
+    ref, ref_pool = run()
+    h = shim.install(ta, pk, cg, layers=ly, fuse_rope=True)
+    try:
+        assert ly.Attention.forward is not before
+        out, pool = run()
+    finally:
+        h.uninstall()
+    assert ly.Attention.forward is before
+    assert torch.equal(out, ref)
+    assert torch.equal(pool.k, ref_pool.k) and torch.equal(pool.v, ref_pool.v)
+
+
+def _stand_in_layers(ta):
+    """A module with infrared's Attention contract (layers.py:142-182), written here."""
+    ly = types.ModuleType("stand_in_layers")
+
+    class Attention(torch.nn.Module):
+        def __init__(self, hidden, nh, nkv, d, dtype, device):
+            super().__init__()
+            self.num_heads, self.num_kv_heads, self.head_dim = nh, nkv, d
+            self.n_rep = nh // nkv
+            self.scale = d ** -0.5
+            kw = dict(dtype=dtype, device=device)
+            self.q_proj = torch.nn.Linear(hidden, nh * d, bias=True, **kw)
+            self.k_proj = torch.nn.Linear(hidden, nkv * d, bias=True, **kw)
+            self.v_proj = torch.nn.Linear(hidden, nkv * d, bias=True, **kw)
+            self.o_proj = torch.nn.Linear(nh * d, hidden, bias=False, **kw)
+
+        def forward(self, x, ctx, layer_idx):
+            b, seq, _ = x.shape
+            q = self.q_proj(x).view(b, seq, self.num_heads, self.head_dim)
+            k = self.k_proj(x).view(b, seq, self.num_kv_heads, self.head_dim)
+            v = self.v_proj(x).view(b, seq, self.num_kv_heads, self.head_dim)
+            cos = ctx.cos.unsqueeze(2).to(q.dtype)
+            sin = ctx.sin.unsqueeze(2).to(q.dtype)
+            half = self.head_dim // 2
+
+            def rot(t):
+                return torch.cat((-t[..., half:], t[..., :half]), dim=-1)
+
+            q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
+            out = ta.paged_attention(q, k, v, ctx.paged, ctx.mask, layer_idx, self.scale,
+                                     self.n_rep)
+            return self.o_proj(out.reshape(b, seq, self.num_heads * self.head_dim))
+
+    ly.Attention = Attention
+    return ly
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_rope_forward_equals_installed_seam(dtype):
+    """Attention.forward with RoPE in the kernel == the same layer through the
+    installed seam (PyTorch RoPE, ir_cache_write, ir_paged_decode), bit for bit."""
+    from infrared_b200 import PagedContext, check_device_errors
+
+    ta, pk, calls = _stand_in_seam()
+    ly = _stand_in_layers(ta)
+    torch.manual_seed(1)
+    attn = ly.Attention(512, 28, 4, 128, dtype, "cuda")
+    w = wl.custom(19, 9, 28, 4, 128, 16, 1, 600, "float32", shared_frac=0.3)
+    kp, vp = [torch.from_numpy(a).cuda().to(dtype) for a in wl.numpy_values(w, 2)[1:3]]
+    t = int(w.context_lens.max())
+    gs = torch.from_numpy(orc.gather_slots_from_tables(w.block_tables, w.context_lens, 16,
+                                                       t)).cuda()
+    mask = torch.from_numpy(orc.decode_mask(w.context_lens, t)).cuda().to(dtype)
+    cos_np, sin_np = orc.rope_tables((w.context_lens - 1)[:, None], 128, 1e6)
+    cos, sin = torch.from_numpy(cos_np).cuda(), torch.from_numpy(sin_np).cuda()   # [B,1,D]
+    x = torch.randn(w.batch, 1, 512, device="cuda").to(dtype)
+
+    def run(fuse):
+        pool = pk.PagedKVPool(2, w.num_blocks, 16, 4, 128, dtype, "cuda")
+        pool.k[1].copy_(kp)
+        pool.v[1].copy_(vp)
+        paged = PagedContext(pool, torch.from_numpy(w.slot_mapping).cuda(), gs,
+                             use_triton=True)
+        ctx = types.SimpleNamespace(cos=cos, sin=sin, mask=mask, paged=paged)
+        h = shim.install(ta, pk, graph_inputs=False, layers=ly, fuse_rope=fuse)
+        try:
+            with torch.no_grad():
+                return attn(x, ctx, 1), pool
+        finally:
+            h.uninstall()
+
+    ref, ref_pool = run(False)
+    assert calls["b200"] == 1
+    out, pool = run(True)
+    assert calls["b200"] == 1          # the fused forward never reached the seam
+    assert torch.equal(out, ref)
+    assert torch.equal(pool.k, ref_pool.k) and torch.equal(pool.v, ref_pool.v)
+    check_device_errors()
