@@ -333,6 +333,109 @@ def decode_from_tables(q: np.ndarray, pool_k: np.ndarray, pool_v: np.ndarray,
     return out
 
 
+# --- prefill / mixed varlen (Sq > 1) -----------------------------------------
+
+
+def varlen_mask(q_seq_ids, q_pos, k_seq_ids, k_pos) -> np.ndarray:
+    """Additive ``[1, 1, Q, K]`` mask of a packed multi-sequence frame: a query
+    token attends a key of the same sequence at or before its position
+    (infrared/model/inputs.py:64-94, ``build_varlen_mask``)."""
+    q_seq_ids, q_pos = np.asarray(q_seq_ids), np.asarray(q_pos)
+    k_seq_ids, k_pos = np.asarray(k_seq_ids), np.asarray(k_pos)
+    allowed = (q_seq_ids[:, None] == k_seq_ids[None, :]) & (k_pos[None, :] <= q_pos[:, None])
+    return np.where(allowed, np.float32(0), np.float32(F32_MIN))[None, None].astype(np.float32)
+
+
+def varlen_frame(block_tables, starts, q_lens, block_size: int):
+    """The packed frame of infrared's mixed step for sequences whose first
+    ``starts[s]`` tokens are cached and ``q_lens[s]`` new tokens are forwarded
+    (infrared/engine/paged_engine.py:478-496): per query token its write slot,
+    sequence id and position; per gathered key its slot, sequence id and
+    position. Returns a dict of numpy arrays."""
+    ws, gs, qs, qp, ks, kp = [], [], [], [], [], []
+    for i, (st, ql) in enumerate(zip(starts, q_lens)):
+        for p in range(st, st + ql):
+            ws.append(slot_of(block_tables[i], p, block_size))
+            qs.append(i)
+            qp.append(p)
+        for p in range(st + ql):
+            gs.append(slot_of(block_tables[i], p, block_size))
+            ks.append(i)
+            kp.append(p)
+    return {"write_slots": np.array(ws, np.int64), "gather_slots": np.array(gs, np.int64)[None],
+            "q_seq_ids": np.array(qs), "q_pos": np.array(qp), "k_seq_ids": np.array(ks),
+            "k_pos": np.array(kp)}
+
+
+def varlen_metadata(gather_slots: np.ndarray, mask: np.ndarray, block_size: int):
+    """Inverse of :func:`varlen_frame` + :func:`varlen_mask` for one packed
+    frame (``gather_slots [1, K]``, ``mask [1, 1, Q, K]``): every query row must
+    allow one contiguous key range ``[lo, lo + n)``; consecutive rows with the
+    same ``lo`` form a sequence whose history is its key range of the last
+    row, block-structured from ``lo``. Returns ``(block_tables, context_lens,
+    q_start, ok)``; ``ok`` is False when the frame does not have that form."""
+    m = mask.reshape(mask.shape[-2], mask.shape[-1])
+    gsl = gather_slots.reshape(-1)
+    q, k = m.shape
+    allowed = m == 0
+    ok = True
+    lo = np.zeros(q, np.int64)
+    cnt = allowed.sum(axis=1).astype(np.int64)
+    for i in range(q):
+        nz = np.flatnonzero(allowed[i])
+        if len(nz) == 0 or nz[-1] - nz[0] + 1 != len(nz):
+            ok = False
+            lo[i] = nz[0] if len(nz) else 0
+            continue
+        lo[i] = nz[0]
+    starts = [0] + [i for i in range(1, q) if lo[i] != lo[i - 1]]
+    q_start = np.array(starts + [q], np.int32)
+    nseq = len(starts)
+    ctx = np.zeros(nseq, np.int32)
+    max_blocks = max(1, -(-int(cnt.max()) // block_size)) if q else 1
+    bt = np.zeros((nseq, max_blocks), np.int32)
+    for s in range(nseq):
+        r0, r1 = q_start[s], q_start[s + 1]
+        c = int(cnt[r1 - 1])
+        ctx[s] = c
+        if np.any(np.diff(cnt[r0:r1]) != 1):
+            ok = False
+        base = int(lo[r0])
+        hist = gsl[base:base + c]
+        first = hist[0:c:block_size]
+        bt[s, :len(first)] = first // block_size
+        pos = np.arange(c)
+        want = bt[s, pos // block_size].astype(np.int64) * block_size + pos % block_size
+        if not np.array_equal(want, hist):
+            ok = False
+    return bt, ctx, q_start, ok
+
+
+def prefill_from_tables(q: np.ndarray, pool_k: np.ndarray, pool_v: np.ndarray,
+                        layer_idx: int, block_tables: np.ndarray, context_lens,
+                        q_start, block_size: int, scale: float, n_rep: int) -> np.ndarray:
+    """Causal attention of packed query rows ``q [Q, H, D]`` over block-table
+    histories: sequence ``s`` owns rows ``[q_start[s], q_start[s+1])``, its
+    last ``q_len`` positions ``ctx - q_len .. ctx - 1``; a row at position
+    ``p`` attends positions ``0..p`` (the naive path with the causal /
+    varlen masks of infrared/model/inputs.py:38-94). Returns float32."""
+    out = np.zeros(q.shape, np.float32)
+    for s in range(len(context_lens)):
+        r0, r1 = int(q_start[s]), int(q_start[s + 1])
+        c, ql = int(context_lens[s]), r1 - r0
+        if ql == 0:
+            continue
+        gs = gather_slots_from_tables(block_tables[s:s + 1], context_lens[s:s + 1],
+                                      block_size, c)
+        k_all = repeat_kv(pool_gather(pool_k, layer_idx, gs), n_rep)
+        v_all = repeat_kv(pool_gather(pool_v, layer_idx, gs), n_rep)
+        pos = np.arange(c - ql, c)
+        allowed = np.arange(c)[None, :] <= pos[:, None]
+        mask = np.where(allowed, np.float32(0), np.float32(F32_MIN))[None, None]
+        out[r0:r1] = masked_attention(q[r0:r1][None], k_all, v_all, mask, scale)[0]
+    return out
+
+
 # --- split-KV partials and their merge (no reference counterpart) ------------
 
 

@@ -90,3 +90,47 @@ BLOCKWISE_BLOCKS = (1, 3, 16, 100)
 # rotary embedding at the new token's position (position = context_len - 1):
 # case -> theta of infrared's RotaryEmbedding
 ROPE_CASES = {"c1": 1e6, "g7_d128_bs16": 1e4, "g8_d128_bs16": 1e6, "g2_d64_bs16": 1e6}
+
+
+# prefill / mixed varlen frames (reference: paged_engine.py:170-221 prefill with a
+# cached prefix, :461-516 packed mixed step): name -> (seed, H, Hkv, D, block size,
+# [(cached tokens, forwarded tokens) per sequence])
+PREFILL_CASES = {
+    "prefill_one": (31, 14, 2, 64, 16, [(37, 63)]),
+    "varlen_mix": (32, 8, 2, 128, 16, [(0, 20), (50, 1), (30, 17), (0, 5)]),
+    "varlen_bs8": (33, 12, 4, 64, 8, [(9, 33), (64, 2), (1, 40)]),
+    "varlen_g7": (34, 7, 1, 128, 16, [(0, 130), (200, 1), (3, 40)]),
+}
+
+
+def prefill_inputs(name: str) -> dict:
+    """Seeded fp32 inputs of a prefill case: block tables, the packed frame, q and
+    this step's K/V for every forwarded token, and the initial pools."""
+    from oracle import paged_attention_np as orc
+
+    seed, h, hkv, d, bs, chunks = PREFILL_CASES[name]
+    rng = np.random.default_rng(seed)
+    starts = [c[0] for c in chunks]
+    qls = [c[1] for c in chunks]
+    ctx = np.array([st + ql for st, ql in chunks], np.int32)
+    nblk = [-(-int(c) // bs) for c in ctx]
+    num_blocks = sum(nblk) + 4
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    bt = np.zeros((len(chunks), max(nblk)), np.int32)
+    off = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[off:off + n]
+        off += n
+    q_start = np.concatenate([[0], np.cumsum(qls)]).astype(np.int32)
+    nq = int(q_start[-1])
+    return {
+        "h": h, "hkv": hkv, "d": d, "bs": bs, "scale": d ** -0.5, "n_rep": h // hkv,
+        "starts": starts, "q_lens": qls, "block_tables": bt, "context_lens": ctx,
+        "q_start": q_start, "num_blocks": num_blocks,
+        "q": rng.standard_normal((nq, h, d), dtype=np.float32),
+        "k": rng.standard_normal((nq, hkv, d), dtype=np.float32),
+        "v": rng.standard_normal((nq, hkv, d), dtype=np.float32),
+        "pool_k": rng.standard_normal((num_blocks * bs, hkv, d), dtype=np.float32),
+        "pool_v": rng.standard_normal((num_blocks * bs, hkv, d), dtype=np.float32),
+        "frame": orc.varlen_frame(bt, starts, qls, bs),
+    }

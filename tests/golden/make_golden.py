@@ -34,6 +34,7 @@ import torch  # noqa: E402
 import cases  # noqa: E402
 from infrared.cache.paged_kv_cache import PagedContext, PagedKVPool  # noqa: E402
 from infrared.engine.cuda_graph import build_decode_static_inputs  # noqa: E402
+from infrared.model.inputs import build_attention_mask, build_varlen_mask  # noqa: E402
 from infrared.model.layers import (RotaryEmbedding, apply_rotary_pos_emb,  # noqa: E402
                                    repeat_kv)
 from infrared.model.triton_attention import (  # noqa: E402
@@ -104,6 +105,31 @@ def run_rope_case(name: str, theta: float, out: dict) -> None:
     out[f"rope/{name}/out"] = res.numpy()[:, 0]
 
 
+def run_prefill_case(name: str, out: dict) -> None:
+    """infrared's prefill (one prompt, cached prefix: build_attention_mask) or
+    packed mixed step (build_varlen_mask) through its naive paged path."""
+    c = cases.prefill_inputs(name)
+    fr = c["frame"]
+    pool = PagedKVPool(1, c["num_blocks"], c["bs"], c["hkv"], c["d"], torch.float32)
+    pool.k[0].copy_(torch.from_numpy(c["pool_k"]))
+    pool.v[0].copy_(torch.from_numpy(c["pool_v"]))
+    if len(c["starts"]) == 1:
+        mask = build_attention_mask([0], c["starts"][0], c["q_lens"][0],
+                                    int(c["context_lens"][0]), torch.float32, "cpu")
+    else:
+        mask = build_varlen_mask(torch.from_numpy(fr["q_seq_ids"]),
+                                 torch.from_numpy(fr["q_pos"]),
+                                 torch.from_numpy(fr["k_seq_ids"]),
+                                 torch.from_numpy(fr["k_pos"]), torch.float32, "cpu")
+    ctx = PagedContext(pool, torch.from_numpy(fr["write_slots"]),
+                       torch.from_numpy(fr["gather_slots"]), use_triton=False)
+    res = paged_attention(torch.from_numpy(c["q"])[None], torch.from_numpy(c["k"])[None],
+                          torch.from_numpy(c["v"])[None], ctx, mask, 0, c["scale"], c["n_rep"])
+    out[f"prefill/{name}/out"] = res.numpy()[0]
+    out[f"prefill/{name}/mask_digest"] = np.array(cases.digest(mask.numpy()))
+    out[f"prefill/{name}/pool_digest"] = np.array(cases.digest(pool.k.numpy(), pool.v.numpy()))
+
+
 def main() -> None:
     torch.manual_seed(0)
     out: dict = {}
@@ -114,6 +140,8 @@ def main() -> None:
     run_blockwise(out)
     for name, theta in cases.ROPE_CASES.items():
         run_rope_case(name, theta, out)
+    for name in cases.PREFILL_CASES:
+        run_prefill_case(name, out)
     dst = HERE / "golden.npz"
     np.savez_compressed(dst, **out)
     print(f"wrote {dst} ({dst.stat().st_size} bytes, {len(out)} arrays)")

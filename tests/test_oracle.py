@@ -187,3 +187,35 @@ def test_rope_oracle_matches_reference(golden, name):
     out = orc.decode_from_tables(q_rot, kp2, vp2, 0, w.block_tables, w.context_lens,
                                  w.block_size, w.scale, w.n_rep)
     np.testing.assert_allclose(out, golden[f"rope/{name}/out"], atol=1e-5, rtol=0)
+
+
+@pytest.mark.parametrize("name", sorted(cases.PREFILL_CASES))
+def test_prefill_oracle_matches_reference(golden, name):
+    """Prefill with a cached prefix and packed mixed steps: the oracle's mask is
+    infrared's mask bit for bit, the pool after the write is infrared's, and
+    the block-table prefill equals infrared's naive path (fp32, 1e-5)."""
+    c = cases.prefill_inputs(name)
+    fr = c["frame"]
+    mask = orc.varlen_mask(fr["q_seq_ids"], fr["q_pos"], fr["k_seq_ids"], fr["k_pos"])
+    assert cases.digest(mask) == str(golden[f"prefill/{name}/mask_digest"])
+    kp, vp = c["pool_k"][None].copy(), c["pool_v"][None].copy()
+    orc.pool_write(kp, vp, 0, c["k"], c["v"], fr["write_slots"])
+    assert cases.digest(kp, vp) == str(golden[f"prefill/{name}/pool_digest"])
+    out = orc.prefill_from_tables(c["q"], kp, vp, 0, c["block_tables"], c["context_lens"],
+                                  c["q_start"], c["bs"], c["scale"], c["n_rep"])
+    np.testing.assert_allclose(out, golden[f"prefill/{name}/out"], atol=1e-5, rtol=0)
+    # the frame's (gather_slots, mask) give back the block-table form
+    bt, ctx, q_start, ok = orc.varlen_metadata(fr["gather_slots"], mask, c["bs"])
+    assert ok
+    np.testing.assert_array_equal(ctx, c["context_lens"])
+    np.testing.assert_array_equal(q_start, c["q_start"])
+    for s in range(len(ctx)):
+        nb = -(-int(ctx[s]) // c["bs"])
+        np.testing.assert_array_equal(bt[s, :nb], c["block_tables"][s, :nb])
+
+
+def test_varlen_metadata_rejects_non_contiguous_rows():
+    mask = orc.varlen_mask([0, 0], [1, 2], [0, 0, 0], [0, 1, 2])
+    mask[0, 0, 1, 1] = orc.F32_MIN          # a hole inside row 1's range
+    _, _, _, ok = orc.varlen_metadata(np.arange(3)[None], mask, 1)
+    assert not ok
