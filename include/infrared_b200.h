@@ -305,6 +305,56 @@ int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
                  int64_t lse_part_stride, int num_parts, int batch,
                  int num_heads, int head_dim, int dtype, ir_stream_t stream);
 
+/* ---------------------------------------------------------- prefill
+ *
+ * Paged attention of packed query rows (prefill with a cached prefix, and
+ * infrared's mixed prefill + decode steps): sequence s owns query rows
+ * [q_start[s], q_start[s+1]) of q [total_q, H, D], which are its LAST q_len
+ * positions ctx - q_len .. ctx - 1 (ctx = context_lens[s], the history length
+ * after this step's K/V were written to the pool). The row at position p
+ * attends positions 0..p of its own sequence, read through block_tables[s].
+ * Replaces infrared's read path for Sq > 1 (_paged_attention_naive,
+ * infrared/model/triton_attention.py:110-129, with the causal mask of
+ * infrared/model/inputs.py:38-61 or the packed-frame mask of :64-94, as
+ * built by infrared/engine/paged_engine.py:197-221 and :461-516).
+ */
+typedef struct ir_prefill_shape {
+  int num_seqs;     /* S: sequences in the frame */
+  int total_q;      /* packed query rows */
+  int num_heads;    /* H */
+  int num_kv_heads; /* Hkv, divides H */
+  int head_dim;     /* 64 or 128 */
+  int block_size;
+  int max_blocks;   /* columns of block_tables */
+  int64_t bt_stride;
+  int64_t q_stride;   /* elements between query rows (>= H * D) */
+  int64_t out_stride; /* elements between output rows (>= H * D) */
+  int64_t num_slots;  /* rows of one layer's pool */
+  float scale;
+  int dtype;          /* IR_DTYPE_* */
+} ir_prefill_shape;
+
+/* Kernel choice for ir_paged_prefill: 0 auto, 1 rows as decode rows (every
+ * query row decoded as its own sequence; any dtype), 2 the tcgen05 tensor-core
+ * kernel (bf16/fp16, power-of-two block sizes >= 8; auto picks it whenever
+ * eligible). Process-wide; a test and tuning hook. */
+int ir_set_prefill_path(int path);
+
+/* Path (1 or 2) ir_paged_prefill takes for this shape. */
+int ir_paged_prefill_plan(const ir_prefill_shape* shape, int* path);
+
+/* Workspace bytes ir_paged_prefill needs (0 for the tensor-core path). */
+size_t ir_paged_prefill_workspace_size(const ir_prefill_shape* shape);
+
+/* out[t, h, :] for every packed query row t. context_lens and q_start are
+ * int32 device arrays; a sequence with context_lens < q_len (or past the
+ * block table) sets IR_DEVERR_CONTEXT_LEN and its rows are not valid output;
+ * bad block ids read zeros and set IR_DEVERR_BLOCK_ID. */
+int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v_pool,
+                     const int32_t* block_tables, const int32_t* context_lens,
+                     const int32_t* q_start, const ir_prefill_shape* shape, void* workspace,
+                     size_t workspace_bytes, int32_t* err_flag, ir_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

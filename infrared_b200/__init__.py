@@ -9,7 +9,9 @@ Three hand-written sm_100a CUDA paths behind a C ABI
   write, and with the rotary embedding of q and the new K), split across all
   SMs in equal token shares with a log-sum-exp merge;
 * ``paged_decode_lse`` + ``lse_merge`` — partials of a KV range and their
-  combination, used to spread one long context over several GPUs.
+  combination, used to spread one long context over several GPUs;
+* ``paged_prefill`` — causal attention of packed query rows (prefill with a
+  cached prefix, mixed prefill + decode frames) on the tcgen05 tensor cores.
 
 ``PagedKVPool``, ``PagedContext`` and ``paged_attention`` keep the
 reference engine's interface; ``shim.install()`` routes infrared's own
@@ -20,12 +22,12 @@ from ._lib import InfraredB200Error, UnsupportedShape
 from .attention import paged_attention
 from .ops import (DeviceError, cache_gather, cache_write, check_device_errors,
                   derive_block_metadata, lse_merge, paged_decode, paged_decode_lse,
-                  paged_decode_rope_write, paged_decode_write)
+                  paged_decode_rope_write, paged_decode_write, paged_prefill)
 from .paged_kv_cache import PagedContext, PagedKVPool
 
 __all__ = [
     "DeviceError", "InfraredB200Error", "PagedContext", "PagedKVPool", "UnsupportedShape",
     "cache_gather", "cache_write", "check_device_errors", "derive_block_metadata",
     "lse_merge", "paged_attention", "paged_decode", "paged_decode_lse",
-    "paged_decode_rope_write", "paged_decode_write",
+    "paged_decode_rope_write", "paged_decode_write", "paged_prefill",
 ]

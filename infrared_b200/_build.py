@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "libinfrared_b200.so"
 
-SOURCES = ["capi.cu", "cache_ops.cu", "decode_generic.cu", "decode_tma.cu"]
+SOURCES = ["capi.cu", "cache_ops.cu", "decode_generic.cu", "decode_tma.cu", "prefill_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -65,8 +65,34 @@ class DecodeShape(ctypes.Structure):
     ]
 
 
+class PrefillShape(ctypes.Structure):
+    """Mirror of ``ir_prefill_shape``."""
+
+    _fields_ = [
+        ("num_seqs", c_int),
+        ("total_q", c_int),
+        ("num_heads", c_int),
+        ("num_kv_heads", c_int),
+        ("head_dim", c_int),
+        ("block_size", c_int),
+        ("max_blocks", c_int),
+        ("bt_stride", c_int64),
+        ("q_stride", c_int64),
+        ("out_stride", c_int64),
+        ("num_slots", c_int64),
+        ("scale", c_float),
+        ("dtype", c_int),
+    ]
+
+
 # (name, restype, argtypes) of every exported function
 _SIGNATURES = {
+    "ir_set_prefill_path": (c_int, [c_int]),
+    "ir_paged_prefill_plan": (c_int, [POINTER(PrefillShape), POINTER(c_int)]),
+    "ir_paged_prefill_workspace_size": (c_size_t, [POINTER(PrefillShape)]),
+    "ir_paged_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, POINTER(PrefillShape), c_void_p, c_size_t, c_void_p,
+                                 c_void_p]),
     "ir_version": (c_int, []),
     "ir_last_error": (c_char_p, []),
     "ir_deverr_name": (c_char_p, [c_int]),

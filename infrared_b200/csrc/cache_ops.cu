@@ -151,6 +151,49 @@ __global__ void build_decode_inputs_kernel(const int32_t* __restrict__ bt, int64
         static_cast<uint16_t>(valid ? 0u : min_bits);
 }
 
+// Per query row of a packed prefill: the row's sequence (largest s with
+// q_start[s] <= t), its context (position + 1) and a copy of the sequence's
+// block-table row, so that every row can be decoded as its own sequence.
+__global__ void prefill_rows_kernel(const int32_t* __restrict__ bt, int64_t bt_stride,
+                                    const int32_t* __restrict__ ctx,
+                                    const int32_t* __restrict__ q_start, int S, int max_blocks,
+                                    int max_ctx, int32_t* __restrict__ row_bt,
+                                    int32_t* __restrict__ row_ctx, int32_t* err) {
+  const int t = blockIdx.x;
+  __shared__ int s_seq;
+  if (threadIdx.x == 0) {
+    int lo = 0, hi = S - 1, found = -1;
+    while (lo <= hi) {
+      const int mid = (lo + hi) >> 1;
+      if (q_start[mid] <= t) {
+        found = mid;
+        lo = mid + 1;
+      } else {
+        hi = mid - 1;
+      }
+    }
+    int c = 0;
+    if (found >= 0 && t < q_start[found + 1]) {
+      const int ql = q_start[found + 1] - q_start[found];
+      const int cs = ctx[found];
+      if (cs < ql || cs > max_ctx) {
+        set_err(err, IR_DEVERR_CONTEXT_LEN);
+      } else {
+        c = cs - ql + (t - q_start[found]) + 1;
+      }
+    } else {
+      found = -1;
+    }
+    row_ctx[t] = c;
+    s_seq = found;
+  }
+  __syncthreads();
+  const int sq = s_seq;
+  for (int j = threadIdx.x; j < max_blocks; j += blockDim.x)
+    row_bt[static_cast<int64_t>(t) * max_blocks + j] =
+        sq >= 0 ? bt[static_cast<int64_t>(sq) * bt_stride + j] : 0;
+}
+
 int grid_for(int64_t work, int threads) {
   return static_cast<int>((work + threads - 1) / threads);
 }
@@ -229,6 +272,15 @@ int launch_build_decode_inputs(const int32_t* bt, int64_t bt_stride,
                                                        batch, t_max, bs, ids, positions,
                                                        write_slots, gather_slots, mask,
                                                        mask_bytes, min_bits);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_prefill_rows(const int32_t* bt, int64_t bt_stride, const int32_t* ctx,
+                        const int32_t* q_start, int S, int total_q, int max_blocks, int max_ctx,
+                        int32_t* row_bt, int32_t* row_ctx, int32_t* err, cudaStream_t stream) {
+  if (total_q == 0) return 0;
+  prefill_rows_kernel<<<total_q, 128, 0, stream>>>(bt, bt_stride, ctx, q_start, S, max_blocks,
+                                                   max_ctx, row_bt, row_ctx, err);
   return static_cast<int>(cudaGetLastError());
 }
 

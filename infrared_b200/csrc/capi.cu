@@ -361,6 +361,92 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
   return cuda_status(e, "merge kernel launch");
 }
 
+// ------------------------------------------------------------ prefill
+
+int g_prefill_path = 0;  // 0 auto, 1 rows as decode rows, 2 tensor cores
+
+bool make_q_map(CUtensorMap* map, const void* q, int total_q, int h, int d, int64_t q_stride,
+                int dtype) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(h),
+                              static_cast<cuuint64_t>(total_q)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2,
+                                 static_cast<cuuint64_t>(q_stride) * 2};
+  const cuuint32_t box[3] = {64, 1, 128};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt = dtype == IR_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(q), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int check_prefill_shape(const ir_prefill_shape* s) {
+  if (!s) return fail(IR_ERR_INVALID_ARG, "shape is null");
+  if (s->num_seqs < 0 || s->total_q < 0) return fail(IR_ERR_INVALID_ARG, "negative size");
+  if (s->num_heads <= 0 || s->num_kv_heads <= 0 || s->num_heads % s->num_kv_heads != 0)
+    return fail(IR_ERR_INVALID_ARG, "num_heads must be a positive multiple of num_kv_heads");
+  if (s->head_dim != 64 && s->head_dim != 128)
+    return fail(IR_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (s->block_size <= 0 || s->max_blocks < 0 || s->num_slots < 0)
+    return fail(IR_ERR_INVALID_ARG, "bad block_size / max_blocks / num_slots");
+  if (s->bt_stride < s->max_blocks) return fail(IR_ERR_INVALID_ARG, "bt_stride < max_blocks");
+  const int64_t row = static_cast<int64_t>(s->num_heads) * s->head_dim;
+  if (s->q_stride < row || s->out_stride < row)
+    return fail(IR_ERR_INVALID_ARG, "q_stride / out_stride < num_heads * head_dim");
+  if (elem_bytes(s->dtype) == 0) return fail(IR_ERR_INVALID_ARG, "unknown dtype");
+  if (static_cast<int64_t>(s->max_blocks) * s->block_size > INT32_MAX)
+    return fail(IR_ERR_INVALID_ARG, "max_blocks * block_size exceeds int32");
+  return IR_OK;
+}
+
+// The tensor-core kernel takes 16-bit dtypes, head_dim 64/128, power-of-two
+// block sizes >= 8 and slot counts addressable by int32 copy coordinates.
+bool prefill_tc_eligible(const ir_prefill_shape* s) {
+  const int bs = s->block_size;
+  return (s->dtype == IR_DTYPE_BF16 || s->dtype == IR_DTYPE_F16) && bs >= 8 &&
+         (bs & (bs - 1)) == 0 && s->num_slots < INT32_MAX && (s->q_stride * 2) % 16 == 0 &&
+         (s->out_stride * 2) % 16 == 0;
+}
+
+int prefill_path(const ir_prefill_shape* s) {
+  if (g_prefill_path == 1) return 1;
+  if (g_prefill_path == 2) return prefill_tc_eligible(s) ? 2 : -1;
+  return prefill_tc_eligible(s) ? 2 : 1;
+}
+
+// Workspace of the rows-as-decode path: per-row tables and contexts, then
+// the decode workspace of a batch of total_q rows.
+ir_decode_shape rows_shape(const ir_prefill_shape* s) {
+  ir_decode_shape d{};
+  d.batch = s->total_q;
+  d.num_heads = s->num_heads;
+  d.num_kv_heads = s->num_kv_heads;
+  d.head_dim = s->head_dim;
+  d.block_size = s->block_size;
+  d.max_blocks = s->max_blocks;
+  d.bt_stride = s->max_blocks;
+  d.q_stride = s->q_stride;
+  d.out_stride = s->out_stride;
+  d.num_slots = s->num_slots;
+  d.scale = s->scale;
+  d.dtype = s->dtype;
+  return d;
+}
+
+int prefill_rows_bytes(const ir_prefill_shape* s, size_t* tables, size_t* ctx, size_t* total) {
+  ir_decode_shape d = rows_shape(s);
+  Plan plan;
+  int rc = make_plan(&d, &plan);
+  if (rc) return rc;
+  *tables = align256(static_cast<size_t>(s->total_q) * s->max_blocks * 4);
+  *ctx = align256(static_cast<size_t>(s->total_q) * 4);
+  *total = *tables + *ctx + plan.bytes;
+  return IR_OK;
+}
+
 // Scratch of ir_paged_decode_noalloc: part of the library image, so the
 // entry point allocates nothing. Host code must not pass the symbol itself
 // to a kernel (on the host it names a host-side shadow, not device memory);
@@ -623,6 +709,102 @@ int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
                                 lse_part_stride, num_parts, batch, num_heads, head_dim,
                                 dtype, stream);
   return cuda_status(e, "lse merge launch");
+}
+
+int ir_set_prefill_path(int path) {
+  if (path < 0 || path > 2) return fail(IR_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_prefill_path = path;
+  return IR_OK;
+}
+
+int ir_paged_prefill_plan(const ir_prefill_shape* shape, int* path) {
+  int rc = check_prefill_shape(shape);
+  if (rc) return rc;
+  const int p = prefill_path(shape);
+  if (p < 0) return fail(IR_ERR_UNSUPPORTED, "tensor-core prefill forced but shape not eligible");
+  if (path) *path = p;
+  return IR_OK;
+}
+
+size_t ir_paged_prefill_workspace_size(const ir_prefill_shape* shape) {
+  if (check_prefill_shape(shape)) return 0;
+  if (prefill_path(shape) != 1) return 0;
+  size_t t, c, total;
+  if (prefill_rows_bytes(shape, &t, &c, &total)) return 0;
+  return total;
+}
+
+int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v_pool,
+                     const int32_t* block_tables, const int32_t* context_lens,
+                     const int32_t* q_start, const ir_prefill_shape* s, void* workspace,
+                     size_t workspace_bytes, int32_t* err_flag, ir_stream_t stream) {
+  int rc = check_prefill_shape(s);
+  if (rc) return rc;
+  if (s->num_seqs == 0 || s->total_q == 0) return IR_OK;
+  if (!out || !q || !k_pool || !v_pool || !context_lens || !q_start ||
+      (s->max_blocks > 0 && !block_tables))
+    return fail(IR_ERR_INVALID_ARG, "null pointer");
+  int path = prefill_path(s);
+  if (path < 0) return fail(IR_ERR_UNSUPPORTED, "tensor-core prefill forced but shape not eligible");
+  if (path == 2 && !(aligned(q, 16) && aligned(out, 16) && aligned(k_pool, 16) &&
+                     aligned(v_pool, 16))) {
+    if (g_prefill_path == 2)
+      return fail(IR_ERR_UNSUPPORTED, "tensor-core prefill forced but pointers misaligned");
+    path = 1;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (path == 2) {
+    irb::PrefillArgs a{};
+    a.q = q;
+    a.q_stride = s->q_stride;
+    a.out = out;
+    a.out_stride = s->out_stride;
+    a.block_tables = block_tables;
+    a.bt_stride = s->bt_stride;
+    a.context_lens = context_lens;
+    a.q_start = q_start;
+    a.S = s->num_seqs;
+    a.total_q = s->total_q;
+    a.H = s->num_heads;
+    a.Hkv = s->num_kv_heads;
+    a.n_rep = s->num_heads / s->num_kv_heads;
+    a.D = s->head_dim;
+    a.bs = s->block_size;
+    a.max_blocks = s->max_blocks;
+    a.num_slots = s->num_slots;
+    a.num_blocks = s->num_slots / s->block_size;
+    a.scale_log2 = s->scale * irb::kLog2e;
+    a.err = err_flag;
+    CUtensorMap tmq, tmk, tmv;
+    const int rows = s->block_size < 128 ? s->block_size : 128;
+    if (!make_q_map(&tmq, q, s->total_q, s->num_heads, s->head_dim, s->q_stride, s->dtype) ||
+        !make_pool_map(&tmk, k_pool, s->num_slots, s->num_kv_heads, s->head_dim, s->dtype,
+                       rows) ||
+        !make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads, s->head_dim, s->dtype,
+                       rows))
+      return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    int e = irb::launch_prefill_tc(tmq, tmk, tmv, a, s->dtype, st);
+    return cuda_status(e, "prefill kernel launch");
+  }
+  // rows as decode rows: each query row is a sequence of context position + 1
+  size_t tb, cb, total;
+  rc = prefill_rows_bytes(s, &tb, &cb, &total);
+  if (rc) return rc;
+  if (!workspace || workspace_bytes < total)
+    return fail(IR_ERR_WORKSPACE, "workspace smaller than ir_paged_prefill_workspace_size");
+  if (!aligned(workspace, 256)) return fail(IR_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* row_bt = reinterpret_cast<int32_t*>(ws);
+  int32_t* row_ctx = reinterpret_cast<int32_t*>(ws + tb);
+  int e = irb::launch_prefill_rows(block_tables, s->bt_stride, context_lens, q_start, s->num_seqs,
+                                   s->total_q, s->max_blocks, s->max_blocks * s->block_size,
+                                   row_bt, row_ctx, err_flag, st);
+  if (e) return cuda_status(e, "prefill row tables");
+  ir_decode_shape d = rows_shape(s);
+  return decode_impl(Mode::kFinal, out, nullptr, nullptr, q, k_pool, v_pool, nullptr, nullptr, 0,
+                     nullptr, row_bt, row_ctx, &d, ws + tb + cb, workspace_bytes - tb - cb,
+                     err_flag, st);
 }
 
 }  // extern "C"

@@ -10,6 +10,29 @@ namespace irb {
 
 struct DecodeArgs;
 
+// Packed-query paged prefill (prefill_tc.cu): sequence s owns query rows
+// [q_start[s], q_start[s+1]) = its last q_len positions of context_lens[s].
+struct PrefillArgs {
+  const void* q;  // [total_q, H, D] rows with row stride q_stride
+  int64_t q_stride;
+  void* out;  // same layout, out_stride
+  int64_t out_stride;
+  const int32_t* block_tables;  // [S, max_blocks] with bt_stride
+  int64_t bt_stride;
+  const int32_t* context_lens;  // [S]
+  const int32_t* q_start;       // [S + 1]
+  int S, total_q, H, Hkv, n_rep, D, bs, max_blocks;
+  int64_t num_slots, num_blocks;
+  float scale_log2;
+  int32_t* err;
+};
+
+// tcgen05 kernel: 16-bit dtypes, D in {64, 128}, block size a power of two
+// >= 8; tmq views q as (D, H, total_q), tmk/tmv the pools as (D, Hkv, slots)
+// with boxes {64, 1, 128} and {64, 1, min(bs, 128)} (128-byte swizzle).
+int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                      const PrefillArgs& a, int dtype, cudaStream_t stream);
+
 // decode_tma.cu: 16-bit pools, D in {64, 128}, group <= 8, bs == 8 or bs % 16 == 0.
 // One CTA covers tma_head_group(Hkv) kv heads; one_box selects the 4-D
 // (one copy per tile side) or the 3-D (one copy per head and half) map.
@@ -47,6 +70,9 @@ int launch_build_decode_inputs(const int32_t* bt, int64_t bt_stride,
                                int64_t* positions, int64_t* write_slots,
                                int64_t* gather_slots, void* mask, int mask_bytes,
                                uint32_t min_bits, cudaStream_t stream);
+int launch_prefill_rows(const int32_t* bt, int64_t bt_stride, const int32_t* ctx,
+                        const int32_t* q_start, int S, int total_q, int max_blocks, int max_ctx,
+                        int32_t* row_bt, int32_t* row_ctx, int32_t* err, cudaStream_t stream);
 int launch_derive_metadata(const int64_t* gs, int64_t gs_stride,
                            const void* mask, int64_t mask_stride,
                            int mask_elem_bytes, int B, int64_t T, int bs,

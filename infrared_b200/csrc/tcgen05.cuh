@@ -1,0 +1,112 @@
+// Blackwell 5th-generation tensor-core helpers (tcgen05, sm_100a): tensor
+// memory allocation, shared-memory matrix descriptors, the single-thread
+// MMA issue, commit-to-mbarrier and tensor-memory loads.
+//
+// Conventions used by the kernels of this library:
+//  * one MMA shape family: kind::f16 (bf16 or fp16 operands, fp32
+//    accumulate), cta_group::1, M = 128 (D row m = TMEM lane m);
+//  * operand tiles in shared memory use the 128-byte swizzle: rows of 128 B
+//    (64 16-bit elements), 8-row atoms of 1024 B, atoms 1024-byte aligned —
+//    exactly the layout a TMA copy with CU_TENSOR_MAP_SWIZZLE_128B writes.
+#pragma once
+
+#include "common.cuh"
+
+namespace irb {
+namespace tc {
+
+// Shared-memory matrix descriptor (64 bit): start address, leading and
+// stride byte offsets (all >> 4), version 1 (sm_100), layout type
+// SWIZZLE_128B (2) in bits 61-63.
+//  K-major operand (rows = M or N, 64 K-elements per 128-B row):
+//    LBO = 16 B (unused by the swizzled layout), SBO = 1024 B between 8-row
+//    atoms; a K step of 16 elements inside an atom advances the start by 32 B.
+//  MN-major operand (rows = K, 64 MN-elements per 128-B row):
+//    LBO = bytes between consecutive 64-element MN chunks, SBO = 1024 B
+//    between 8-row (8 K) atoms.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes) {
+  uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation: A and B of
+// the same 16-bit type (bf16 = 1, fp16 = 0), A K-major, B K-major or
+// MN-major, shape M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16, bool b_mn_major) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] . B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Arrive (once) on `bar` when every MMA this thread issued so far completes.
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Tensor-memory allocation: executed by one whole warp; the base address is
+// written to `slot` in shared memory.
+__device__ __forceinline__ void alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp w reads lanes
+// 32 * (w % 4) .. + 31; the caller puts that lane offset into taddr). The
+// load and its wait sit in one asm statement, so no use of the registers can
+// be scheduled before the data has arrived.
+__device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+      "[%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace tc
+}  // namespace irb

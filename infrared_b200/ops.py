@@ -462,3 +462,89 @@ def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor,
         lse_parts.data_ptr(), lse_parts.stride(0), p, b, h, d, dtype_code(out.dtype),
         _stream(dev)))
     return out
+
+
+# --- prefill / mixed varlen (Sq > 1) ----------------------------------------
+
+
+def set_prefill_path(path: int) -> None:
+    """0 auto, 1 rows as decode rows, 2 the tcgen05 tensor-core kernel."""
+    check(_lib.load().ir_set_prefill_path(int(path)))
+
+
+def _prefill_shape(q, k_pool, block_tables, q_start, block_size, scale, out_stride):
+    t, h, d = q.shape
+    s = _lib.PrefillShape()
+    s.num_seqs = q_start.numel() - 1
+    s.total_q = t
+    s.num_heads = h
+    s.num_kv_heads = k_pool.shape[1]
+    s.head_dim = d
+    s.block_size = block_size
+    s.max_blocks = block_tables.shape[1]
+    s.bt_stride = block_tables.stride(0) if block_tables.shape[0] else block_tables.shape[1]
+    s.q_stride = q.stride(0) if t else h * d
+    s.out_stride = out_stride
+    s.num_slots = k_pool.shape[0]
+    s.scale = float(scale)
+    s.dtype = dtype_code(q.dtype)
+    return s
+
+
+def prefill_plan(q, k_pool, block_tables, q_start, block_size, scale=1.0):
+    """``(path, workspace_bytes)`` of :func:`paged_prefill` for these shapes."""
+    s = _prefill_shape(q, k_pool, block_tables, q_start, block_size, scale,
+                       q.shape[1] * q.shape[2])
+    lib = _lib.load()
+    path = _lib.c_int()
+    check(lib.ir_paged_prefill_plan(s, path))
+    return path.value, lib.ir_paged_prefill_workspace_size(s)
+
+
+def paged_prefill(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                  block_tables: torch.Tensor, context_lens: torch.Tensor,
+                  q_start: torch.Tensor, scale: float, block_size: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal paged attention of packed query rows ``q [total_q, H, D]``.
+
+    Sequence ``s`` owns rows ``q_start[s] .. q_start[s+1]-1``, its last
+    positions ``context_lens[s] - q_len .. context_lens[s] - 1`` (the pool
+    already holds this step's K/V); each row attends its own sequence up to
+    its position. ``block_tables`` int32 ``[S, max_blocks]``,
+    ``context_lens`` int32 ``[S]``, ``q_start`` int32 ``[S + 1]``.
+    """
+    _dev_index(q)
+    if q.dim() != 3 or q.stride(2) != 1 or q.stride(1) != q.shape[2]:
+        raise ValueError("q must be [total_q, H, D] with [H, D] contiguous rows")
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    if k_pool.shape != v_pool.shape or k_pool.dtype != q.dtype or v_pool.dtype != q.dtype:
+        raise ValueError("pools must match each other and q's dtype")
+    if k_pool.shape[2] != q.shape[2]:
+        raise ValueError("head_dim of q and pools differ")
+    for name, t, n in (("context_lens", context_lens, None), ("q_start", q_start, None)):
+        if t.dtype != torch.int32 or not t.is_contiguous() or t.device != q.device:
+            raise ValueError(f"{name} must be a contiguous int32 tensor on q's device")
+    if block_tables.dtype != torch.int32 or block_tables.dim() != 2 or \
+            (block_tables.numel() and block_tables.stride(1) != 1) or \
+            block_tables.device != q.device:
+        raise ValueError("block_tables must be int32 [S, max_blocks] with unit column stride")
+    nseq = q_start.numel() - 1
+    if nseq < 0 or block_tables.shape[0] != nseq or context_lens.numel() != nseq:
+        raise ValueError("q_start must have one more entry than block_tables / context_lens")
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
+            out.stride(1) != q.shape[2]:
+        raise ValueError("out must be [total_q, H, D] of q's dtype with contiguous rows")
+    dev = _dev_index(q)
+    s = _prefill_shape(q, k_pool, block_tables, q_start, block_size, scale,
+                       out.stride(0) if out.shape[0] else q.shape[1] * q.shape[2])
+    lib = _lib.load()
+    nbytes = lib.ir_paged_prefill_workspace_size(s)
+    ws = workspace(max(nbytes, 256), dev)
+    check(lib.ir_paged_prefill(out.data_ptr(), q.data_ptr(), k_pool.data_ptr(),
+                               v_pool.data_ptr(), block_tables.data_ptr(),
+                               context_lens.data_ptr(), q_start.data_ptr(), s, ws.data_ptr(),
+                               ws.numel(), error_flag(dev).data_ptr(), _stream(dev)))
+    return out

@@ -1,0 +1,163 @@
+"""Paged prefill / mixed varlen attention (ir_paged_prefill) against the oracle.
+
+Bars: fp32 within 1e-5 max-abs of the reference's own golden outputs; bf16 /
+fp16 within atol = rtol = 2e-2 of the fp32 oracle on the same rounded
+inputs, on both kernels (tcgen05 tensor cores and rows-as-decode).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from gpu_helpers import DEV, assert_close_bf16, host_f32
+import infrared_b200 as irb
+from infrared_b200 import ops
+from oracle import paged_attention_np as orc
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")]
+
+
+@pytest.fixture(autouse=True)
+def _clean_errors():
+    ops.set_prefill_path(0)
+    ops.error_flag().zero_()
+    yield
+    ops.set_prefill_path(0)
+    ops.check_device_errors()
+
+
+def _device_case(c, dtype):
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(DEV)  # noqa: E731
+    kp, vp = t(c["pool_k"]).to(dtype), t(c["pool_v"]).to(dtype)
+    ws = t(c["frame"]["write_slots"])
+    irb.cache_write(t(c["k"]).to(dtype), t(c["v"]).to(dtype), kp, vp, ws)
+    return (t(c["q"]).to(dtype), kp, vp, t(c["block_tables"]), t(c["context_lens"]),
+            t(c["q_start"]))
+
+
+@pytest.mark.parametrize("name", sorted(cases.PREFILL_CASES))
+def test_prefill_golden_fp32(golden, name):
+    c = cases.prefill_inputs(name)
+    q, kp, vp, bt, ctx, qs = _device_case(c, torch.float32)
+    assert ops.prefill_plan(q, kp, bt, qs, c["bs"])[0] == 1
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, c["scale"], c["bs"])
+    assert np.abs(host_f32(out) - golden[f"prefill/{name}/out"]).max() <= 1e-5
+
+
+@pytest.mark.parametrize("path", [2, 1])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("name", sorted(cases.PREFILL_CASES))
+def test_prefill_golden_half(name, dtype, path):
+    c = cases.prefill_inputs(name)
+    q, kp, vp, bt, ctx, qs = _device_case(c, dtype)
+    ops.set_prefill_path(path)
+    assert ops.prefill_plan(q, kp, bt, qs, c["bs"])[0] == path
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, c["scale"], c["bs"])
+    want = orc.prefill_from_tables(host_f32(q), host_f32(kp)[None], host_f32(vp)[None], 0,
+                                   c["block_tables"], c["context_lens"], c["q_start"], c["bs"],
+                                   c["scale"], c["n_rep"])
+    assert_close_bf16(host_f32(out), want)
+
+
+def _random_frame(seed, h, hkv, d, bs, chunks, dtype):
+    rng = np.random.default_rng(seed)
+    ctx = np.array([st + ql for st, ql in chunks], np.int32)
+    nblk = [-(-int(x) // bs) for x in ctx]
+    num_blocks = sum(nblk) + 3
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    bt = np.zeros((len(chunks), max(nblk)), np.int32)
+    off = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[off:off + n]
+        off += n
+    q_start = np.concatenate([[0], np.cumsum([ql for _, ql in chunks])]).astype(np.int32)
+    nq = int(q_start[-1])
+    q = torch.from_numpy(rng.standard_normal((nq, h, d), dtype=np.float32)).to(DEV).to(dtype)
+    kp = torch.from_numpy(rng.standard_normal((num_blocks * bs, hkv, d),
+                                              dtype=np.float32)).to(DEV).to(dtype)
+    vp = torch.from_numpy(rng.standard_normal((num_blocks * bs, hkv, d),
+                                              dtype=np.float32)).to(DEV).to(dtype)
+    return (q, kp, vp, torch.from_numpy(bt).to(DEV), torch.from_numpy(ctx).to(DEV),
+            torch.from_numpy(q_start).to(DEV), bt, ctx, q_start)
+
+
+SWEEP = [
+    # (H, Hkv, D, bs, [(cached, forwarded), ...])
+    (28, 4, 128, 16, [(0, 300), (17, 1), (500, 129), (0, 1), (64, 64)]),
+    (14, 2, 64, 16, [(0, 257), (3, 5), (128, 128)]),
+    (8, 8, 128, 32, [(10, 200), (0, 33)]),
+    (16, 2, 128, 8, [(100, 150), (1, 1), (0, 7)]),
+    (12, 4, 64, 64, [(0, 129), (250, 20)]),
+    (8, 1, 128, 128, [(130, 140), (0, 3)]),
+    (4, 4, 64, 256, [(300, 70)]),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("cfg", SWEEP)
+def test_prefill_sweep_tensor_cores(cfg, dtype):
+    h, hkv, d, bs, chunks = cfg
+    q, kp, vp, bt, ctx, qs, bt_np, ctx_np, qs_np = _random_frame(7 + h + d + bs, h, hkv, d, bs,
+                                                                 chunks, dtype)
+    assert ops.prefill_plan(q, kp, bt, qs, bs)[0] == 2
+    scale = d ** -0.5
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, scale, bs)
+    want = orc.prefill_from_tables(host_f32(q), host_f32(kp)[None], host_f32(vp)[None], 0,
+                                   bt_np, ctx_np, qs_np, bs, scale, h // hkv)
+    assert_close_bf16(host_f32(out), want)
+
+
+def test_prefill_long_prompt_rows_against_oracle():
+    """One 2048-token prompt at the Qwen2.5-7B geometry; rows spread over the
+    q tiles (incl. the diagonal tiles' first and last rows) vs the oracle."""
+    h, hkv, d, bs = 28, 4, 128, 16
+    q, kp, vp, bt, ctx, qs, bt_np, ctx_np, qs_np = _random_frame(5, h, hkv, d, bs, [(0, 2048)],
+                                                                 torch.bfloat16)
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, d ** -0.5, bs)
+    rows = [0, 1, 127, 128, 129, 1000, 1023, 1024, 2046, 2047]
+    qh = host_f32(q)
+    kh, vh = host_f32(kp)[None], host_f32(vp)[None]
+    for r in rows:
+        sub_q = qh[r:r + 1]
+        want = orc.prefill_from_tables(sub_q, kh, vh, 0, bt_np, np.array([r + 1], np.int32),
+                                       np.array([0, 1], np.int32), bs, d ** -0.5, h // hkv)
+        assert_close_bf16(host_f32(out[r:r + 1]), want)
+
+
+def test_prefill_paths_agree_and_are_deterministic():
+    h, hkv, d, bs = 28, 4, 128, 16
+    q, kp, vp, bt, ctx, qs, *_ = _random_frame(9, h, hkv, d, bs, [(40, 200), (0, 1), (3, 77)],
+                                               torch.bfloat16)
+    a = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.088, bs)
+    b = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.088, bs)
+    assert torch.equal(a, b)
+    ops.set_prefill_path(1)
+    c = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.088, bs)
+    assert (a.float() - c.float()).abs().max().item() < 2e-2
+
+
+def test_prefill_bad_context_is_flagged_not_faulted():
+    h, hkv, d, bs = 8, 2, 64, 16
+    q, kp, vp, bt, ctx, qs, *_ = _random_frame(3, h, hkv, d, bs, [(0, 40), (5, 10)],
+                                               torch.bfloat16)
+    bad = ctx.clone()
+    bad[0] = 20                       # shorter than its 40 query rows
+    irb.paged_prefill(q, kp, vp, bt, bad, qs, 0.125, bs)
+    with pytest.raises(ops.DeviceError, match="CONTEXT_LEN"):
+        ops.check_device_errors()
+    # the next call on the same context is fine
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.125, bs)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+
+
+def test_prefill_empty_frame():
+    q = torch.empty(0, 8, 64, device=DEV, dtype=torch.bfloat16)
+    kp = torch.zeros(64, 2, 64, device=DEV, dtype=torch.bfloat16)
+    bt = torch.zeros(0, 4, dtype=torch.int32, device=DEV)
+    ctx = torch.zeros(0, dtype=torch.int32, device=DEV)
+    qs = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = irb.paged_prefill(q, kp, kp, bt, ctx, qs, 0.125, 16)
+    assert out.shape == (0, 8, 64)
