@@ -2,13 +2,14 @@
 """Paged-decode attention throughput on B200 — one JSON line per run.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c2|c3|c4|c5]
+                    [--config c2|c3|c4|c5|p1]
 
 A step is one decode-attention call (one layer) over one batch of the
 workload: ``c2`` (default) is the Qwen2.5-7B geometry batch of 64 sequences
 with contexts U[512, 4096]; ``c3`` adds the fused K/V cache write over 256
 sequences with shared prefixes; ``c4`` is 4 x 32k contexts; ``c5`` is a
-whole greedy decode step of a random-init Qwen2.5-7B (tok/s). At N GPUs (one
+whole greedy decode step of a random-init Qwen2.5-7B (tok/s); ``p1`` is a
+causal prefill of 8 x 4096-token prompts (TFLOP/s, tcgen05). At N GPUs (one
 process per GPU, launched by torchrun) every rank decodes its own batch of
 the workload — the sequences are sharded, there is no collective on the data
 path — so the scaling is weak and ``value`` is the bytes all ranks moved
@@ -57,7 +58,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c2")
+    p.add_argument("--config", choices=["c2", "c3", "c4", "c5", "p1"], default="c2")
     p.add_argument("--sets", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -447,6 +448,9 @@ def run_reference(args):
                           "step; the reference's CPU path restated here is the attention path "
                           "(configs c2/c3/c4)"}), flush=True)
         return
+    if args.config == "p1":
+        run_reference_prefill(args)
+        return
     w = make_workload(args.config, 0)
     gbs, secs, n = time_cpu_oracle(w, steps=args.steps, warmup=args.warmup)
     per_step = secs / max(n, 1)
@@ -471,6 +475,52 @@ def run_reference(args):
                          "sample": "reference naive CPU path restated in oracle/ (numpy): "
                                    "one sequence of the workload per step"},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_prefill(args):
+    """The reference's naive CPU path for a prefill (gather, repeat_kv, causal
+    masked attention; restated in oracle/) on one 512-token prompt of the P1
+    geometry per step, timed on the host cores."""
+    import torch
+
+    from infrared_b200 import workloads as wl
+    from oracle import paged_attention_np as orc
+
+    w = wl.prefill_frame("p1-sample", 0, [0], [512])
+    rng = np.random.default_rng(0)
+    slots = w.num_blocks * w.block_size
+    kp = (rng.standard_normal((1, slots, w.num_kv_heads, w.head_dim), np.float32) * 0.5)
+    vp = (rng.standard_normal((1, slots, w.num_kv_heads, w.head_dim), np.float32) * 0.5)
+    q = rng.standard_normal((w.total_q, w.num_heads, w.head_dim), np.float32) * 0.5
+    torch.set_num_threads(cpu_threads())
+
+    def one():
+        orc.prefill_from_tables(q, kp, vp, 0, w.block_tables, w.context_lens, w.q_start,
+                                w.block_size, w.scale, w.num_heads // w.num_kv_heads)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        one()
+    n, t0 = 0, time.perf_counter()
+    while n < max(args.steps, 1) and time.perf_counter() - t0 < 20.0:
+        one()
+        n += 1
+    secs = time.perf_counter() - t0
+    tflops = w.flops() * n / secs / 1e12
+    line = {
+        "impl": "reference", "metric": "paged prefill attention TFLOP/s (causal, useful FLOPs)",
+        "value": round(tflops, 5), "unit": "TFLOP/s", "n_gpus": 1, "steps": n,
+        "warmup": args.warmup, "ms_per_step": round(secs / n * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (P1 geometry)",
+        "config": {"workload": "P1 geometry, one 512-token prompt per step (bounded sample)"},
+        "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOP/s", "cores": cpu_threads(),
+                         "kind": "port",
+                         "sample": "reference naive CPU prefill restated in oracle/ (numpy): "
+                                   "one 512-token prompt, 28 heads, per step"},
+        "e2e": {"value": round(tflops, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -705,12 +755,125 @@ def run_model(args):
         print(json.dumps(line), flush=True)
 
 
+def run_prefill(args):
+    """P1: causal prefill of 8 x 4096-token prompts at the Qwen2.5-7B attention
+    geometry on the tcgen05 kernel (one launch per step); TFLOP/s of useful
+    (causal) FLOPs against the measured bf16 dense peak. Every rank runs its
+    own prompts (weak scaling, no collective)."""
+    import torch
+    import torch.distributed as dist
+
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import ops
+    from infrared_b200 import workloads as wl
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    w = wl.p1(seed=rank, batch=args.batch or 8)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    slots = w.num_blocks * w.block_size
+    kp = (torch.randn(slots, w.num_kv_heads, w.head_dim, generator=g, device=dev) * 0.5
+          ).to(torch.bfloat16)
+    vp = (torch.randn(slots, w.num_kv_heads, w.head_dim, generator=g, device=dev) * 0.5
+          ).to(torch.bfloat16)
+    q = (torch.randn(w.total_q, w.num_heads, w.head_dim, generator=g, device=dev) * 0.5
+         ).to(torch.bfloat16)
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    ctx = torch.from_numpy(w.context_lens).to(dev)
+    qs = torch.from_numpy(w.q_start).to(dev)
+    out = torch.empty_like(q)
+    ops.set_prefill_path(args.decode_path if args.decode_path in (1, 2) else 0)
+    path, _ = ops.prefill_plan(q, kp, bt, qs, w.block_size, w.scale)
+    flops = w.flops()
+
+    def step():
+        ops.paged_prefill(q, kp, vp, bt, ctx, qs, w.scale, w.block_size, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    clocks = ClockSampler(local)
+    ev[0].record()
+    for _ in range(args.steps):
+        step()
+    ev[1].record()
+    ev[1].synchronize()
+    clk = clocks.stop()
+    ms = ev[0].elapsed_time(ev[1])
+    ms_job = irdist.max_over_ranks(ms, device=dev) if world > 1 else ms
+    ops.check_device_errors(dev)
+    # e2e: q from pinned host memory in, the output back, every step
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    q_dev = torch.empty_like(q)
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        q_dev.copy_(q_host, non_blocking=True)
+        ops.paged_prefill(q_dev, kp, vp, bt, ctx, qs, w.scale, w.block_size, out=out)
+        out_host.copy_(out, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    ev[0].record()
+    for _ in range(e2e_steps):
+        q_dev.copy_(q_host, non_blocking=True)
+        ops.paged_prefill(q_dev, kp, vp, bt, ctx, qs, w.scale, w.block_size, out=out)
+        out_host.copy_(out, non_blocking=True)
+    ev[1].record()
+    ev[1].synchronize()
+    e2e_ms = ev[0].elapsed_time(ev[1])
+    e2e_ms = irdist.max_over_ranks(e2e_ms, device=dev) if world > 1 else e2e_ms
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    per_step = ms_job / args.steps
+    tflops = flops / (ms / args.steps / 1e3) / 1e12
+    line = {
+        "metric": "paged prefill attention TFLOP/s (causal, useful FLOPs)",
+        "value": round(flops * world / (per_step / 1e3) / 1e12, 1), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1)*0.5 q/K/V, random block tables",
+        "config": {"workload": f"P1: {len(w.q_lens)} prompts x {int(w.q_lens[0])} tokens, "
+                               "Qwen2.5-7B attention (28 q / 4 kv heads, head_dim 128), "
+                               "block 16, causal",
+                   "total_q_rows": w.total_q, "flops_per_step": flops,
+                   "kernel_path": {1: "rows as decode rows", 2: "tcgen05"}[path],
+                   "l2": "q + out = 470 MB per step, larger than L2",
+                   "timing": "K back-to-back launches, CUDA events, max over ranks"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
+                     "peak_kind": "measured" if peaks else "fallback", "traffic": None,
+                     "scope": "one prefill launch, per GPU"},
+        "e2e": {"value": round(flops * world / (e2e_ms / e2e_steps / 1e3) / 1e12, 1),
+                "unit": "TFLOP/s", "h2d_bytes_per_step": q.numel() * 2,
+                "d2h_bytes_per_step": out.numel() * 2,
+                "ms_per_step": round(e2e_ms / e2e_steps, 4)},
+        "clocks": clk,
+        "gpu_launches": args.steps,
+    }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.config == "c5":
         run_model(args)
+    elif args.config == "p1":
+        run_prefill(args)
     elif args.config == "c4" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_chunked(args)
     else:

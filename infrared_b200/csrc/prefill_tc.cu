@@ -9,19 +9,23 @@
 // One CTA = 128 query rows of one sequence for one query head (grid:
 // q tiles x heads). Six warps:
 //   warp 4      producer: TMA copies of the Q tile (once) and of each
-//               128-key K tile and V tile (one 16-row box per 16-slot block
-//               and 64-column half) into rings of NS stages;
+//               128-key K tile and V tile (one box per block and 64-column
+//               half; block-table lookups spread over the warp's lanes and
+//               done one tile ahead) into rings of NS stages;
 //   warp 5      MMA issuer (one thread): S = Q.K^T (M=128, N=128 keys,
-//               K=D) into one of two TMEM buffers, then O_tile = P.V
-//               (M=128, N=D, K=128 keys) into a third, tcgen05.mma
+//               K=D) into one of two TMEM buffers, and O += P.V (M=128,
+//               N=D, K=128 keys) into the TMEM accumulator, tcgen05.mma
 //               kind::f16 with operands in 128-byte-swizzled shared memory;
 //               tcgen05.commit releases stages and signals the softmax;
-//   warps 0-3   softmax (thread r = query row r = TMEM lane r): row max of
-//               the masked scores, exp2 probabilities written as 16-bit P
-//               into shared memory (the A operand of the P.V MMA), running
-//               sum, and the fp32 output accumulated in registers from each
-//               tile's O_tile (rescaled when the row max grows).
-// The QK^T MMA of tile j+1 runs while the softmax works on tile j.
+//   warps 0-3   softmax (thread r = query row r = TMEM lane r): one
+//               128-column TMEM load of the row's scores, masked row max,
+//               exp2 probabilities written as 16-bit P into one of two
+//               shared-memory buffers (the A operand of the P.V MMA) and
+//               their running sum. P is taken relative to a reference max
+//               that moves only when the row max grows by more than 2^8
+//               (then the row of O in TMEM and the sum are rescaled), so
+//               the accumulator is rarely touched and the P.V MMA of tile j
+//               overlaps the softmax of tile j + 1.
 // Every wait is bounded (2 s); on a timeout the CTA flags IR_DEVERR_TIMEOUT,
 // lets its copies and MMAs drain (bounded), frees its tensor memory and ends.
 #include "tcgen05.cuh"
@@ -35,7 +39,8 @@ constexpr int kRows = 128;     // query rows per CTA (MMA M)
 constexpr int kKeys = 128;     // keys per K/V tile
 constexpr int kThreads = 192;  // warps 0-3 softmax, 4 producer, 5 MMA
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128, O_tile at 256
+constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128, O at 256
+constexpr float kRescaleLog2 = 8.f;  // move the reference max when it grows by > 2^8
 
 template <int D>
 struct PLayout {
@@ -44,15 +49,15 @@ struct PLayout {
   static constexpr int kQ = kHalves * kHalf;             // Q tile
   static constexpr int kSide = kHalves * kKeys * 128;    // one K or V tile
   static constexpr int NS = D == 128 ? 2 : 4;            // stages per ring
+  static constexpr int kP = 2 * kHalf;                   // P: 2 halves x 128 rows x 128 B
   static constexpr int off_q = 0;
   static constexpr int off_k = kQ;
   static constexpr int off_v = off_k + NS * kSide;
-  static constexpr int off_p = off_v + NS * kSide;       // P: 2 halves x 128 rows x 128 B
-  static constexpr int kP = 2 * kHalf;
-  static constexpr int off_bar = off_p + kP;
+  static constexpr int off_p = off_v + NS * kSide;       // two P buffers
+  static constexpr int off_bar = off_p + 2 * kP;
   // q_full, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[2], s_free[2],
-  // p_full, o_full, o_free, drain
-  static constexpr int kBars = 1 + 4 * NS + 8;
+  // p_full[2], p_done[2], drain
+  static constexpr int kBars = 1 + 4 * NS + 9;
   static constexpr int off_misc = off_bar + kBars * 8;
   static constexpr int kBytes = off_misc + 64;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
@@ -105,12 +110,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = k_full + NS;
   uint64_t* v_full = k_empty + NS;
   uint64_t* v_empty = v_full + NS;
-  uint64_t* s_full = v_empty + NS;  // [2]
-  uint64_t* s_free = s_full + 2;    // [2]
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_full = p_full + 1;
-  uint64_t* o_free = o_full + 1;
-  uint64_t* drain = o_free + 1;
+  uint64_t* s_full = v_empty + NS;  // [2] S buffer b holds tile j (j % 2 == b)
+  uint64_t* s_free = s_full + 2;    // [2] the softmax has read S buffer b
+  uint64_t* p_full = s_free + 2;    // [2] P buffer b written (and O rescaled)
+  uint64_t* p_done = p_full + 2;    // [2] the P.V MMA reading P buffer b completed
+  uint64_t* drain = p_done + 2;
   int* misc = reinterpret_cast<int*>(smem + L::off_misc);  // seq, tile, tmem base
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y;
@@ -134,10 +138,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kRows);
+      mbar_init(&p_full[i], kRows);
+      mbar_init(&p_done[i], 1);
     }
-    mbar_init(p_full, kRows);
-    mbar_init(o_full, 1);
-    mbar_init(o_free, kRows);
     mbar_init(drain, 1);
     fence_mbar_init();
   }
@@ -172,63 +175,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     // ---------------------------------------------------------- producer
+    // Lane i < nbox resolves box i of a tile (block-table lookup) one tile
+    // ahead, so the lookups of tile j + 1 overlap the waits of tile j, and
+    // issues that box's copies itself.
+    bool ok = true;
     if (lane == 0) {
-      bool ok = true;
       mbar_arrive_expect_tx(q_full, L::kQ);
 #pragma unroll
       for (int hf = 0; hf < L::kHalves; ++hf)
         tma_load_3d(smem + L::off_q + hf * L::kHalf, &tmq, q_full, 64 * hf, h, r0);
-      const int R = a.bs < kKeys ? a.bs : kKeys;  // rows per box
-      const int nbox = kKeys / R;
-      const int32_t* btr = a.block_tables + static_cast<int64_t>(s) * a.bt_stride;
-      const int oob = static_cast<int>(a.num_slots);  // zero-filled by the copy
-      int issued = 0;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j % NS;
-        const uint32_t par = ((j / NS) & 1) ^ 1;
-        // rows of the tile's blocks (out-of-range coordinates read zeros)
-        auto row_of = [&](int i) {
-          const int key0 = j * kKeys + i * R;
-          if (key0 >= ctx) return oob;
-          const int id = btr[key0 / a.bs];
-          if (id < 0 || id >= a.num_blocks) {
-            set_err(a.err, IR_DEVERR_BLOCK_ID);
-            return oob;
-          }
-          return id * a.bs + key0 % a.bs;
-        };
-        if (!mbar_wait_bounded(&k_empty[st], par)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&k_full[st], L::kSide);
-        uint8_t* kd = smem + L::off_k + st * L::kSide;
-        for (int i = 0; i < nbox; ++i) {
-          const int row = row_of(i);
-#pragma unroll
-          for (int hf = 0; hf < L::kHalves; ++hf)
-            tma_load_3d(kd + hf * (kKeys * 128) + i * R * 128, &tmk, &k_full[st], 64 * hf, kvh,
-                        row);
-        }
-        if (!mbar_wait_bounded(&v_empty[st], par)) {
-          ok = false;
-          // the K copies of this tile are in flight: count it as issued
-          issued = j + 1;
-          break;
-        }
-        mbar_arrive_expect_tx(&v_full[st], L::kSide);
-        uint8_t* vd = smem + L::off_v + st * L::kSide;
-        for (int i = 0; i < nbox; ++i) {
-          const int row = row_of(i);
-#pragma unroll
-          for (int hf = 0; hf < L::kHalves; ++hf)
-            tma_load_3d(vd + hf * (kKeys * 128) + i * R * 128, &tmv, &v_full[st], 64 * hf, kvh,
-                        row);
-        }
-        issued = j + 1;
+    }
+    const int R = a.bs < kKeys ? a.bs : kKeys;  // rows per box
+    const int nbox = kKeys / R;                 // <= 16
+    const int32_t* btr = a.block_tables + static_cast<int64_t>(s) * a.bt_stride;
+    const int oob = static_cast<int>(a.num_slots);  // read as zeros by the copy
+    auto row_of = [&](int j) {
+      if (lane >= nbox || j >= n_kv) return oob;
+      const int key0 = j * kKeys + lane * R;
+      if (key0 >= ctx) return oob;
+      const int id = btr[key0 / a.bs];
+      if (id < 0 || id >= a.num_blocks) {
+        set_err(a.err, IR_DEVERR_BLOCK_ID);
+        return oob;
       }
+      return id * a.bs + key0 % a.bs;
+    };
+    int row_cur = row_of(0);
+    int issued = 0;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      const int row_next = row_of(j + 1);
+      const int st = j % NS;
+      const uint32_t par = ((j / NS) & 1) ^ 1;
+      int w = 1;
+      if (lane == 0) w = mbar_wait_bounded(&k_empty[st], par) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, w, 0)) {
+        ok = false;
+        break;
+      }
+      uint8_t* kd = smem + L::off_k + st * L::kSide;
+      uint8_t* vd = smem + L::off_v + st * L::kSide;
+      // lane i issues the copies of box i (the expected bytes are posted first)
+      if (lane == 0) mbar_arrive_expect_tx(&k_full[st], L::kSide);
+      __syncwarp();
+      if (lane < nbox) {
+#pragma unroll
+        for (int hf = 0; hf < L::kHalves; ++hf)
+          tma_load_3d(kd + hf * (kKeys * 128) + lane * R * 128, &tmk, &k_full[st], 64 * hf,
+                      kvh, row_cur);
+      }
+      issued = j + 1;  // K copies of tile j are in flight from here on
+      if (lane == 0) w = mbar_wait_bounded(&v_empty[st], par) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, w, 0)) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&v_full[st], L::kSide);
+      __syncwarp();
+      if (lane < nbox) {
+#pragma unroll
+        for (int hf = 0; hf < L::kHalves; ++hf)
+          tma_load_3d(vd + hf * (kKeys * 128) + lane * R * 128, &tmv, &v_full[st], 64 * hf,
+                      kvh, row_cur);
+      }
+      row_cur = row_next;
+    }
+    if (lane == 0) {
       if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
-      // no copy may still be writing when the CTA ends
+      // no copy may still be writing when the CTA ends: the V copies of the
+      // last tile exist only if the loop completed it
       mbar_wait_bounded(q_full, 0);
       for (int j = issued > NS ? issued - NS : 0; j < issued; ++j) {
         mbar_wait_bounded(&k_full[j % NS], (j / NS) & 1);
@@ -261,19 +275,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int st = j % NS;
+        const int st = j % NS, b = j & 1;
         if (!mbar_wait_bounded(&v_full[st], (j / NS) & 1)) return false;
-        if (!mbar_wait_bounded(p_full, j & 1)) return false;
-        if (!mbar_wait_bounded(o_free, (j & 1) ^ 1)) return false;
+        if (!mbar_wait_bounded(&p_full[b], (j >> 1) & 1)) return false;
         tc::fence_after_sync();
         const uint32_t vb = smem_u32(smem + L::off_v + st * L::kSide);
+        const uint32_t pbb = pb + b * L::kP;
 #pragma unroll
         for (int k = 0; k < kKeys / 16; ++k) {
           const uint32_t po = (k >> 2) * L::kHalf + (k & 3) * 32;
-          tc::mma_f16_ss(tmem + kColO, tc::sw128_desc(pb + po, 16, 1024),
-                         tc::sw128_desc(vb + k * 2048, kKeys * 128, 1024), kIdO, k > 0);
+          tc::mma_f16_ss(tmem + kColO, tc::sw128_desc(pbb + po, 16, 1024),
+                         tc::sw128_desc(vb + k * 2048, kKeys * 128, 1024), kIdO,
+                         j > 0 || k > 0);
         }
-        tc::commit(o_full);
+        tc::commit(&p_done[b]);
         tc::commit(&v_empty[st]);
         return true;
       };
@@ -293,63 +308,65 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const int pos = pos0 + r;
     const int lim = min(pos, ctx - 1);  // last key this row may attend
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    float m_ref = -INFINITY;  // reference max of the P values (log2 units)
+    float l = 0.f;
     bool ok = true;
-    uint8_t* prow = smem + L::off_p + (r >> 3) * 1024 + (r & 7) * 128;
+    // tcgen05.ld / st are warp-collective: every wait result is made warp-uniform
+    auto wait_all = [&](uint64_t* bar, uint32_t par) {
+      return __all_sync(0xffffffffu, mbar_wait_bounded(bar, par));
+    };
     for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
+      const int b = j & 1;
       const int kbase = j * kKeys;
-      // tcgen05.ld is warp-collective: a warp leaves the loop as a whole
-      if (!__all_sync(0xffffffffu, mbar_wait_bounded(&s_full[sb], (j >> 1) & 1))) {
+      if (!wait_all(&s_full[b], (j >> 1) & 1)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
-      float mx = -INFINITY;
+      float v[kKeys];
+      tc::ld128(lane_addr + b * kKeys, v);
+      tc::fence_before_sync();
+      mbar_arrive(&s_free[b]);
+      // keys past this row's limit exist only in the last one or two tiles
+      // (the diagonal); mask them to -inf there, so exp2 gives exactly 0
+      if (kbase + kKeys - 1 > lim) {
 #pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) {
-        float v[32];
-        tc::ld32(lane_addr + sb * kKeys + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (kbase + c * 32 + i <= lim) mx = fmaxf(mx, v[i]);
+        for (int i = 0; i < kKeys; ++i)
+          if (kbase + i > lim) v[i] = -INFINITY;
       }
-      const float m_new = fmaxf(m, mx * a.scale_log2);
+      float mx;
+      {
+        float t8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) t8[k] = v[k];
+#pragma unroll
+        for (int i = 8; i < kKeys; ++i) t8[i & 7] = fmaxf(t8[i & 7], v[i]);
+        mx = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
+                   fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
+      }
+      mx *= a.scale_log2;
+      // move the reference max only when it has grown by more than 2^8
+      const bool move = mx > m_ref + kRescaleLog2;
+      const float m_new = move ? mx : m_ref;
+      const float factor = ex2(m_ref - m_new);  // 0 on the first tile, 1 if not moved
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2(m - m_use);
-      if (j > 0) {
-        // tile j-1's P.V: O = O * alpha_{j-1} + O_tile
-        if (!__all_sync(0xffffffffu, mbar_wait_bounded(o_full, (j - 1) & 1))) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tc::ld32(lane_addr + kColO + c * 32, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_prev, v[i]);
-        }
-        tc::fence_before_sync();
-        mbar_arrive(o_free);
+      // P buffer b is free once the P.V MMA of tile j - 2 has completed
+      if (j >= 2 && !wait_all(&p_done[b], ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
       }
-      // probabilities of tile j -> P (16-bit, swizzled K-major rows)
-      float sum = 0.f;
+      uint8_t* prow = smem + L::off_p + b * L::kP + (r >> 3) * 1024 + (r & 7) * 128;
+      float s8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s8[k] = 0.f;
 #pragma unroll
       for (int c = 0; c < kKeys / 32; ++c) {
-        float v[32];
-        tc::ld32(lane_addr + sb * kKeys + c * 32, v);
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const int key = kbase + c * 32 + i;
-          const float p0 = key <= lim ? ex2(fmaf(v[i], a.scale_log2, -m_use)) : 0.f;
-          const float p1 = key + 1 <= lim ? ex2(fmaf(v[i + 1], a.scale_log2, -m_use)) : 0.f;
-          sum += p0 + p1;
+          const float p0 = ex2(fmaf(v[c * 32 + i], a.scale_log2, -m_use));
+          const float p1 = ex2(fmaf(v[c * 32 + i + 1], a.scale_log2, -m_use));
+          s8[(i >> 1) & 7] += p0 + p1;
           pk[i >> 1] = pack2<T>(p0, p1);
         }
         uint8_t* hrow = prow + (c >> 1) * L::kHalf;
@@ -360,11 +377,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
         }
       }
+      // rows whose reference moved: O *= factor (after the P.V of tile j - 1)
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        if (!wait_all(&p_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        const float f = move ? factor : 1.f;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tc::ld32(lane_addr + kColO + c * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= f;
+          tc::st32(lane_addr + kColO + c * 32, o);
+        }
+      }
       if (j == n_kv - 1 && kbase + r >= ctx) {
         // key row r of the last tile lies past the context: zero its V row so
         // that 0 * (stale pool bits) cannot reach the output
         if (mbar_wait_bounded(&v_full[j % NS], (j / NS) & 1)) {
-          uint8_t* vrow = smem + L::off_v + (j % NS) * L::kSide + (r >> 3) * 1024 + (r & 7) * 128;
+          uint8_t* vrow =
+              smem + L::off_v + (j % NS) * L::kSide + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
           for (int hf = 0; hf < L::kHalves; ++hf)
 #pragma unroll
@@ -377,46 +412,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_shared();
       tc::fence_before_sync();
-      mbar_arrive(p_full);
-      mbar_arrive(&s_free[sb]);
-      l = fmaf(l, alpha, sum);
-      m = m_new;
-      alpha_prev = alpha;
+      mbar_arrive(&p_full[b]);
+      const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      l = fmaf(l, factor, sum);
+      m_ref = m_new;
       if (!__all_sync(0xffffffffu, ok)) {
         ok = false;
         break;
       }
     }
     if (ok) {
-      if (__all_sync(0xffffffffu, mbar_wait_bounded(o_full, (n_kv - 1) & 1))) {
+      const int jl = n_kv - 1;
+      if (wait_all(&p_done[jl & 1], (jl >> 1) & 1)) {
         tc::fence_after_sync();
+        const float inv = 1.f / l;
+        T* dst = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r0 + r) * a.out_stride +
+                 static_cast<int64_t>(h) * D;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tc::ld32(lane_addr + kColO + c * 32, v);
+          float o[32];
+          tc::ld32(lane_addr + kColO + c * 32, o);  // whole warp (collective)
+          if (r < nrows) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_prev, v[i]);
+            for (int d = 0; d < 32; d += 8) {
+              uint4 w;
+              w.x = pack2<T>(o[d] * inv, o[d + 1] * inv);
+              w.y = pack2<T>(o[d + 2] * inv, o[d + 3] * inv);
+              w.z = pack2<T>(o[d + 4] * inv, o[d + 5] * inv);
+              w.w = pack2<T>(o[d + 6] * inv, o[d + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + d) = w;
+            }
+          }
         }
       } else {
         ok = false;
       }
     }
-    if (!ok) {
-      set_err(a.err, IR_DEVERR_TIMEOUT);
-    } else if (r < nrows) {
-      const float inv = 1.f / l;
-      T* dst = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r0 + r) * a.out_stride +
-               static_cast<int64_t>(h) * D;
-#pragma unroll
-      for (int d = 0; d < D; d += 8) {
-        uint4 w;
-        w.x = pack2<T>(o[d] * inv, o[d + 1] * inv);
-        w.y = pack2<T>(o[d + 2] * inv, o[d + 3] * inv);
-        w.z = pack2<T>(o[d + 4] * inv, o[d + 5] * inv);
-        w.w = pack2<T>(o[d + 6] * inv, o[d + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + d) = w;
-      }
-    }
+    if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
     tc::fence_before_sync();
   }
   __syncthreads();

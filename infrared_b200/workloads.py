@@ -15,6 +15,8 @@ path, inputs are synthetic by design):
 * ``c3`` as c2 with B=256, ctx ~ U[128, 2048], new-token slots in randomly
   allocated tail blocks, ~30 % of sequences sharing 1-8 leading blocks.
 * ``c4`` bf16 7B geometry, B=4, ctx = 32768 each (split-KV / multi-GPU).
+* ``p1`` prefill (Sq > 1): bf16 7B attention geometry, 8 prompts of 4096
+  tokens each forwarded at once (causal), block 16.
 """
 
 from __future__ import annotations
@@ -220,3 +222,74 @@ def torch_values(w: Workload, seed: int, device):
     kn = randn(w.batch, w.num_kv_heads, w.head_dim)
     vn = randn(w.batch, w.num_kv_heads, w.head_dim)
     return q, kp, vp, kn, vn
+
+
+# --- prefill frames -----------------------------------------------------------
+
+
+@dataclass
+class PrefillWorkload:
+    """Packed prefill frame: sequence s has ``starts[s]`` cached tokens and
+    forwards ``q_lens[s]`` new ones (rows ``q_start[s] .. q_start[s+1]-1``)."""
+
+    name: str
+    num_heads: int
+    num_kv_heads: int
+    head_dim: int
+    block_size: int
+    starts: np.ndarray
+    q_lens: np.ndarray
+    block_tables: np.ndarray
+    num_blocks: int
+    dtype: str = "bfloat16"
+
+    @property
+    def context_lens(self) -> np.ndarray:
+        return (self.starts + self.q_lens).astype(np.int32)
+
+    @property
+    def q_start(self) -> np.ndarray:
+        return np.concatenate([[0], np.cumsum(self.q_lens)]).astype(np.int32)
+
+    @property
+    def total_q(self) -> int:
+        return int(self.q_lens.sum())
+
+    @property
+    def scale(self) -> float:
+        return self.head_dim ** -0.5
+
+    def flops(self) -> int:
+        """Useful FLOPs: every query row at position p scores p + 1 keys
+        (QK^T and P.V, 2 * D each, per query head)."""
+        tot = 0
+        for st, ql in zip(self.starts.tolist(), self.q_lens.tolist()):
+            # sum over p in [st, st + ql) of (p + 1)
+            tot += ql * (2 * st + ql + 1) // 2
+        return 4 * self.head_dim * self.num_heads * tot
+
+
+def prefill_frame(name: str, seed: int, starts, q_lens, num_heads: int = 28,
+                  num_kv_heads: int = 4, head_dim: int = 128, block_size: int = 16,
+                  dtype: str = "bfloat16") -> PrefillWorkload:
+    rng = np.random.default_rng(seed)
+    starts = np.asarray(starts, np.int64)
+    q_lens = np.asarray(q_lens, np.int64)
+    ctx = starts + q_lens
+    nblk = -(-ctx // block_size)
+    num_blocks = int(nblk.sum())
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    bt = np.zeros((len(ctx), int(nblk.max())), np.int32)
+    off = 0
+    for i, n in enumerate(nblk.tolist()):
+        bt[i, :n] = perm[off:off + n]
+        off += n
+    return PrefillWorkload(name, num_heads, num_kv_heads, head_dim, block_size, starts, q_lens,
+                           bt, num_blocks, dtype)
+
+
+def p1(seed: int = 0, batch: int = 8, prompt: int = 4096) -> PrefillWorkload:
+    return prefill_frame("p1", seed, [0] * batch, [prompt] * batch)
+
+
+PREFILL_CONFIGS = {"p1": p1}
