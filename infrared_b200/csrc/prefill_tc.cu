@@ -7,20 +7,23 @@
 // infrared/model/inputs.py:38-94 applied to infrared's paged read).
 //
 // One CTA = 128 query rows of one sequence for one query head (grid:
-// q tiles x heads). Six warps:
-//   warp 4      producer: TMA copies of the Q tile (once) and of each
-//               128-key K tile and V tile (one box per block and 64-column
-//               half; block-table lookups spread over the warp's lanes and
-//               done one tile ahead) into rings of NS stages;
-//   warp 5      MMA issuer (one thread): S = Q.K^T (M=128, N=128 keys,
+// q tiles x heads). Eleven warps:
+//   warps 8, 9  producers: TMA copies of the Q tile (once) and of each
+//               128-key K tile (warp 8) and V tile (warp 9), one box per
+//               block and 64-column half, into rings of NS stages; the
+//               block-table lookups are spread over the lanes and done one
+//               tile ahead;
+//   warp 10     MMA issuer (one thread): S = Q.K^T (M=128, N=128 keys,
 //               K=D) into one of two TMEM buffers, and O += P.V (M=128,
 //               N=D, K=128 keys) into the TMEM accumulator, tcgen05.mma
 //               kind::f16 with operands in 128-byte-swizzled shared memory;
 //               tcgen05.commit releases stages and signals the softmax;
-//   warps 0-3   softmax (thread r = query row r = TMEM lane r): one
-//               128-column TMEM load of the row's scores, masked row max,
-//               exp2 probabilities written as 16-bit P into one of two
-//               shared-memory buffers (the A operand of the P.V MMA) and
+//   warps 0-7   softmax: two threads per query row r (= TMEM lane r; warps
+//               w and w + 4 share rows 32 (w % 4) ..), each takes 64 of the
+//               tile's 128 keys: one 64-column TMEM load of its scores,
+//               masked max (combined with the partner's through shared
+//               memory), exp2 probabilities written as 16-bit P into one of
+//               two shared-memory buffers (the A operand of the P.V MMA) and
 //               their running sum. P is taken relative to a reference max
 //               that moves only when the row max grows by more than 2^8
 //               (then the row of O in TMEM and the sum are rescaled), so
@@ -37,7 +40,8 @@ namespace {
 
 constexpr int kRows = 128;     // query rows per CTA (MMA M)
 constexpr int kKeys = 128;     // keys per K/V tile
-constexpr int kThreads = 192;  // warps 0-3 softmax, 4 producer, 5 MMA
+constexpr int kThreads = 352;  // warps 0-7 softmax, 8-9 producers, 10 MMA
+constexpr int kSoftmax = 256;  // softmax threads: 2 per query row (one per 64-key half)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128, O at 256
 constexpr float kRescaleLog2 = 8.f;  // move the reference max when it grows by > 2^8
@@ -59,7 +63,8 @@ struct PLayout {
   // p_full[2], p_done[2], drain
   static constexpr int kBars = 1 + 4 * NS + 9;
   static constexpr int off_misc = off_bar + kBars * 8;
-  static constexpr int kBytes = off_misc + 64;
+  static constexpr int off_red = off_misc + 64;         // [2 halves][128 rows] fp32 exchange
+  static constexpr int kBytes = off_red + 2 * kRows * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
 };
 
@@ -137,8 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], kRows);
-      mbar_init(&p_full[i], kRows);
+      mbar_init(&s_free[i], kSoftmax);
+      mbar_init(&p_full[i], kSoftmax);
       mbar_init(&p_done[i], 1);
     }
     mbar_init(drain, 1);
@@ -173,13 +178,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = static_cast<uint32_t>(misc[2]);
 
-  if (warp == 4) {
-    // ---------------------------------------------------------- producer
-    // Lane i < nbox resolves box i of a tile (block-table lookup) one tile
-    // ahead, so the lookups of tile j + 1 overlap the waits of tile j, and
-    // issues that box's copies itself.
+  if (warp == 8 || warp == 9) {
+    // ---------------------------------------------------------- producers
+    // Warp 8 fills the K ring (and loads Q), warp 9 the V ring, so K tiles
+    // run ahead of the V waits. Lane i < nbox resolves box i of a tile
+    // (block-table lookup) one tile ahead, so the lookups of tile j + 1
+    // overlap the waits of tile j, and issues that box's copies itself.
+    const bool is_k = warp == 8;
+    uint64_t* full = is_k ? k_full : v_full;
+    uint64_t* empty = is_k ? k_empty : v_empty;
+    const CUtensorMap* tm = is_k ? &tmk : &tmv;
+    uint8_t* ring = smem + (is_k ? L::off_k : L::off_v);
     bool ok = true;
-    if (lane == 0) {
+    if (is_k && lane == 0) {
       mbar_arrive_expect_tx(q_full, L::kQ);
 #pragma unroll
       for (int hf = 0; hf < L::kHalves; ++hf)
@@ -202,54 +213,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     int row_cur = row_of(0);
     int issued = 0;
-    for (int j = 0; j < n_kv && ok; ++j) {
+    for (int j = 0; j < n_kv; ++j) {
       const int row_next = row_of(j + 1);
       const int st = j % NS;
-      const uint32_t par = ((j / NS) & 1) ^ 1;
       int w = 1;
-      if (lane == 0) w = mbar_wait_bounded(&k_empty[st], par) ? 1 : 0;
+      if (lane == 0) w = mbar_wait_bounded(&empty[st], ((j / NS) & 1) ^ 1) ? 1 : 0;
       if (!__shfl_sync(0xffffffffu, w, 0)) {
         ok = false;
         break;
       }
-      uint8_t* kd = smem + L::off_k + st * L::kSide;
-      uint8_t* vd = smem + L::off_v + st * L::kSide;
       // lane i issues the copies of box i (the expected bytes are posted first)
-      if (lane == 0) mbar_arrive_expect_tx(&k_full[st], L::kSide);
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], L::kSide);
       __syncwarp();
       if (lane < nbox) {
+        uint8_t* dst = ring + st * L::kSide + lane * R * 128;
 #pragma unroll
         for (int hf = 0; hf < L::kHalves; ++hf)
-          tma_load_3d(kd + hf * (kKeys * 128) + lane * R * 128, &tmk, &k_full[st], 64 * hf,
-                      kvh, row_cur);
+          tma_load_3d(dst + hf * (kKeys * 128), tm, &full[st], 64 * hf, kvh, row_cur);
       }
-      issued = j + 1;  // K copies of tile j are in flight from here on
-      if (lane == 0) w = mbar_wait_bounded(&v_empty[st], par) ? 1 : 0;
-      if (!__shfl_sync(0xffffffffu, w, 0)) {
-        ok = false;
-        break;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&v_full[st], L::kSide);
-      __syncwarp();
-      if (lane < nbox) {
-#pragma unroll
-        for (int hf = 0; hf < L::kHalves; ++hf)
-          tma_load_3d(vd + hf * (kKeys * 128) + lane * R * 128, &tmv, &v_full[st], 64 * hf,
-                      kvh, row_cur);
-      }
+      issued = j + 1;
       row_cur = row_next;
     }
     if (lane == 0) {
       if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
-      // no copy may still be writing when the CTA ends: the V copies of the
-      // last tile exist only if the loop completed it
-      mbar_wait_bounded(q_full, 0);
-      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j) {
-        mbar_wait_bounded(&k_full[j % NS], (j / NS) & 1);
-        if (ok || j + 1 < issued) mbar_wait_bounded(&v_full[j % NS], (j / NS) & 1);
-      }
+      // no copy may still be writing when the CTA ends
+      if (is_k) mbar_wait_bounded(q_full, 0);
+      for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+        mbar_wait_bounded(&full[j % NS], (j / NS) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == 10) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       bool ok = mbar_wait_bounded(q_full, 0);
@@ -304,12 +296,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax
-    const int r = threadIdx.x;  // query row = TMEM lane
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const int r = threadIdx.x & (kRows - 1);  // query row = TMEM lane
+    const int kh = threadIdx.x >> 7;          // which 64 keys of each tile
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const int pos = pos0 + r;
     const int lim = min(pos, ctx - 1);  // last key this row may attend
-    float m_ref = -INFINITY;  // reference max of the P values (log2 units)
-    float l = 0.f;
+    float* red = reinterpret_cast<float*>(smem + L::off_red);  // [2][128]
+    // The two warps of a row group meet at named barrier 1 + warp % 4 (64
+    // threads). They leave the tile loop together, right after such a
+    // meeting whose AND of "all waits succeeded" is false, so neither can
+    // wait at a barrier the other will not reach.
+    const uint32_t pair_bar = 1 + (warp & 3);
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory"); };
+    auto pair_and = [&](bool v) {
+      uint32_t o;
+      asm volatile(
+          "{\n\t.reg .pred pi, po;\n\t"
+          "setp.ne.u32 pi, %1, 0;\n\t"
+          "bar.red.and.pred po, %2, 64, pi;\n\t"
+          "selp.u32 %0, 1, 0, po;\n\t}"
+          : "=r"(o)
+          : "r"(v ? 1u : 0u), "r"(pair_bar)
+          : "memory");
+      return o != 0;
+    };
+    constexpr int kDh = D / 2;  // O columns this thread rescales / writes
+    float m_ref = -INFINITY;    // reference max of the P values (log2 units)
+    float l = 0.f;              // this half's share of the row sum
     bool ok = true;
     // tcgen05.ld / st are warp-collective: every wait result is made warp-uniform
     auto wait_all = [&](uint64_t* bar, uint32_t par) {
@@ -317,21 +330,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     for (int j = 0; j < n_kv; ++j) {
       const int b = j & 1;
-      const int kbase = j * kKeys;
-      if (!wait_all(&s_full[b], (j >> 1) & 1)) {
+      const int kbase = j * kKeys + kh * 64;
+      float v[64];
+      if (wait_all(&s_full[b], (j >> 1) & 1)) {
+        tc::fence_after_sync();
+        tc::ld64(lane_addr + b * kKeys + kh * 64, v);
+        tc::fence_before_sync();
+        mbar_arrive(&s_free[b]);
+      } else {
         ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      float v[kKeys];
-      tc::ld128(lane_addr + b * kKeys, v);
-      tc::fence_before_sync();
-      mbar_arrive(&s_free[b]);
-      // keys past this row's limit exist only in the last one or two tiles
-      // (the diagonal); mask them to -inf there, so exp2 gives exactly 0
-      if (kbase + kKeys - 1 > lim) {
 #pragma unroll
-        for (int i = 0; i < kKeys; ++i)
+        for (int i = 0; i < 64; ++i) v[i] = -INFINITY;
+      }
+      // keys past this row's limit exist only in the diagonal tiles: -inf there
+      if (kbase + 63 > lim) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
           if (kbase + i > lim) v[i] = -INFINITY;
       }
       float mx;
@@ -340,72 +354,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) t8[k] = v[k];
 #pragma unroll
-        for (int i = 8; i < kKeys; ++i) t8[i & 7] = fmaxf(t8[i & 7], v[i]);
+        for (int i = 8; i < 64; ++i) t8[i & 7] = fmaxf(t8[i & 7], v[i]);
         mx = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
                    fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
       }
-      mx *= a.scale_log2;
+      // the row max over both halves (the partner thread holds the other 64 keys)
+      red[kh * kRows + r] = mx;
+      if (!pair_and(ok)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, red[(kh ^ 1) * kRows + r]) * a.scale_log2;
+      pair_sync();  // both read before the next tile's write
       // move the reference max only when it has grown by more than 2^8
       const bool move = mx > m_ref + kRescaleLog2;
       const float m_new = move ? mx : m_ref;
       const float factor = ex2(m_ref - m_new);  // 0 on the first tile, 1 if not moved
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       // P buffer b is free once the P.V MMA of tile j - 2 has completed
-      if (j >= 2 && !wait_all(&p_done[b], ((j - 2) >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      uint8_t* prow = smem + L::off_p + b * L::kP + (r >> 3) * 1024 + (r & 7) * 128;
+      if (j >= 2 && !wait_all(&p_done[b], ((j - 2) >> 1) & 1)) ok = false;
+      // this half's keys are the 64-column half kh of the P tile
+      uint8_t* prow =
+          smem + L::off_p + b * L::kP + kh * L::kHalf + (r >> 3) * 1024 + (r & 7) * 128;
       float s8[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) s8[k] = 0.f;
 #pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) {
-        uint32_t pk[16];
+      for (int c = 0; c < 8; ++c) {  // 16-byte chunks of 8 keys
+        uint32_t pk[4];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2(fmaf(v[c * 32 + i], a.scale_log2, -m_use));
-          const float p1 = ex2(fmaf(v[c * 32 + i + 1], a.scale_log2, -m_use));
-          s8[(i >> 1) & 7] += p0 + p1;
+        for (int i = 0; i < 8; i += 2) {
+          const float p0 = ex2(fmaf(v[c * 8 + i], a.scale_log2, -m_use));
+          const float p1 = ex2(fmaf(v[c * 8 + i + 1], a.scale_log2, -m_use));
+          s8[c] += p0 + p1;
           pk[i >> 1] = pack2<T>(p0, p1);
         }
-        uint8_t* hrow = prow + (c >> 1) * L::kHalf;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int ch = ((c & 1) * 4 + k) ^ (r & 7);
-          *reinterpret_cast<uint4*>(hrow + ch * 16) =
-              make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-        }
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      // rows whose reference moved: O *= factor (after the P.V of tile j - 1)
-      if (j > 0 && __any_sync(0xffffffffu, move)) {
-        if (!wait_all(&p_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
-          ok = false;
-          break;
-        }
+      // rows whose reference moved: O *= factor (after the P.V of tile j - 1);
+      // this thread rescales its half of the columns
+      bool rescale = j > 0 && __any_sync(0xffffffffu, move);
+      if (rescale && !wait_all(&p_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+        ok = false;
+        rescale = false;
+      }
+      if (rescale) {
         tc::fence_after_sync();
         const float f = move ? factor : 1.f;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kDh / 32; ++c) {
           float o[32];
-          tc::ld32(lane_addr + kColO + c * 32, o);
+          const uint32_t col = kColO + kh * kDh + c * 32;
+          tc::ld32(lane_addr + col, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= f;
-          tc::st32(lane_addr + kColO + c * 32, o);
+          tc::st32(lane_addr + col, o);
         }
       }
-      if (j == n_kv - 1 && kbase + r >= ctx) {
-        // key row r of the last tile lies past the context: zero its V row so
-        // that 0 * (stale pool bits) cannot reach the output
+      if (j == n_kv - 1 && j * kKeys + r >= ctx && kh < L::kHalves) {
+        // key row r of the last tile lies past the context: zero its V row
+        // (this thread: 64-column half kh) so that 0 * (stale pool bits)
+        // cannot reach the output
         if (mbar_wait_bounded(&v_full[j % NS], (j / NS) & 1)) {
-          uint8_t* vrow =
-              smem + L::off_v + (j % NS) * L::kSide + (r >> 3) * 1024 + (r & 7) * 128;
+          uint8_t* vrow = smem + L::off_v + (j % NS) * L::kSide + kh * (kKeys * 128) +
+                          (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-          for (int hf = 0; hf < L::kHalves; ++hf)
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-              *reinterpret_cast<uint4*>(vrow + hf * (kKeys * 128) + k * 16) =
-                  make_uint4(0, 0, 0, 0);
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<uint4*>(vrow + k * 16) = make_uint4(0, 0, 0, 0);
         } else {
           ok = false;
         }
@@ -416,22 +432,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       l = fmaf(l, factor, sum);
       m_ref = m_new;
-      if (!__all_sync(0xffffffffu, ok)) {
-        ok = false;
-        break;
-      }
+      // a failed wait in this tile is acted on at the next tile's meeting
     }
+    // the row sum over both halves (all pairs still in step: the loop count
+    // and the break points are the same for both warps of a row group)
+    red[kh * kRows + r] = l;
+    pair_sync();
+    const float l_row = l + red[(kh ^ 1) * kRows + r];
     if (ok) {
       const int jl = n_kv - 1;
       if (wait_all(&p_done[jl & 1], (jl >> 1) & 1)) {
         tc::fence_after_sync();
-        const float inv = 1.f / l;
+        const float inv = 1.f / l_row;
         T* dst = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r0 + r) * a.out_stride +
-                 static_cast<int64_t>(h) * D;
+                 static_cast<int64_t>(h) * D + kh * kDh;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kDh / 32; ++c) {
           float o[32];
-          tc::ld32(lane_addr + kColO + c * 32, o);  // whole warp (collective)
+          tc::ld32(lane_addr + kColO + kh * kDh + c * 32, o);  // whole warp (collective)
           if (r < nrows) {
 #pragma unroll
             for (int d = 0; d < 32; d += 8) {
