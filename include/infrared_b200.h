@@ -355,6 +355,25 @@ int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v
                      const int32_t* q_start, const ir_prefill_shape* shape, void* workspace,
                      size_t workspace_bytes, int32_t* err_flag, ir_stream_t stream);
 
+/*
+ * The block-table form of one packed frame as infrared's engine builds it
+ * for Sq > 1 (prefill with a cached prefix, paged_engine.py:197-221; the
+ * mixed step, :461-516): gather_slots int64 [num_keys] (the histories of the
+ * frame's sequences laid end to end) and the additive mask
+ * [num_rows, num_keys] (row stride mask_stride elements; 0 = allowed) of
+ * infrared/model/inputs.py:38-94. Writes block_tables [num_rows, max_blocks]
+ * (row s for sequence s), context_lens [num_rows], q_start [num_rows + 1]
+ * and *num_seqs (all device memory); scratch: 3 * num_rows int32. A mask
+ * row that is not one contiguous range, or a sequence whose rows do not
+ * advance by one position, sets IR_DEVERR_MASK; slots that are not block
+ * structured set IR_DEVERR_NOT_BLOCKED.
+ */
+int ir_derive_varlen_metadata(const int64_t* gather_slots, int64_t num_keys, const void* mask,
+                              int64_t mask_stride, int mask_dtype, int num_rows,
+                              int block_size, int max_blocks, int32_t* block_tables,
+                              int32_t* context_lens, int32_t* q_start, int32_t* num_seqs,
+                              int32_t* scratch, int32_t* err_flag, ir_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

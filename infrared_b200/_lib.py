@@ -88,6 +88,9 @@ class PrefillShape(ctypes.Structure):
 # (name, restype, argtypes) of every exported function
 _SIGNATURES = {
     "ir_set_prefill_path": (c_int, [c_int]),
+    "ir_derive_varlen_metadata": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int,
+                                          c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_void_p]),
     "ir_paged_prefill_plan": (c_int, [POINTER(PrefillShape), POINTER(c_int)]),
     "ir_paged_prefill_workspace_size": (c_size_t, [POINTER(PrefillShape)]),
     "ir_paged_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

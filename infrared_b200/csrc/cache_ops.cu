@@ -194,6 +194,142 @@ __global__ void prefill_rows_kernel(const int32_t* __restrict__ bt, int64_t bt_s
         sq >= 0 ? bt[static_cast<int64_t>(sq) * bt_stride + j] : 0;
 }
 
+// ---- packed prefill frames (Sq > 1): (gather_slots, mask) -> block tables
+//
+// infrared's mixed step gathers every sequence's history into one key axis
+// and masks each query row to its own sequence's causal prefix
+// (infrared/model/inputs.py:64-94); its single-prompt prefill is the same
+// with one sequence (:38-61). Row i of such a mask allows exactly one
+// contiguous key range [lo_i, lo_i + cnt_i); consecutive rows with the same lo
+// form a sequence whose cnt grows by one per row; its history is the key
+// range of its last row, block-structured from lo.
+
+// Per query row: first allowed key column and the number of allowed columns
+// (flags MASK when they are not one contiguous range).
+__global__ void varlen_rows_kernel(const void* __restrict__ mask, int64_t mask_stride,
+                                   int elem_bytes, int64_t K, int32_t* __restrict__ lo,
+                                   int32_t* __restrict__ cnt, int32_t* err) {
+  const int64_t i = blockIdx.x;
+  const int tid = threadIdx.x;
+  __shared__ int64_t s_cnt[32], s_min[32], s_max[32];
+  int64_t c = 0, mn = K, mx = -1;
+  for (int64_t t = tid; t < K; t += blockDim.x) {
+    if (mask_zero(mask, elem_bytes, i * mask_stride + t)) {
+      ++c;
+      mn = t < mn ? t : mn;
+      mx = t > mx ? t : mx;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    c += __shfl_xor_sync(0xffffffffu, c, o);
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const int warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    s_cnt[warp] = c;
+    s_min[warp] = mn;
+    s_max[warp] = mx;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    c = 0;
+    mn = K;
+    mx = -1;
+    for (int w = 0; w < nw; ++w) {
+      c += s_cnt[w];
+      mn = min(mn, s_min[w]);
+      mx = max(mx, s_max[w]);
+    }
+    if (c == 0 || mx - mn + 1 != c) set_err(err, IR_DEVERR_MASK);
+    lo[i] = static_cast<int32_t>(c == 0 ? 0 : mn);
+    cnt[i] = static_cast<int32_t>(c);
+  }
+}
+
+// One block: sequence boundaries (rows whose lo differs from the previous
+// row's), q_start, the history length of each sequence (cnt of its last
+// row) and its first key column; checks that cnt grows by one per row.
+__global__ void varlen_seqs_kernel(const int32_t* __restrict__ lo, const int32_t* __restrict__ cnt,
+                                   int Q, int32_t* __restrict__ q_start, int32_t* __restrict__ ctx,
+                                   int32_t* __restrict__ lo_seq, int32_t* __restrict__ nseq,
+                                   int32_t* err) {
+  __shared__ int32_t s_warp[32];
+  __shared__ int32_t s_carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  if (tid == 0) s_carry = 0;
+  __syncthreads();
+  for (int base = 0; base < Q; base += blockDim.x) {
+    const int i = base + tid;
+    const bool valid = i < Q;
+    const bool start = valid && (i == 0 || lo[i] != lo[i - 1]);
+    if (valid && !start && cnt[i] != cnt[i - 1] + 1) set_err(err, IR_DEVERR_MASK);
+    // block-wide inclusive scan of the start flags
+    int v = start ? 1 : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += y;
+    }
+    if (lane == 31) s_warp[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int w = lane < nw ? s_warp[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      if (lane < nw) s_warp[lane] = w;
+    }
+    __syncthreads();
+    const int incl = v + (warp > 0 ? s_warp[warp - 1] : 0) + s_carry;
+    const int seq = incl - 1;  // sequence of row i
+    if (start) {
+      q_start[seq] = i;
+      lo_seq[seq] = lo[i];
+    }
+    if (valid && (i == Q - 1 || lo[i + 1] != lo[i])) ctx[seq] = cnt[i];
+    __syncthreads();
+    if (tid == blockDim.x - 1) s_carry = incl;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    q_start[s_carry] = Q;
+    *nseq = s_carry;
+  }
+}
+
+// Block table of sequence blockIdx.x from its key range of the gathered
+// slots; flags NOT_BLOCKED when the range is not block-structured.
+__global__ void varlen_tables_kernel(const int64_t* __restrict__ gs, const int32_t* __restrict__ lo_seq,
+                                     const int32_t* __restrict__ ctx, const int32_t* __restrict__ nseq,
+                                     int bs, int max_blocks, int32_t* __restrict__ bt,
+                                     int32_t* err) {
+  const int sq = blockIdx.x;
+  if (sq >= *nseq) return;
+  const int64_t base = lo_seq[sq];
+  const int c = ctx[sq];
+  const int nb = (c + bs - 1) / bs;
+  if (nb > max_blocks) {
+    if (threadIdx.x == 0) set_err(err, IR_DEVERR_CONTEXT_LEN);
+    return;
+  }
+  bool bad = false;
+  for (int j = threadIdx.x; j < max_blocks; j += blockDim.x) {
+    int32_t id = 0;
+    if (j < nb) {
+      const int64_t s0 = gs[base + static_cast<int64_t>(j) * bs];
+      if (s0 < 0 || s0 % bs != 0 || s0 / bs > INT32_MAX) bad = true;
+      id = static_cast<int32_t>(s0 / bs);
+    }
+    bt[static_cast<int64_t>(sq) * max_blocks + j] = id;
+  }
+  for (int t = threadIdx.x; t < c; t += blockDim.x) {
+    const int64_t s0 = gs[base + (t / bs) * bs];
+    if (gs[base + t] != (s0 / bs) * bs + t % bs) bad = true;
+  }
+  if (bad) set_err(err, IR_DEVERR_NOT_BLOCKED);
+}
+
 int grid_for(int64_t work, int threads) {
   return static_cast<int>((work + threads - 1) / threads);
 }
@@ -281,6 +417,24 @@ int launch_prefill_rows(const int32_t* bt, int64_t bt_stride, const int32_t* ctx
   if (total_q == 0) return 0;
   prefill_rows_kernel<<<total_q, 128, 0, stream>>>(bt, bt_stride, ctx, q_start, S, max_blocks,
                                                    max_ctx, row_bt, row_ctx, err);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int launch_derive_varlen(const int64_t* gs, const void* mask, int64_t mask_stride,
+                         int mask_elem_bytes, int Q, int64_t K, int bs, int max_blocks,
+                         int32_t* bt, int32_t* ctx, int32_t* q_start, int32_t* nseq,
+                         int32_t* scratch, int32_t* err, cudaStream_t stream) {
+  if (Q == 0) {
+    cudaError_t e = cudaMemsetAsync(nseq, 0, 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(q_start, 0, 4, stream);
+    return static_cast<int>(e);
+  }
+  int32_t* lo = scratch;
+  int32_t* cnt = scratch + Q;
+  int32_t* lo_seq = scratch + 2 * static_cast<int64_t>(Q);
+  varlen_rows_kernel<<<Q, 256, 0, stream>>>(mask, mask_stride, mask_elem_bytes, K, lo, cnt, err);
+  varlen_seqs_kernel<<<1, 1024, 0, stream>>>(lo, cnt, Q, q_start, ctx, lo_seq, nseq, err);
+  varlen_tables_kernel<<<Q, 128, 0, stream>>>(gs, lo_seq, ctx, nseq, bs, max_blocks, bt, err);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -615,6 +615,27 @@ int ir_derive_block_metadata(const int64_t* gather_slots, int64_t gs_stride,
   return cuda_status(e, "metadata launch");
 }
 
+int ir_derive_varlen_metadata(const int64_t* gather_slots, int64_t num_keys, const void* mask,
+                              int64_t mask_stride, int mask_dtype, int num_rows,
+                              int block_size, int max_blocks, int32_t* block_tables,
+                              int32_t* context_lens, int32_t* q_start, int32_t* num_seqs,
+                              int32_t* scratch, int32_t* err_flag, ir_stream_t stream) {
+  const int eb = elem_bytes(mask_dtype);
+  if (eb == 0) return fail(IR_ERR_INVALID_ARG, "bad mask dtype");
+  if (num_rows < 0 || num_keys < 0 || block_size <= 0 || max_blocks < 0)
+    return fail(IR_ERR_INVALID_ARG, "bad sizes");
+  if (num_keys > INT32_MAX) return fail(IR_ERR_UNSUPPORTED, "num_keys overflows int32");
+  if (mask_stride < num_keys) return fail(IR_ERR_INVALID_ARG, "mask_stride < num_keys");
+  if (!q_start || !num_seqs || (num_rows > 0 && (!gather_slots || !mask || !block_tables ||
+                                                 !context_lens || !scratch)))
+    return fail(IR_ERR_INVALID_ARG, "null pointer");
+  int e = irb::launch_derive_varlen(gather_slots, mask, mask_stride, eb, num_rows, num_keys,
+                                    block_size, max_blocks, block_tables, context_lens,
+                                    q_start, num_seqs, scratch, err_flag,
+                                    static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "varlen metadata launch");
+}
+
 int ir_paged_decode(void* out, const void* q, const void* k_pool,
                     const void* v_pool, const int32_t* block_tables,
                     const int32_t* context_lens, const ir_decode_shape* shape,

@@ -73,6 +73,10 @@ int launch_build_decode_inputs(const int32_t* bt, int64_t bt_stride,
 int launch_prefill_rows(const int32_t* bt, int64_t bt_stride, const int32_t* ctx,
                         const int32_t* q_start, int S, int total_q, int max_blocks, int max_ctx,
                         int32_t* row_bt, int32_t* row_ctx, int32_t* err, cudaStream_t stream);
+int launch_derive_varlen(const int64_t* gs, const void* mask, int64_t mask_stride,
+                         int mask_elem_bytes, int Q, int64_t K, int bs, int max_blocks,
+                         int32_t* bt, int32_t* ctx, int32_t* q_start, int32_t* nseq,
+                         int32_t* scratch, int32_t* err, cudaStream_t stream);
 int launch_derive_metadata(const int64_t* gs, int64_t gs_stride,
                            const void* mask, int64_t mask_stride,
                            int mask_elem_bytes, int B, int64_t T, int bs,

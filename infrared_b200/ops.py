@@ -548,3 +548,33 @@ def paged_prefill(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                                context_lens.data_ptr(), q_start.data_ptr(), s, ws.data_ptr(),
                                ws.numel(), error_flag(dev).data_ptr(), _stream(dev)))
     return out
+
+
+def derive_varlen_metadata(gather_slots: torch.Tensor, mask: torch.Tensor, block_size: int):
+    """``(block_tables [S, max_blocks], context_lens [S], q_start [S + 1])`` of
+    one packed frame in infrared's form (``gather_slots [1, K]`` int64 and
+    the additive ``mask [1, 1, Q, K]`` of inputs.py:38-94), built on the
+    device; reading the sequence count back is one small synchronising copy.
+    Inconsistent frames set device error bits (``check_device_errors``).
+    """
+    _dev_index(mask)
+    gs = gather_slots.reshape(-1)
+    if gs.dtype != torch.int64 or not gs.is_contiguous():
+        gs = gs.to(torch.int64).contiguous()
+    q, k = mask.shape[-2], mask.shape[-1]
+    m2 = mask.reshape(q, k)
+    if m2.stride(1) != 1:
+        m2 = m2.contiguous()
+    dev = _dev_index(mask)
+    max_blocks = max(1, -(-k // block_size))
+    bt = torch.empty((max(q, 1), max_blocks), dtype=torch.int32, device=mask.device)
+    ctx = torch.empty(max(q, 1), dtype=torch.int32, device=mask.device)
+    q_start = torch.empty(q + 1, dtype=torch.int32, device=mask.device)
+    nseq = torch.empty(1, dtype=torch.int32, device=mask.device)
+    scratch = torch.empty(max(3 * q, 1), dtype=torch.int32, device=mask.device)
+    check(_lib.load().ir_derive_varlen_metadata(
+        gs.data_ptr(), k, m2.data_ptr(), m2.stride(0) if q else k, dtype_code(m2.dtype), q,
+        block_size, max_blocks, bt.data_ptr(), ctx.data_ptr(), q_start.data_ptr(),
+        nseq.data_ptr(), scratch.data_ptr(), error_flag(dev).data_ptr(), _stream(dev)))
+    s = int(nseq.item())
+    return bt[:s], ctx[:s], q_start[:s + 1]

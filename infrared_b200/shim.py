@@ -15,9 +15,12 @@ infrared:
 * ``PagedKVPool.write`` on CUDA tensors -> ``ir_cache_write``;
 * ``_should_use_triton`` -> True for CUDA decode calls (``Sq == 1``) with
   ``head_dim`` 64 or 128 in fp32 / bf16 / fp16 and ``use_triton`` set;
-  prefill and mixed varlen batches (``Sq > 1``) keep infrared's own path;
+  with ``prefill=True`` also for packed prefill / mixed frames (``B == 1``,
+  ``Sq > 1``), which otherwise keep infrared's own path;
 * ``_paged_attention_triton`` -> ``ir_derive_block_metadata`` (once per
-  forward) + ``ir_paged_decode``;
+  forward) + ``ir_paged_decode`` for decode calls, and
+  ``ir_derive_varlen_metadata`` (once per forward) + ``ir_paged_prefill``
+  (tcgen05 tensor cores) for packed frames;
 * (optional, ``graph_inputs=True``) ``cuda_graph.build_decode_static_inputs``
   (infrared/engine/cuda_graph.py:105-155, a module global read by
   ``CudaGraphDecoder.decode`` at :211) -> ``ir_build_decode_inputs`` for CUDA
@@ -41,7 +44,7 @@ from dataclasses import dataclass
 import torch
 
 from . import ops
-from .attention import block_metadata
+from .attention import block_metadata, prefill_frame
 
 _SUPPORTED = (torch.float32, torch.bfloat16, torch.float16)
 
@@ -52,11 +55,20 @@ def should_use_b200(q: torch.Tensor, want: bool) -> bool:
             and q.shape[-1] in (64, 128) and q.dtype in _SUPPORTED)
 
 
+def should_use_b200_with_prefill(q: torch.Tensor, want: bool) -> bool:
+    """The gate plus packed Sq > 1 frames (B == 1)."""
+    return (bool(want) and q.is_cuda and q.dim() == 4 and
+            (q.shape[1] == 1 or q.shape[0] == 1)
+            and q.shape[-1] in (64, 128) and q.dtype in _SUPPORTED)
+
+
 def paged_attention_b200(q: torch.Tensor, paged, mask: torch.Tensor, layer_idx: int,
                          scale: float, n_rep: int) -> torch.Tensor:
     """Read path with the signature of ``_paged_attention_triton``
     (triton_attention.py:310-318): the pool already holds this step's K/V."""
     b, sq, h, d = q.shape
+    if sq != 1:
+        return prefill_frame(q, paged, mask, layer_idx, scale)
     pool = paged.pool
     bt, ctx = block_metadata(paged, mask)
     out = torch.empty((b, sq, h, d), dtype=q.dtype, device=q.device)
@@ -136,7 +148,8 @@ class Installed:
 
 
 def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
-            graph_inputs: bool = True, layers=None, fuse_rope: bool = False) -> Installed:
+            graph_inputs: bool = True, layers=None, fuse_rope: bool = False,
+            prefill: bool = False) -> Installed:
     """Route infrared's paged decode attention to the B200 kernels.
 
     ``triton_attention`` / ``paged_kv_cache`` / ``cuda_graph`` / ``layers``
@@ -145,7 +158,8 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
     ``infrared.model.layers`` modules (any modules with the same names and call
     contract work); ``graph_inputs=False`` leaves infrared's graph-input
     builder alone; ``fuse_rope=True`` also replaces ``Attention.forward`` so
-    that RoPE runs inside the decode kernel.
+    that RoPE runs inside the decode kernel; ``prefill=True`` also routes
+    packed prefill / mixed frames (``Sq > 1``) to the tensor-core kernel.
     """
     ta = triton_attention or importlib.import_module("infrared.model.triton_attention")
     pk = paged_kv_cache or importlib.import_module("infrared.cache.paged_kv_cache")
@@ -155,7 +169,7 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
     pool_cls = pk.PagedKVPool
     saved = {"gate": ta._should_use_triton, "read": ta._paged_attention_triton,
              "write": pool_cls.write}
-    ta._should_use_triton = should_use_b200
+    ta._should_use_triton = should_use_b200_with_prefill if prefill else should_use_b200
     ta._paged_attention_triton = paged_attention_b200
     pool_cls.write = _make_write(saved["write"])
     if cg is not None:

@@ -383,7 +383,7 @@ def test_reference_cuda_kernel_test_ported():
     np.testing.assert_allclose(host_f32(got), want, atol=FP32_TOL, rtol=0)
 
 
-def test_mirror_rejects_prefill_and_cpu():
+def test_mirror_rejects_batched_prefill_and_cpu():
     w, *vals = cases.attention_inputs("g2_d64_bs16")
     q, k, v, pool, ws, gs, mask = _seam(w, vals, torch.float32)
     ctx = irb.PagedContext(pool, ws, gs)

@@ -161,3 +161,72 @@ def test_prefill_empty_frame():
     qs = torch.zeros(1, dtype=torch.int32, device=DEV)
     out = irb.paged_prefill(q, kp, kp, bt, ctx, qs, 0.125, 16)
     assert out.shape == (0, 8, 64)
+
+
+# ----------------------------------------------------------- infrared's frame form
+
+
+def _frame_tensors(c, dtype):
+    fr = c["frame"]
+    mask = torch.from_numpy(orc.varlen_mask(fr["q_seq_ids"], fr["q_pos"], fr["k_seq_ids"],
+                                            fr["k_pos"])).to(DEV)
+    if dtype != torch.float32:
+        mask = mask.to(dtype)   # finfo(fp32).min -> -inf in 16 bits: still "blocked"
+    return torch.from_numpy(fr["gather_slots"]).to(DEV), mask
+
+
+@pytest.mark.parametrize("mask_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("name", sorted(cases.PREFILL_CASES))
+def test_derive_varlen_metadata_bit_exact(name, mask_dtype):
+    c = cases.prefill_inputs(name)
+    gs, mask = _frame_tensors(c, mask_dtype)
+    bt, ctx, qs = ops.derive_varlen_metadata(gs, mask, c["bs"])
+    want_bt, want_ctx, want_qs, ok = orc.varlen_metadata(c["frame"]["gather_slots"],
+                                                         host_f32(mask), c["bs"])
+    assert ok
+    np.testing.assert_array_equal(ctx.cpu().numpy(), want_ctx)
+    np.testing.assert_array_equal(qs.cpu().numpy(), want_qs)
+    np.testing.assert_array_equal(bt.cpu().numpy()[:, :want_bt.shape[1]], want_bt)
+
+
+def test_derive_varlen_metadata_flags_broken_frames():
+    c = cases.prefill_inputs("varlen_mix")
+    gs, mask = _frame_tensors(c, torch.float32)
+    bad = mask.clone()
+    bad[0, 0, 3, 1] = torch.finfo(torch.float32).min   # a hole inside row 3's range
+    ops.derive_varlen_metadata(gs, bad, c["bs"])
+    with pytest.raises(ops.DeviceError, match="MASK"):
+        ops.check_device_errors()
+    gs2 = gs.clone()
+    gs2[0, 5] += 1                                       # not block structured
+    ops.derive_varlen_metadata(gs2, mask, c["bs"])
+    with pytest.raises(ops.DeviceError, match="NOT_BLOCKED"):
+        ops.check_device_errors()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("name", sorted(cases.PREFILL_CASES))
+def test_mirror_paged_attention_prefill_frames(golden, name, dtype):
+    """infrared's seam signature with a packed frame: write, then prefill."""
+    from infrared_b200.attention import clear_metadata_cache
+
+    c = cases.prefill_inputs(name)
+    fr = c["frame"]
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(DEV)  # noqa: E731
+    pool = irb.PagedKVPool(1, c["num_blocks"], c["bs"], c["hkv"], c["d"], dtype, DEV)
+    pool.k[0].copy_(t(c["pool_k"]).to(dtype))
+    pool.v[0].copy_(t(c["pool_v"]).to(dtype))
+    gs, mask = _frame_tensors(c, dtype)
+    paged = irb.PagedContext(pool, t(fr["write_slots"]), gs, use_triton=True)
+    q, k, v = (t(c[n]).to(dtype)[None] for n in ("q", "k", "v"))
+    clear_metadata_cache()
+    out = irb.paged_attention(q, k, v, paged, mask, 0, c["scale"], c["n_rep"])
+    assert out.shape == q.shape
+    if dtype == torch.float32:
+        assert np.abs(host_f32(out[0]) - golden[f"prefill/{name}/out"]).max() <= 1e-5
+    else:
+        want = orc.prefill_from_tables(host_f32(q[0]), host_f32(pool.k[0])[None],
+                                       host_f32(pool.v[0])[None], 0, c["block_tables"],
+                                       c["context_lens"], c["q_start"], c["bs"], c["scale"],
+                                       c["n_rep"])
+        assert_close_bf16(host_f32(out[0]), want)

@@ -328,3 +328,41 @@ def test_fused_rope_forward_equals_installed_seam(dtype):
     assert torch.equal(out, ref)
     assert torch.equal(pool.k, ref_pool.k) and torch.equal(pool.v, ref_pool.v)
     check_device_errors()
+
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_shim_routes_prefill_frames_when_enabled():
+    """install(prefill=True): a packed Sq > 1 frame goes to the tensor-core
+    prefill; without it, the seam's own path runs."""
+    import cases
+    from infrared_b200 import PagedContext, check_device_errors
+    from infrared_b200.attention import clear_metadata_cache
+
+    c = cases.prefill_inputs("varlen_g7")
+    fr = c["frame"]
+    dtype = torch.bfloat16
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).cuda()  # noqa: E731
+    mask = t(orc.varlen_mask(fr["q_seq_ids"], fr["q_pos"], fr["k_seq_ids"],
+                             fr["k_pos"])).to(dtype)
+    q, k, v = (t(c[n]).to(dtype)[None] for n in ("q", "k", "v"))
+    outs = {}
+    for prefill in (True, False):
+        ta, pk, calls = _stand_in_seam()
+        h = shim.install(ta, pk, graph_inputs=False, prefill=prefill)
+        try:
+            pool = pk.PagedKVPool(1, c["num_blocks"], c["bs"], c["hkv"], c["d"], dtype, "cuda")
+            pool.k[0].copy_(t(c["pool_k"]).to(dtype))
+            pool.v[0].copy_(t(c["pool_v"]).to(dtype))
+            paged = PagedContext(pool, t(fr["write_slots"]), t(fr["gather_slots"]),
+                                 use_triton=True)
+            clear_metadata_cache()
+            outs[prefill] = ta.paged_attention(q, k, v, paged, mask, 0, c["scale"], c["n_rep"])
+            assert calls["b200"] == (1 if prefill else 0)
+            assert calls["naive"] == (0 if prefill else 1)
+        finally:
+            h.uninstall()
+    check_device_errors()
+    diff = (outs[True].float() - outs[False].float()).abs().max().item()
+    assert diff < 2e-2
