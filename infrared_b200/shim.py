@@ -25,6 +25,11 @@ infrared:
   (infrared/engine/cuda_graph.py:105-155, a module global read by
   ``CudaGraphDecoder.decode`` at :211) -> ``ir_build_decode_inputs`` for CUDA
   devices, which removes the per-element Python loop of every graph step;
+* (optional, ``eager_inputs=True``) ``PagedBatchEngine._decode_logits_eager``
+  (infrared/engine/paged_engine.py:290-332, a method) -> the same forward
+  with its decode inputs (write slots, per-row slot lists, mask, positions,
+  ids) built by ``ir_build_decode_inputs`` in one launch instead of one
+  small tensor build per sequence; other devices keep infrared's method;
 * (optional, ``fuse_rope=True``) ``layers.Attention.forward``
   (infrared/model/layers.py:156-182, a class attribute) -> the same
   projections, then ONE ``ir_paged_decode_rope_write`` that applies RoPE to
@@ -113,6 +118,27 @@ def _make_attention_forward(original):
     return forward
 
 
+def _make_decode_logits_eager(original, paged_context_cls):
+    from .graph_inputs import build_decode_static_inputs as on_device
+
+    def _decode_logits_eager(self, running):
+        device, dtype = self.model.device, self.model.dtype
+        if torch.device(device).type != "cuda" or not running:
+            return original(self, running)
+        num_cached = [s.num_cached_tokens for s in running]
+        inp = on_device([s.block_table for s in running], num_cached,
+                        [s.last_token for s in running], len(running), max(num_cached) + 1,
+                        self.block_size, device, dtype)
+        logits = self.model.forward(
+            inp.ids, inp.positions, inp.mask,
+            paged=paged_context_cls(self.pool, inp.write_slots, inp.gather_slots,
+                                    use_triton=self.enable_triton_attention))
+        return logits[:, -1]
+    _decode_logits_eager.__doc__ = ("PagedBatchEngine._decode_logits_eager with its inputs "
+                                    "built on the device (ir_build_decode_inputs).")
+    return _decode_logits_eager
+
+
 def _make_graph_inputs(original, decode_inputs_cls):
     from .graph_inputs import build_decode_static_inputs as on_device
 
@@ -136,6 +162,7 @@ class Installed:
     saved: dict
     cuda_graph: object = None
     attention_cls: object = None
+    engine_cls: object = None
 
     def uninstall(self) -> None:
         self.triton_attention._should_use_triton = self.saved["gate"]
@@ -145,11 +172,14 @@ class Installed:
             self.cuda_graph.build_decode_static_inputs = self.saved["graph_inputs"]
         if self.attention_cls is not None:
             self.attention_cls.forward = self.saved["forward"]
+        if self.engine_cls is not None:
+            self.engine_cls._decode_logits_eager = self.saved["eager"]
 
 
 def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
             graph_inputs: bool = True, layers=None, fuse_rope: bool = False,
-            prefill: bool = False) -> Installed:
+            prefill: bool = False, paged_engine=None,
+            eager_inputs: bool = False) -> Installed:
     """Route infrared's paged decode attention to the B200 kernels.
 
     ``triton_attention`` / ``paged_kv_cache`` / ``cuda_graph`` / ``layers``
@@ -159,7 +189,9 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
     contract work); ``graph_inputs=False`` leaves infrared's graph-input
     builder alone; ``fuse_rope=True`` also replaces ``Attention.forward`` so
     that RoPE runs inside the decode kernel; ``prefill=True`` also routes
-    packed prefill / mixed frames (``Sq > 1``) to the tensor-core kernel.
+    packed prefill / mixed frames (``Sq > 1``) to the tensor-core kernel;
+    ``eager_inputs=True`` builds the eager decode step's inputs on the device
+    (``paged_engine`` defaults to ``infrared.engine.paged_engine``).
     """
     ta = triton_attention or importlib.import_module("infrared.model.triton_attention")
     pk = paged_kv_cache or importlib.import_module("infrared.cache.paged_kv_cache")
@@ -182,4 +214,10 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
         attn_cls = ly.Attention
         saved["forward"] = attn_cls.forward
         attn_cls.forward = _make_attention_forward(saved["forward"])
-    return Installed(ta, pool_cls, saved, cg, attn_cls)
+    eng_cls = None
+    if eager_inputs:
+        pe = paged_engine or importlib.import_module("infrared.engine.paged_engine")
+        eng_cls = pe.PagedBatchEngine
+        saved["eager"] = eng_cls._decode_logits_eager
+        eng_cls._decode_logits_eager = _make_decode_logits_eager(saved["eager"], pk.PagedContext)
+    return Installed(ta, pool_cls, saved, cg, attn_cls, eng_cls)

@@ -366,3 +366,87 @@ def test_shim_routes_prefill_frames_when_enabled():
     check_device_errors()
     diff = (outs[True].float() - outs[False].float()).abs().max().item()
     assert diff < 2e-2
+
+
+# ---------------------------------------------------------------- eager decode inputs
+
+
+class _Rec:
+    """A stand-in engine with the attributes _decode_logits_eager reads; its
+    model records the forward's inputs."""
+
+    def __init__(self, device, dtype, bs):
+        import types as _t
+
+        self.block_size = bs
+        self.enable_triton_attention = True
+        self.pool = object()
+        self.calls = []
+
+        def forward(ids, positions, mask, paged):
+            self.calls.append((ids, positions, mask, paged))
+            return torch.zeros(ids.shape[0], 1, 7, device=ids.device)
+
+        self.model = _t.SimpleNamespace(device=device, dtype=dtype, forward=forward)
+
+
+def _running(rng, n, bs, num_blocks):
+    import types as _t
+
+    perm = list(rng.permutation(num_blocks))
+    seqs = []
+    for _ in range(n):
+        nc = int(rng.integers(0, 90))
+        seqs.append(_t.SimpleNamespace(num_cached_tokens=nc, last_token=int(rng.integers(0, 999)),
+                                       block_table=[int(perm.pop()) for _ in range(nc // bs + 1)]))
+    return seqs
+
+
+def test_eager_inputs_cpu_falls_through(infrared):
+    ta, pk, cg = infrared
+    import infrared.engine.paged_engine as pe
+
+    sentinel = object()
+    h = shim.install(ta, pk, cg, paged_engine=pe, eager_inputs=True)
+    try:
+        eng = _Rec("cpu", torch.float32, 4)
+        calls = []
+        orig = h.saved["eager"]
+        h.saved["eager"] = lambda self, running: calls.append(running) or sentinel
+        # rebuild the replacement around the stub to see the fall-through
+        fn = shim._make_decode_logits_eager(h.saved["eager"], pk.PagedContext)
+        assert fn(eng, [1, 2]) is sentinel and calls == [[1, 2]]
+        h.saved["eager"] = orig
+    finally:
+        h.uninstall()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_eager_inputs_built_on_device(dtype):
+    """The eager decode step's forward inputs, built by ir_build_decode_inputs,
+    equal infrared's per-sequence construction (restated in the oracle)."""
+    from infrared_b200 import PagedContext
+
+    rng = np.random.default_rng(5)
+    bs = 8
+    running = _running(rng, 6, bs, 128)
+    eng = _Rec(torch.device("cuda"), dtype, bs)
+    fn = shim._make_decode_logits_eager(lambda *a: pytest.fail("fell through"), PagedContext)
+    out = fn(eng, running)
+    assert out.shape == (6, 7)
+    ids, positions, mask, paged = eng.calls[0]
+    ctx = [s.num_cached_tokens + 1 for s in running]
+    want = orc.build_decode_inputs([s.block_table for s in running],
+                                   [s.num_cached_tokens for s in running],
+                                   [s.last_token for s in running], len(running), max(ctx), bs)
+    np.testing.assert_array_equal(ids.cpu().numpy(), want["ids"])
+    np.testing.assert_array_equal(positions.cpu().numpy(), want["positions"])
+    np.testing.assert_array_equal(paged.write_slots.cpu().numpy(), want["write_slots"])
+    np.testing.assert_array_equal(paged.gather_slots.cpu().numpy(), want["gather_slots"])
+    m = mask.float().cpu().numpy()
+    blocked = want["mask"] != 0
+    assert (m[~blocked] == 0).all()
+    assert (m[blocked] == float(torch.finfo(dtype).min)).all()
+    assert paged.use_triton
