@@ -46,6 +46,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128, O at 256
 constexpr float kRescaleLog2 = 8.f;  // move the reference max when it grows by > 2^8
 
+
 template <int D>
 struct PLayout {
   static constexpr int kHalves = D / 64;
@@ -350,13 +351,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float mx;
       {
-        float t8[8];
+        float t4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-        for (int k = 0; k < 8; ++k) t8[k] = v[k];
+        for (int i = 4; i < 64; i += 8) {
 #pragma unroll
-        for (int i = 8; i < 64; ++i) t8[i & 7] = fmaxf(t8[i & 7], v[i]);
-        mx = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
-                   fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
+          for (int k = 0; k < 4; ++k) t4[k] = max3(t4[k], v[i + 2 * k], v[i + 2 * k + 1]);
+        }
+        mx = max3(fmaxf(t4[0], t4[1]), t4[2], t4[3]);
       }
       // the row max over both halves (the partner thread holds the other 64 keys)
       red[kh * kRows + r] = mx;
@@ -376,17 +377,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this half's keys are the 64-column half kh of the P tile
       uint8_t* prow =
           smem + L::off_p + b * L::kP + kh * L::kHalf + (r >> 3) * 1024 + (r & 7) * 128;
-      float s8[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) s8[k] = 0.f;
+      // x = s * scale_log2 - m and the running sums, two keys per instruction
+      const unsigned long long sc2 = f2pack(a.scale_log2, a.scale_log2);
+      const unsigned long long nm2 = f2pack(-m_use, -m_use);
+      unsigned long long s2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // 16-byte chunks of 8 keys
         uint32_t pk[4];
 #pragma unroll
         for (int i = 0; i < 8; i += 2) {
-          const float p0 = ex2(fmaf(v[c * 8 + i], a.scale_log2, -m_use));
-          const float p1 = ex2(fmaf(v[c * 8 + i + 1], a.scale_log2, -m_use));
-          s8[c] += p0 + p1;
+          const float2 x = f2unpack(fma2(f2pack(v[c * 8 + i], v[c * 8 + i + 1]), sc2, nm2));
+          const float p0 = ex2(x.x);
+          const float p1 = ex2(x.y);
+          s2[i >> 1] = add2(s2[i >> 1], f2pack(p0, p1));
           pk[i >> 1] = pack2<T>(p0, p1);
         }
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
@@ -429,7 +432,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_shared();
       tc::fence_before_sync();
       mbar_arrive(&p_full[b]);
-      const float sum = ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      const float2 u0 = f2unpack(add2(s2[0], s2[1]));
+      const float2 u1 = f2unpack(add2(s2[2], s2[3]));
+      const float sum = (u0.x + u0.y) + (u1.x + u1.y);
       l = fmaf(l, factor, sum);
       m_ref = m_new;
       // a failed wait in this tile is acted on at the next tile's meeting
