@@ -805,7 +805,10 @@ int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v
         !make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads, s->head_dim, s->dtype,
                        rows))
       return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-    int e = irb::launch_prefill_tc(tmq, tmk, tmv, a, s->dtype, st);
+    int sms = 0;
+    int rc2 = cached(-1, sm_count_now, 0, &sms);
+    if (rc2) return cuda_status(rc2, "device query");
+    int e = irb::launch_prefill_tc(tmq, tmk, tmv, a, s->dtype, sms > 0 ? sms : 148, st);
     return cuda_status(e, "prefill kernel launch");
   }
   // rows as decode rows: each query row is a sequence of context position + 1

@@ -31,7 +31,7 @@ struct PrefillArgs {
 // >= 8; tmq views q as (D, H, total_q), tmk/tmv the pools as (D, Hkv, slots)
 // with boxes {64, 1, 128} and {64, 1, min(bs, 128)} (128-byte swizzle).
 int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
-                      const PrefillArgs& a, int dtype, cudaStream_t stream);
+                      const PrefillArgs& a, int dtype, int sm_count, cudaStream_t stream);
 
 // decode_tma.cu: 16-bit pools, D in {64, 128}, group <= 8, bs == 8 or bs % 16 == 0.
 // One CTA covers tma_head_group(Hkv) kv heads; one_box selects the 4-D
