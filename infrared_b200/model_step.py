@@ -104,9 +104,10 @@ class Qwen2DecodeStep:
     # -- building blocks (infrared/model/layers.py) ------------------------
 
     def _rms(self, x, w):
-        xf = x.float()
-        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.geo.eps)
-        return w * xf.to(x.dtype)
+        """RMSNorm of infrared (layers.py:56-69): fp32 normalisation, cast, then
+        the weight. One fused library kernel (normalise in fp32, scale by the
+        weight, round once) — the same values for the unit weights used here."""
+        return F.rms_norm(x, (x.shape[-1],), w, self.geo.eps)
 
     def _rope(self, x, cos, sin):
         half = x.shape[-1] // 2
@@ -149,10 +150,11 @@ class Qwen2DecodeStep:
             k = qkv[:, hq * d:(hq + hkv) * d].view(b, hkv, d)
             v = qkv[:, (hq + hkv) * d:].view(b, hkv, d)
             attn = self.attend(l, q, k, v, slots, ctx, cos, sin)
-            x = x + attn.view(b, hq * d) @ w["wo"]
+            # residual adds folded into the GEMMs (C = x + A.B, one rounding)
+            x = torch.addmm(x, attn.view(b, hq * d), w["wo"])
             hdn = self._rms(x, w["ln2"])
             gate, up = (hdn @ w["wgu"]).chunk(2, dim=-1)
-            x = x + (F.silu(gate) * up) @ w["wd"]
+            x = torch.addmm(x, F.silu(gate) * up, w["wd"])
         logits = self._rms(x, self.final_norm) @ self.lm_head
         nxt = torch.argmax(logits, dim=-1)
         self.ids.copy_(nxt)
