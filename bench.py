@@ -65,6 +65,8 @@ def parse_args():
     p.add_argument("--soak", type=float, default=1.5,
                    help="seconds of untimed replays before timing (clock sampling)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                   help="c4 over several GPUs: partials by peer stores or an NCCL all-gather")
     p.add_argument("--batch", type=int, default=0,
                    help="override the workload's per-GPU batch (c2/c3/c4)")
     p.add_argument("--decode-path", type=int, default=0,
@@ -528,7 +530,9 @@ def run_reference_prefill(args):
 
 def run_chunked(args):
     """C4 over N GPUs: every sequence's KV split into N chunks, one per GPU;
-    partials all-gathered over NCCL and merged (strong scaling)."""
+    partials exchanged by peer stores over NVLink (``--exchange p2p``, one
+    kernel that also merges) or all-gathered over NCCL and merged
+    (``--exchange nccl``); strong scaling."""
     import torch
     import torch.distributed as dist
 
@@ -548,15 +552,17 @@ def run_chunked(args):
     nsets = max(args.sets, -(-3 * 126 * 2 ** 20 // max(local_bytes, 1)))
     sets = [wl.torch_values(w, 7 + s, dev) for s in range(nsets)]   # same q on every rank
     total_bytes = w.algorithmic_bytes()
+    ex = irdist.PeerExchange(w.batch, w.num_heads, w.head_dim, dev) \
+        if args.exchange == "p2p" else None
 
     def step(i):
         q, kp, vp, _, _ = sets[i % nsets]
-        return irdist.chunked_decode(q, kp, vp, tables, ctx, w.scale, w.block_size)
+        return irdist.chunked_decode(q, kp, vp, tables, ctx, w.scale, w.block_size, exchange=ex)
 
     for i in range(max(args.warmup, 3)):
         step(i)
     torch.cuda.synchronize(dev)
-    # K steps (decode + NCCL all-gather + merge each) in one CUDA graph
+    # K steps (decode + exchange + merge each) in one CUDA graph
     stream = torch.cuda.Stream(dev)
     stream.wait_stream(torch.cuda.current_stream(dev))
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -593,7 +599,8 @@ def run_chunked(args):
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
-        o = irdist.chunked_decode(q_dev, kp0, vp0, tables, ctx, w.scale, w.block_size)
+        o = irdist.chunked_decode(q_dev, kp0, vp0, tables, ctx, w.scale, w.block_size,
+                                  exchange=ex)
         out_host.copy_(o, non_blocking=True)
 
     for _ in range(3):
@@ -617,8 +624,10 @@ def run_chunked(args):
         "data": "synthetic: seeded N(0,1)*0.5 q/K/V, random block tables",
         "config": {"workload": "C4: B=4 x ctx 32768, KV chunked over the GPUs",
                    "global_batch": w.batch, "bytes_per_step_total": total_bytes,
-                   "parallelism": f"KV-chunk split x{world}: partials all-gathered (NCCL) "
-                                  "and log-sum-exp merged on every rank",
+                   "parallelism": f"KV-chunk split x{world}: partials " + (
+                       "stored into every rank's buffer over NVLink (peer stores, "
+                       "epoch-counted arrival)" if ex is not None else
+                       "all-gathered (NCCL)") + ", log-sum-exp merged on every rank",
                    "l2": f"{nsets} rotating pool sets (> 3x L2 between reuses)",
                    "timing": "K steps in one CUDA graph (NCCL captured), CUDA events, "
                              "max over ranks"},
@@ -626,14 +635,16 @@ def run_chunked(args):
         "roofline": {"bound": "hbm", "achieved": round(per_gpu, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(per_gpu / peak, 4), "peak_kind": peak_kind,
                      "traffic": None,
-                     "scope": "one rank: its KV chunk + q/out per step, incl. all-gather"},
+                     "scope": "one rank: its KV chunk + q/out per step, incl. the exchange"},
         "e2e": {"value": round(total_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
                 "unit": "GB/s", "h2d_bytes_per_step": q_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2,
                 "ms_per_step": round(e2e_ms / args.steps, 5)},
         "clocks": clk,
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 3 * args.steps,   # decode, split merge, exchange or lse merge
     }
+    if ex is not None:
+        ex.close()
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:

@@ -374,6 +374,38 @@ int ir_derive_varlen_metadata(const int64_t* gather_slots, int64_t num_keys, con
                               int32_t* context_lens, int32_t* q_start, int32_t* num_seqs,
                               int32_t* scratch, int32_t* err_flag, ir_stream_t stream);
 
+/* ---------------------------------------------------------- peer exchange
+ *
+ * The KV-chunk split over the GPUs of one node (one process per GPU) without
+ * a collective library call: in one kernel, every rank's (o, lse) partial
+ * (ir_paged_decode_lse) is stored over NVLink into every peer's exchange
+ * buffer in 16-byte chunks that carry the call's flag, and each rank merges
+ * the world's partials as soon as their flags arrive (ir_lse_merge's
+ * arithmetic, in rank order, so all ranks write identical rows). No reference
+ * counterpart: infrared is single-GPU. Buffers come from ir_peer_alloc
+ * (zeroed) and are mapped into the other processes with ir_peer_handle /
+ * ir_peer_open; bufs[] lists all world buffers as seen by the calling
+ * process, bufs[rank] being its own. Every rank must make the same sequence
+ * of calls with the same shapes on one stream; the calls may be captured in
+ * a CUDA graph. A peer that stops calling makes the waits run out after 2 s
+ * with IR_DEVERR_TIMEOUT, after which the buffers must be allocated anew.
+ */
+#define IR_PEER_HANDLE_BYTES 64
+int ir_peer_alloc(size_t bytes, void** ptr);
+int ir_peer_free(void* ptr);
+int ir_peer_handle(const void* ptr, void* handle /* IR_PEER_HANDLE_BYTES */);
+int ir_peer_open(const void* handle, void** ptr);
+int ir_peer_close(void* ptr);
+/* Exchange buffer bytes for world ranks, rows = batch * heads, head_dim. */
+size_t ir_peer_exchange_bytes(int world, int rows, int head_dim);
+/* o [batch * num_heads, head_dim] fp32 (16-byte aligned) and lse
+ * [batch * num_heads] fp32 of this rank in; out [batch, num_heads, head_dim]
+ * (row stride out_stride, dtype) = all ranks' partials of this call merged.
+ * head_dim a multiple of 4 up to 128, world 1..8. */
+int ir_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse,
+                     void* const* bufs, int world, int rank, int batch, int num_heads,
+                     int head_dim, int dtype, int32_t* err_flag, ir_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -88,6 +88,14 @@ class PrefillShape(ctypes.Structure):
 # (name, restype, argtypes) of every exported function
 _SIGNATURES = {
     "ir_set_prefill_path": (c_int, [c_int]),
+    "ir_peer_alloc": (c_int, [c_size_t, POINTER(c_void_p)]),
+    "ir_peer_free": (c_int, [c_void_p]),
+    "ir_peer_handle": (c_int, [c_void_p, c_void_p]),
+    "ir_peer_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "ir_peer_close": (c_int, [c_void_p]),
+    "ir_peer_exchange_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "ir_peer_exchange": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, POINTER(c_void_p),
+                                 c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "ir_derive_varlen_metadata": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int,
                                           c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_void_p, c_void_p]),

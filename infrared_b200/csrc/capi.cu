@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 
 #include <map>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -478,6 +479,29 @@ int noalloc_scratch(void** out) {
 
 }  // namespace
 
+namespace {
+
+// Kernel arguments of the peer exchange from the C ABI's arrays.
+int peer_args(void* const* bufs, int world, int rank, int rows, int head_dim, int32_t* err,
+              irb::PeerArgs* a) {
+  if (!bufs || world <= 0 || world > 8 || rank < 0 || rank >= world)
+    return fail(IR_ERR_INVALID_ARG, "world must be 1..8 and rank < world");
+  if (head_dim <= 0 || head_dim > 128 || head_dim % 4 != 0 || rows < 0)
+    return fail(IR_ERR_INVALID_ARG, "head_dim must be a multiple of 4 up to 128");
+  *a = irb::PeerArgs{};
+  for (int i = 0; i < world; ++i) {
+    if (!bufs[i] || !aligned(bufs[i], 256)) return fail(IR_ERR_INVALID_ARG, "bad peer buffer");
+    a->bufs[i] = static_cast<uint8_t*>(bufs[i]);
+  }
+  a->world = world;
+  a->rank = rank;
+  a->rows = rows;
+  a->D = head_dim;
+  a->err = err;
+  return IR_OK;
+}
+}  // namespace
+
 extern "C" {
 
 int ir_version(void) { return 100; }
@@ -829,6 +853,58 @@ int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v
   return decode_impl(Mode::kFinal, out, nullptr, nullptr, q, k_pool, v_pool, nullptr, nullptr, 0,
                      nullptr, row_bt, row_ctx, &d, ws + tb + cb, workspace_bytes - tb - cb,
                      err_flag, st);
+}
+
+// ---------------------------------------------------------------- peer exchange
+
+int ir_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(IR_ERR_INVALID_ARG, "null pointer or zero size");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  return cuda_status(static_cast<int>(e), "peer buffer allocation");
+}
+
+int ir_peer_free(void* ptr) { return cuda_status(static_cast<int>(cudaFree(ptr)), "cudaFree"); }
+
+int ir_peer_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return fail(IR_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e == cudaSuccess) std::memcpy(handle, &h, sizeof(h));
+  return cuda_status(static_cast<int>(e), "cudaIpcGetMemHandle");
+}
+
+int ir_peer_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(IR_ERR_INVALID_ARG, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cuda_status(
+      static_cast<int>(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess)),
+      "cudaIpcOpenMemHandle");
+}
+
+int ir_peer_close(void* ptr) {
+  return cuda_status(static_cast<int>(cudaIpcCloseMemHandle(ptr)), "cudaIpcCloseMemHandle");
+}
+
+size_t ir_peer_exchange_bytes(int world, int rows, int head_dim) {
+  if (world <= 0 || world > 8 || rows < 0 || head_dim <= 0) return 0;
+  return irb::peer_exchange_bytes(world, rows, head_dim);
+}
+
+int ir_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse,
+                     void* const* bufs, int world, int rank, int batch, int num_heads,
+                     int head_dim, int dtype, int32_t* err_flag, ir_stream_t stream) {
+  irb::PeerArgs a;
+  if (batch < 0 || num_heads <= 0) return fail(IR_ERR_INVALID_ARG, "bad batch / num_heads");
+  int rc = peer_args(bufs, world, rank, batch * num_heads, head_dim, err_flag, &a);
+  if (rc) return rc;
+  if (!o || !lse || !aligned(o, 16)) return fail(IR_ERR_INVALID_ARG, "o must be 16-byte aligned");
+  if (!out || elem_bytes(dtype) == 0 || out_stride < static_cast<int64_t>(num_heads) * head_dim)
+    return fail(IR_ERR_INVALID_ARG, "bad output");
+  return cuda_status(irb::launch_peer_exchange(out, out_stride, o, lse, num_heads, dtype, a,
+                                               static_cast<cudaStream_t>(stream)),
+                     "peer exchange launch");
 }
 
 }  // extern "C"

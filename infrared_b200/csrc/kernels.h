@@ -33,6 +33,19 @@ struct PrefillArgs {
 int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
                       const PrefillArgs& a, int dtype, int sm_count, cudaStream_t stream);
 
+// peer_exchange.cu: KV-chunk partials stored into every GPU of the node
+// (buffers mapped with CUDA IPC) in a flagged 16-byte chunk format and merged,
+// in one kernel; see the file header for the buffer layout and the protocol.
+struct PeerArgs {
+  uint8_t* bufs[8];  // every rank's exchange buffer as mapped in this process
+  int world, rank;
+  int rows, D;       // rows = batch * heads
+  int32_t* err;
+};
+size_t peer_exchange_bytes(int world, int rows, int D);
+int launch_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse, int H,
+                         int dtype, const PeerArgs& p, cudaStream_t s);
+
 // decode_tma.cu: 16-bit pools, D in {64, 128}, group <= 8, bs == 8 or bs % 16 == 0.
 // One CTA covers tma_head_group(Hkv) kv heads; one_box selects the 4-D
 // (one copy per tile side) or the 3-D (one copy per head and half) map.

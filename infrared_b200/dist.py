@@ -11,8 +11,12 @@ Two partitionings, neither of which exists in infrared (it is single-GPU):
   its log-sum-exp over that range (``ir_paged_decode_lse``), and one
   all-gather of the fp32 partials (o and lse packed in one buffer:
   ``B*H*(D+1)*4`` bytes per GPU) lets every rank combine them with
-  ``ir_lse_merge``. Data only moves through the collective into each rank's
-  own memory — no kernel reads another GPU's memory.
+  ``ir_lse_merge``; or (``PeerExchange``) each rank stores its partial
+  straight into every rank's exchange buffer over NVLink and merges the
+  world's partials as each 16-byte chunk's flag shows it arrived, in one
+  kernel.
+  Kernels only STORE to peer memory; every read is of the rank's own
+  memory.
 
 The compute steps are parameters of ``chunked_decode`` so the exchange can
 be exercised on CPU ranks (gloo) with the oracle in tests; ``partial_fn``
@@ -81,20 +85,98 @@ def _cuda_merge(o_parts, lse_parts, dtype):
     return ops.lse_merge(o_parts, lse_parts, dtype)
 
 
+class PeerExchange:
+    """Exchange of KV-chunk partials by peer stores (``ir_peer_exchange``)
+    instead of an all-gather: each rank allocates one zeroed exchange
+    buffer, the buffers are mapped into every process with CUDA IPC (handles
+    traded once with ``all_gather_object``), and every call stores this
+    rank's ``(o, lse)`` into all peers' buffers over NVLink and merges the
+    world's partials as their flags arrive, in one kernel. All ranks must call
+    :meth:`merge` the same number of times; :meth:`close` unmaps and frees
+    (collective)."""
+
+    def __init__(self, batch: int, num_heads: int, head_dim: int, device, group=None):
+        import ctypes
+
+        from . import _lib
+        from ._lib import check
+
+        self._lib, self._check = _lib.load(), check
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.batch, self.num_heads, self.head_dim = batch, num_heads, head_dim
+        self.device = torch.device(device)
+        rows = batch * num_heads
+        nbytes = self._lib.ir_peer_exchange_bytes(self.world, rows, head_dim)
+        if nbytes == 0:
+            raise ValueError("unsupported world size or shape for the peer exchange")
+        own = ctypes.c_void_p()
+        check(self._lib.ir_peer_alloc(nbytes, ctypes.byref(own)))
+        handle = (ctypes.c_char * 64)()
+        check(self._lib.ir_peer_handle(own, handle))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        ptrs = []
+        for r, hd in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(own.value)
+            else:
+                pp = ctypes.c_void_p()
+                check(self._lib.ir_peer_open(ctypes.c_char_p(hd), ctypes.byref(pp)))
+                ptrs.append(pp.value)
+        self._own = own.value
+        self._ptrs = ptrs
+        self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
+        dist.barrier(group=group)
+
+    def merge(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Push ``o [B, H, D]`` / ``lse [B, H]`` (fp32, contiguous) of this rank and
+        write the combined result of all ranks into ``out [B, H, D]``."""
+        from .ops import _dev_index, _stream, dtype_code, error_flag
+
+        dev = _dev_index(o)
+        err = error_flag(dev).data_ptr()
+        stream = _stream(dev)
+        self._check(self._lib.ir_peer_exchange(out.data_ptr(), out.stride(0), o.data_ptr(),
+                                               lse.data_ptr(), self._bufs, self.world, self.rank,
+                                               self.batch, self.num_heads, self.head_dim,
+                                               dtype_code(out.dtype), err, stream))
+        return out
+
+    def close(self) -> None:
+        if self._ptrs is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for r, ptr in enumerate(self._ptrs):
+            if r != self.rank:
+                self._check(self._lib.ir_peer_close(ptr))
+        dist.barrier(group=self.group)
+        self._check(self._lib.ir_peer_free(self._own))
+        self._ptrs = None
+
+
 def chunked_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                    tables: torch.Tensor, ctx: torch.Tensor, scale: float, block_size: int,
                    out_dtype: torch.dtype | None = None, group=None,
-                   partial_fn=_cuda_partial, merge_fn=_cuda_merge) -> torch.Tensor:
+                   partial_fn=_cuda_partial, merge_fn=_cuda_merge,
+                   exchange: PeerExchange | None = None) -> torch.Tensor:
     """Decode attention of ``q [B, H, D]`` over a KV range held on this rank,
     combined across all ranks of ``group``; every rank returns the full
     ``[B, H, D]`` result. Each rank passes its own ``tables``/``ctx``
-    (``kv_chunk_tables``) and pool; ``q`` is the same on every rank."""
+    (``kv_chunk_tables``) and pool; ``q`` is the same on every rank. With an
+    ``exchange`` the partials move by peer stores (:class:`PeerExchange`),
+    otherwise by one NCCL all-gather."""
     b, h, d = q.shape
     world = dist.get_world_size(group)
     packed = torch.empty(b * h * (d + 1), dtype=torch.float32, device=q.device)
     o = packed[: b * h * d].view(b, h, d)
     lse = packed[b * h * d:].view(b, h)
     partial_fn(q, k_pool, v_pool, tables, ctx, scale, block_size, o, lse)
+    if exchange is not None:
+        out = torch.empty((b, h, d), dtype=out_dtype or q.dtype, device=q.device)
+        return exchange.merge(o, lse, out)
     gathered = torch.empty(world * packed.numel(), dtype=torch.float32, device=q.device)
     dist.all_gather_into_tensor(gathered, packed, group=group)
     gathered = gathered.view(world, packed.numel())

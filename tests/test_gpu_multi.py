@@ -1,0 +1,100 @@
+"""KV-chunk decode over 2 GPUs: the peer-store exchange against the NCCL
+all-gather path and the single-GPU decode (needs 2 GPUs; skipped otherwise).
+
+Each rank is a spawned process on its own GPU. Bars: the peer exchange equals
+the NCCL path within fp32 merge rounding (1e-3) and the single-GPU decode
+within the bf16 bar (2e-2); repeated calls (the exchange's epoch counters
+advancing) and CUDA-graph replays give the same result every time.
+"""
+
+import datetime
+import socket
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs 2 GPUs")]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    import torch.distributed as dist
+
+    import infrared_b200 as irb
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import ops
+    from infrared_b200 import workloads as wl
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", world_size=world,
+                            rank=rank, device_id=dev, timeout=datetime.timedelta(seconds=60))
+    res = {}
+    try:
+        w = wl.c4(seed=0, batch=3, ctx_len=4608)
+        q, kp, vp, _, _ = wl.torch_values(w, 7, dev)
+        tables_np, ctx_np, _ = irdist.kv_chunk_tables(w.block_tables, w.context_lens,
+                                                      w.block_size, world, rank)
+        tables = torch.from_numpy(tables_np).to(dev)
+        ctx = torch.from_numpy(ctx_np).to(dev)
+        full = irb.paged_decode(q, kp, vp, torch.from_numpy(w.block_tables).to(dev),
+                                torch.from_numpy(w.context_lens).to(dev), w.scale, w.block_size)
+        ref = irdist.chunked_decode(q, kp, vp, tables, ctx, w.scale, w.block_size)
+        ex = irdist.PeerExchange(w.batch, w.num_heads, w.head_dim, dev)
+        outs = [irdist.chunked_decode(q, kp, vp, tables, ctx, w.scale, w.block_size,
+                                      exchange=ex) for _ in range(6)]
+        torch.cuda.synchronize()
+        res["p2p_vs_nccl"] = (outs[0].float() - ref.float()).abs().max().item()
+        res["p2p_vs_full"] = (outs[0].float() - full.float()).abs().max().item()
+        res["repeat_equal"] = all(torch.equal(outs[0], o) for o in outs[1:])
+        # captured in a CUDA graph and replayed: epochs advance on the device
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                cap = irdist.chunked_decode(q, kp, vp, tables, ctx, w.scale, w.block_size,
+                                            exchange=ex)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        eq = True
+        for _ in range(3):
+            g.replay()
+            torch.cuda.synchronize()
+            eq = eq and torch.equal(cap, outs[0])
+        res["graph_equal"] = eq
+        del g
+        ops.check_device_errors()
+        res["errors"] = 0
+        ex.close()
+    except Exception as e:  # noqa: BLE001 - reported to the parent test
+        res["exception"] = repr(e)
+    finally:
+        dist.destroy_process_group()
+    results.put((rank, res))
+
+
+def test_peer_exchange_two_gpus():
+    ctx = torch.multiprocessing.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, res = results.get(timeout=300)
+        got[rank] = res
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res in sorted(got.items()):
+        assert "exception" not in res, f"rank {rank}: {res}"
+        assert res["p2p_vs_nccl"] < 1e-3, res
+        assert res["p2p_vs_full"] < 2e-2, res
+        assert res["repeat_equal"] and res["graph_equal"], res
