@@ -1,5 +1,6 @@
-"""KV-chunk decode over 2 GPUs: the peer-store exchange against the NCCL
-all-gather path and the single-GPU decode (needs 2 GPUs; skipped otherwise).
+"""KV-chunk decode over 2-4 GPUs (as many as the box has, at most 4): the
+peer-store exchange against the NCCL all-gather path and the single-GPU
+decode (needs 2 GPUs; skipped otherwise).
 
 Each rank is a spawned process on its own GPU. Bars: the peer exchange equals
 the NCCL path within fp32 merge rounding (1e-3) and the single-GPU decode
@@ -80,15 +81,16 @@ def _worker(rank, world, port, results):
     results.put((rank, res))
 
 
-def test_peer_exchange_two_gpus():
+def test_peer_exchange_gpus():
+    world = min(torch.cuda.device_count(), 4)
     ctx = torch.multiprocessing.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
-    for _ in range(2):
+    for _ in range(world):
         rank, res = results.get(timeout=300)
         got[rank] = res
     for p in procs:
