@@ -412,12 +412,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float mx;
         {
+          // four independent chains: v[0..3], then v[4..59] eight at a time, then v[60..63]
           float t4[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
-          for (int i = 4; i < 64; i += 8) {
+          for (int i = 4; i < 60; i += 8) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) t4[k] = max3(t4[k], v[i + 2 * k], v[i + 2 * k + 1]);
           }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) t4[k] = fmaxf(t4[k], v[60 + k]);
           mx = max3(fmaxf(t4[0], t4[1]), t4[2], t4[3]);
         }
         // the row max over both halves (the partner thread holds the other 64 keys)
