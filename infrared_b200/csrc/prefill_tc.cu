@@ -6,29 +6,29 @@
 // table from the paged K/V pool (the causal / varlen masks of
 // infrared/model/inputs.py:38-94 applied to infrared's paged read).
 //
-// One CTA = 128 query rows of one sequence for one query head (grid:
-// q tiles x heads). Eleven warps:
+// Work item = 128 query rows of one sequence for one query head; one
+// persistent CTA per SM walks the items, longest first. Eleven warps:
 //   warps 8, 9  producers: TMA copies of the Q tile (once) and of each
 //               128-key K tile (warp 8) and V tile (warp 9), one box per
 //               block and 64-column half, into rings of NS stages; the
 //               block-table lookups are spread over the lanes and done one
 //               tile ahead;
 //   warp 10     MMA issuer (one thread): S = Q.K^T (M=128, N=128 keys,
-//               K=D) into one of two TMEM buffers, and O += P.V (M=128,
-//               N=D, K=128 keys) into the TMEM accumulator, tcgen05.mma
-//               kind::f16 with operands in 128-byte-swizzled shared memory;
-//               tcgen05.commit releases stages and signals the softmax;
-//   warps 0-7   softmax: two threads per query row r (= TMEM lane r; warps
-//               w and w + 4 share rows 32 (w % 4) ..), each takes 64 of the
-//               tile's 128 keys: one 64-column TMEM load of its scores,
-//               masked max (combined with the partner's through shared
-//               memory), exp2 probabilities written as 16-bit P into one of
-//               two shared-memory buffers (the A operand of the P.V MMA) and
+//               K=D) into one of three TMEM buffers, two tiles ahead, and
+//               O += P.V (M=128, N=D, K=128 keys) into the TMEM accumulator,
+//               tcgen05.mma kind::f16 with operands in 128-byte-swizzled
+//               shared memory; tcgen05.commit releases stages and signals
+//               the softmax;
+//   warps 0-7   softmax, two warpgroups taking alternate K/V tiles: thread r
+//               of a warpgroup owns query row r (= TMEM lane r) and all 128
+//               keys of its tiles: TMEM loads of its scores, masked max,
+//               exp2 probabilities written as 16-bit P into the warpgroup's
+//               shared-memory P buffer (the A operand of the P.V MMA) and
 //               their running sum. P is taken relative to a reference max
 //               that moves only when the row max grows by more than 2^8
-//               (then the row of O in TMEM and the sum are rescaled), so
-//               the accumulator is rarely touched and the P.V MMA of tile j
-//               overlaps the softmax of tile j + 1.
+//               (then the row of O in TMEM is rescaled); the reference is
+//               handed from tile to tile through shared memory, so the two
+//               warps sharing a scheduler work on different tiles at once.
 // Every wait is bounded (2 s); on a timeout the CTA flags IR_DEVERR_TIMEOUT,
 // lets its copies and MMAs drain (bounded), frees its tensor memory and ends.
 #include "tcgen05.cuh"
@@ -40,10 +40,11 @@ namespace {
 
 constexpr int kRows = 128;     // query rows per CTA (MMA M)
 constexpr int kKeys = 128;     // keys per K/V tile
-constexpr int kThreads = 352;  // warps 0-7 softmax, 8-9 producers, 10 MMA
-constexpr int kSoftmax = 256;  // softmax threads: 2 per query row (one per 64-key half)
+constexpr int kThreads = 352;  // warps 0-7 softmax (two warpgroups), 8-9 producers, 10 MMA
+constexpr int kWgThreads = 128;  // one softmax warpgroup: one thread per query row
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;  // S buffers at columns 0 and 128, O at 256
+constexpr int kSBuf = 3;  // S buffers: Q.K^T runs two tiles ahead of the softmax
+constexpr uint32_t kColO = kSBuf * kKeys;  // S buffers at columns 0, 128, 256; O at 384
 constexpr float kRescaleLog2 = 8.f;  // move the reference max when it grows by > 2^8
 
 
@@ -60,12 +61,14 @@ struct PLayout {
   static constexpr int off_v = off_k + NS * kSide;
   static constexpr int off_p = off_v + NS * kSide;       // two P buffers
   static constexpr int off_bar = off_p + 2 * kP;
-  // q_full, q_empty, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[2],
-  // s_free[2], p_full[2], p_done[2], o_free, drain
-  static constexpr int kBars = 2 + 4 * NS + 10;
+  // q_full, q_empty, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[kSBuf],
+  // s_free[kSBuf], p_full[2], p_done[2], o_free, drain, ref_full[2], l_ready
+  static constexpr int kBars = 2 + 4 * NS + 2 * kSBuf + 9;
   static constexpr int off_misc = off_bar + kBars * 8;
-  static constexpr int off_red = off_misc + 64;         // [2 halves][128 rows] fp32 exchange
-  static constexpr int kBytes = off_red + 2 * kRows * 4;
+  // reference max per row after tile g, [g & 1][128 rows], then the row sums one
+  // softmax warpgroup hands to the other at the end of an item [128 rows]
+  static constexpr int off_ref = off_misc + 64;
+  static constexpr int kBytes = off_ref + 3 * kRows * 4;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
 };
 
@@ -155,12 +158,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* k_empty = k_full + NS;
   uint64_t* v_full = k_empty + NS;
   uint64_t* v_empty = v_full + NS;
-  uint64_t* s_full = v_empty + NS;  // [2] S buffer b holds tile g (g % 2 == b)
-  uint64_t* s_free = s_full + 2;    // [2] the softmax has read S buffer b
-  uint64_t* p_full = s_free + 2;    // [2] P buffer b written (and O rescaled)
-  uint64_t* p_done = p_full + 2;    // [2] the P.V MMA reading P buffer b completed
-  uint64_t* o_free = p_done + 2;    // the softmax has read the item's O
+  uint64_t* s_full = v_empty + NS;    // [kSBuf] S buffer b holds tile g (g % kSBuf == b)
+  uint64_t* s_free = s_full + kSBuf;  // [kSBuf] the softmax has read S buffer b
+  uint64_t* p_full = s_free + kSBuf;  // [2] P buffer b written (and O rescaled)
+  uint64_t* p_done = p_full + 2;      // [2] the P.V MMA reading P buffer b completed
+  uint64_t* o_free = p_done + 2;      // the softmax has read the item's O
   uint64_t* drain = o_free + 1;
+  uint64_t* ref_full = drain + 1;     // [2] the reference max after tile g is in sref[g & 1]
+  uint64_t* l_ready = ref_full + 2;   // the other warpgroup's row sums are in lsum
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::off_misc);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -173,14 +178,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kSBuf; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], kSoftmax);
-      mbar_init(&p_full[i], kSoftmax);
-      mbar_init(&p_done[i], 1);
+      mbar_init(&s_free[i], kWgThreads);
     }
-    mbar_init(o_free, kSoftmax);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], kWgThreads);
+      mbar_init(&p_done[i], 1);
+      mbar_init(&ref_full[i], kWgThreads);
+    }
+    mbar_init(o_free, kWgThreads);
     mbar_init(drain, 1);
+    mbar_init(l_ready, kWgThreads);
     fence_mbar_init();
   }
   if (threadIdx.x == 64) {
@@ -290,9 +299,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (x.s < 0) continue;
       if (lane == 0) {
         auto issue_qk = [&](int gg, int j) -> bool {
-          const int st = gg % NS, sb = gg & 1;
+          const int st = gg % NS, sb = gg % kSBuf;
           if (!mbar_wait_bounded(&k_full[st], (gg / NS) & 1)) return false;
-          if (!mbar_wait_bounded(&s_free[sb], ((gg >> 1) & 1) ^ 1)) return false;
+          if (!mbar_wait_bounded(&s_free[sb], ((gg / kSBuf) & 1) ^ 1)) return false;
           tc::fence_after_sync();
           const uint32_t kb = smem_u32(smem + L::off_k + st * L::kSide);
 #pragma unroll
@@ -327,10 +336,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::commit(&v_empty[st]);
           return true;
         };
+        // Q.K^T of tile j + 2 is queued ahead of P.V of tile j: the next S
+        // never waits in the tensor pipe behind a P.V that waits for a softmax
         ok = mbar_wait_bounded(q_full, ii & 1);
         if (ok) ok = issue_qk(g, 0);
+        if (ok && x.n_kv > 1) ok = issue_qk(g + 1, 1);
         for (int j = 0; j < x.n_kv && ok; ++j) {
-          if (j + 1 < x.n_kv) ok = issue_qk(g + j + 1, j + 1);
+          if (j + 2 < x.n_kv) ok = issue_qk(g + j + 2, j + 2);
           if (ok) ok = issue_pv(g + j, j);
         }
       }
@@ -349,35 +361,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------- softmax
+    // Two warpgroups take alternate K/V tiles (warpgroup g & 1 takes the
+    // CTA's tile g); thread r of a warpgroup owns query row r (= TMEM lane r)
+    // and all 128 keys of its tiles, so the two warps that share a scheduler
+    // work on different tiles and overlap. What crosses from one tile to the
+    // next is the row's reference max: tile g stores the reference its P
+    // values use in sref[g & 1] and arrives on ref_full[g & 1]; tile g + 1
+    // waits for it. (Slot g & 1 is written again by tile g + 2 only after
+    // that tile has seen tile g + 1's reference, which tile g + 1 published
+    // after reading slot g & 1.) Each warpgroup keeps its own row sums; at the
+    // end of an item the other warpgroup hands its sums to the warpgroup of
+    // the item's last tile through lsum / l_ready, and that one normalises
+    // and writes the item's rows and releases O.
+    const int wg = warp >> 2;
     const int r = threadIdx.x & (kRows - 1);  // query row = TMEM lane
-    const int kh = threadIdx.x >> 7;          // which 64 keys of each tile
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    float* red = reinterpret_cast<float*>(smem + L::off_red);  // [2][128]
-    // The two warps of a row group meet at named barrier 1 + warp % 4 (64
-    // threads). They leave the loops together, right after such a meeting
-    // whose AND of "all waits succeeded" is false, so neither can wait at a
-    // barrier the other will not reach.
-    const uint32_t pair_bar = 1 + (warp & 3);
-    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(pair_bar) : "memory"); };
-    auto pair_and = [&](bool v) {
-      uint32_t o;
-      asm volatile(
-          "{\n\t.reg .pred pi, po;\n\t"
-          "setp.ne.u32 pi, %1, 0;\n\t"
-          "bar.red.and.pred po, %2, 64, pi;\n\t"
-          "selp.u32 %0, 1, 0, po;\n\t}"
-          : "=r"(o)
-          : "r"(v ? 1u : 0u), "r"(pair_bar)
-          : "memory");
-      return o != 0;
-    };
-    constexpr int kDh = D / 2;  // O columns this thread rescales / writes
-    // tcgen05.ld / st are warp-collective: every wait result is made warp-uniform
-    auto wait_all = [&](uint64_t* bar, uint32_t par) {
-      return __all_sync(0xffffffffu, mbar_wait_bounded(bar, par));
-    };
+    float* sref = reinterpret_cast<float*>(smem + L::off_ref);  // [2][128]
+    float* lsum = sref + 2 * kRows;                              // [128]
     bool ok = true;
-    int g = 0;
+    // tcgen05.ld / st are warp-collective: every wait result is warp-uniform;
+    // after a failed wait the remaining waits are skipped (arrivals go on), so
+    // the walk ends quickly and the other roles' bounded waits end theirs
+    auto wait_all = [&](uint64_t* bar, uint32_t par) {
+      if (!ok) return false;
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, par));
+      return ok;
+    };
+    const unsigned long long sc2 = f2pack(a.scale_log2, a.scale_log2);
+    // keys past this row's limit exist only in the diagonal tiles: -inf there
+    auto mask = [&](float (&v)[64], int k0, int lim) {
+      if (k0 + 63 > lim) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (k0 + i > lim) v[i] = -INFINITY;
+      }
+    };
+    auto half_max = [&](const float (&v)[64]) {
+      // four independent chains: v[0..3], then v[4..59] eight at a time, then v[60..63]
+      float t4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+      for (int i = 4; i < 60; i += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) t4[k] = max3(t4[k], v[i + 2 * k], v[i + 2 * k + 1]);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) t4[k] = fmaxf(t4[k], v[60 + k]);
+      return max3(fmaxf(t4[0], t4[1]), t4[2], t4[3]);
+    };
+    // p = 2^(s * scale_log2 - m) for 64 keys, written as 16-bit P into the
+    // 64-column half h of P buffer b (128-byte swizzle), summed two at a time
+    auto exp_store = [&](const float (&v)[64], int b, int h, unsigned long long nm2,
+                         unsigned long long (&s2)[4]) {
+      uint8_t* prow = smem + L::off_p + b * L::kP + h * L::kHalf + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 16-byte chunks of 8 keys
+        uint32_t pk[4];
+#pragma unroll
+        for (int i = 0; i < 8; i += 2) {
+          const float2 xx = f2unpack(fma2(f2pack(v[c * 8 + i], v[c * 8 + i + 1]), sc2, nm2));
+          const float p0 = ex2(xx.x);
+          const float p1 = ex2(xx.y);
+          s2[i >> 1] = add2(s2[i >> 1], f2pack(p0, p1));
+          pk[i >> 1] = pack2<T>(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    };
+    int g = 0, ii = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       const Item x = item_of(a, it, lane);
       if (x.s == -1) break;
@@ -387,108 +438,84 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int pos = x.pos0 + r;
       const int lim = min(pos, x.ctx - 1);  // last key this row may attend
-      float m_ref = -INFINITY;  // reference max of the P values (log2 units)
-      float l = 0.f;            // this half's share of the row sum
-      for (int j = 0; j < x.n_kv; ++j) {
+      const int gl = g + x.n_kv - 1;        // the item's last tile
+      float l = 0.f;           // this warpgroup's part of the row sum, relative to m_l
+      float m_l = -INFINITY;   // the reference of this warpgroup's last tile
+      for (int j = (wg - g) & 1; j < x.n_kv; j += 2) {
         const int gg = g + j;
-        const int b = gg & 1;
-        const int kbase = j * kKeys + kh * 64;
+        const int b = gg & 1;         // P buffer and reference slot (== wg)
+        const int sb = gg % kSBuf;    // S buffer
+        const int k0 = j * kKeys;
         float v[64];
-        if (wait_all(&s_full[b], (gg >> 1) & 1)) {
+        // the row max over the tile: keys 0-63, then 64-127 (kept in registers)
+        float mx = -INFINITY;
+        if (wait_all(&s_full[sb], (gg / kSBuf) & 1)) {
           tc::fence_after_sync();
-          tc::ld64(lane_addr + b * kKeys + kh * 64, v);
-          tc::fence_before_sync();
-          mbar_arrive(&s_free[b]);
+          tc::ld64(lane_addr + sb * kKeys, v);
+          mask(v, k0, lim);
+          mx = half_max(v);
+          // the first half's max is taken before the second half is loaded:
+          // 64 scores live at a time, not 128
+          asm volatile("" ::"f"(mx));
+          tc::ld64(lane_addr + sb * kKeys + 64, v);
+          mask(v, k0 + 64, lim);
+          mx = fmaxf(mx, half_max(v)) * a.scale_log2;
         } else {
-          ok = false;
 #pragma unroll
           for (int i = 0; i < 64; ++i) v[i] = -INFINITY;
         }
-        // keys past this row's limit exist only in the diagonal tiles: -inf there
-        if (kbase + 63 > lim) {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (kbase + i > lim) v[i] = -INFINITY;
-        }
-        float mx;
-        {
-          // four independent chains: v[0..3], then v[4..59] eight at a time, then v[60..63]
-          float t4[4] = {v[0], v[1], v[2], v[3]};
-#pragma unroll
-          for (int i = 4; i < 60; i += 8) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) t4[k] = max3(t4[k], v[i + 2 * k], v[i + 2 * k + 1]);
-          }
-#pragma unroll
-          for (int k = 0; k < 4; ++k) t4[k] = fmaxf(t4[k], v[60 + k]);
-          mx = max3(fmaxf(t4[0], t4[1]), t4[2], t4[3]);
-        }
-        // the row max over both halves (the partner thread holds the other 64 keys)
-        red[kh * kRows + r] = mx;
-        if (!pair_and(ok)) {
-          ok = false;
-          break;
-        }
-        mx = fmaxf(mx, red[(kh ^ 1) * kRows + r]) * a.scale_log2;
-        pair_sync();  // both read before the next tile's write
-        // move the reference max only when it has grown by more than 2^8
-        const bool move = mx > m_ref + kRescaleLog2;
-        const float m_new = move ? mx : m_ref;
-        const float factor = ex2(m_ref - m_new);  // 0 on the first tile, 1 if not moved
+        // the reference of the previous tile (none at an item's first tile)
+        float prev = -INFINITY;
+        if (gg > 0 && wait_all(&ref_full[(gg - 1) & 1], ((gg - 1) >> 1) & 1) && j > 0)
+          prev = sref[((gg - 1) & 1) * kRows + r];
+        // move the reference only when the max has grown by more than 2^8
+        const bool move = mx > prev + kRescaleLog2;
+        const float m_new = move ? mx : prev;
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        sref[b * kRows + r] = m_use;
+        mbar_arrive(&ref_full[b]);
         // P buffer b is free once the P.V MMA of tile gg - 2 has completed
-        if (gg >= 2 && !wait_all(&p_done[b], ((gg - 2) >> 1) & 1)) ok = false;
-        // this half's keys are the 64-column half kh of the P tile
-        uint8_t* prow =
-            smem + L::off_p + b * L::kP + kh * L::kHalf + (r >> 3) * 1024 + (r & 7) * 128;
-        // x = s * scale_log2 - m and the running sums, two keys per instruction
-        const unsigned long long sc2 = f2pack(a.scale_log2, a.scale_log2);
+        if (gg >= 2) wait_all(&p_done[b], ((gg - 2) >> 1) & 1);
         const unsigned long long nm2 = f2pack(-m_use, -m_use);
         unsigned long long s2[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {  // 16-byte chunks of 8 keys
-          uint32_t pk[4];
-#pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            const float2 xx = f2unpack(fma2(f2pack(v[c * 8 + i], v[c * 8 + i + 1]), sc2, nm2));
-            const float p0 = ex2(xx.x);
-            const float p1 = ex2(xx.y);
-            s2[i >> 1] = add2(s2[i >> 1], f2pack(p0, p1));
-            pk[i >> 1] = pack2<T>(p0, p1);
-          }
-          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
-              make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        }
-        // rows whose reference moved: O *= factor (after the P.V of tile gg - 1,
-        // of this item); this thread rescales its half of the columns
-        bool rescale = j > 0 && __any_sync(0xffffffffu, move);
-        if (rescale && !wait_all(&p_done[(gg - 1) & 1], ((gg - 1) >> 1) & 1)) {
-          ok = false;
-          rescale = false;
-        }
-        if (rescale) {
+        exp_store(v, b, 1, nm2, s2);
+        asm volatile("" ::: "memory");  // keys 64-127 are stored before anything below
+        // rows whose reference moved: O *= 2^(prev - m_use), after the P.V of
+        // tile gg - 1 (this item's) and before this tile's
+        if (j > 0 && __any_sync(0xffffffffu, move) &&
+            wait_all(&p_done[(gg - 1) & 1], ((gg - 1) >> 1) & 1)) {
           tc::fence_after_sync();
-          const float f = move ? factor : 1.f;
+          const float f = move ? ex2(prev - m_use) : 1.f;
 #pragma unroll
-          for (int c = 0; c < kDh / 32; ++c) {
+          for (int c = 0; c < D / 32; ++c) {
             float o[32];
-            const uint32_t col = kColO + kh * kDh + c * 32;
+            const uint32_t col = kColO + c * 32;
             tc::ld32(lane_addr + col, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= f;
             tc::st32(lane_addr + col, o);
           }
         }
-        if (j == x.n_kv - 1 && j * kKeys + r >= x.ctx && kh < L::kHalves) {
+        // keys 0-63 again (unconditionally: a skipped load would keep keys
+        // 64-127 live through the pass above; after a failed wait the
+        // values are unused garbage in allocated tensor memory)
+        tc::ld64(lane_addr + sb * kKeys, v);
+        mask(v, k0, lim);
+        exp_store(v, b, 0, nm2, s2);
+        tc::fence_before_sync();
+        mbar_arrive(&s_free[sb]);
+        if (j == x.n_kv - 1 && k0 + r >= x.ctx) {
           // key row r of the last tile lies past the context: zero its V row
-          // (this thread: 64-column half kh) so that 0 * (stale pool bits)
-          // cannot reach the output
-          if (mbar_wait_bounded(&v_full[gg % NS], (gg / NS) & 1)) {
-            uint8_t* vrow = smem + L::off_v + (gg % NS) * L::kSide + kh * (kKeys * 128) +
-                            (r >> 3) * 1024 + (r & 7) * 128;
+          // so that 0 * (stale pool bits) cannot reach the output
+          if (ok && mbar_wait_bounded(&v_full[gg % NS], (gg / NS) & 1)) {
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              *reinterpret_cast<uint4*>(vrow + k * 16) = make_uint4(0, 0, 0, 0);
+            for (int h = 0; h < L::kHalves; ++h) {
+              uint8_t* vrow = smem + L::off_v + (gg % NS) * L::kSide + h * (kKeys * 128) +
+                              (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                *reinterpret_cast<uint4*>(vrow + k * 16) = make_uint4(0, 0, 0, 0);
+            }
           } else {
             ok = false;
           }
@@ -498,48 +525,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&p_full[b]);
         const float2 u0 = f2unpack(add2(s2[0], s2[1]));
         const float2 u1 = f2unpack(add2(s2[2], s2[3]));
-        l = fmaf(l, factor, (u0.x + u0.y) + (u1.x + u1.y));
-        m_ref = m_new;
-        // a failed wait in this tile is acted on at the next meeting
+        const float fl = m_l == m_use ? 1.f : ex2(m_l - m_use);  // 0 before the first tile
+        l = fmaf(l, fl, (u0.x + u0.y) + (u1.x + u1.y));
+        m_l = m_use;
       }
-      // the row sum over both halves; the pair agrees whether to go on
-      red[kh * kRows + r] = l;
-      const bool pok = pair_and(ok);
-      const float l_row = l + red[(kh ^ 1) * kRows + r];
-      pair_sync();  // both read before the next item's first write
-      if (!pok) {
-        ok = false;
-        break;
-      }
-      const int gl = g + x.n_kv - 1;
-      if (wait_all(&p_done[gl & 1], (gl >> 1) & 1)) {
-        tc::fence_after_sync();
-        const float inv = 1.f / l_row;
-        T* dst = reinterpret_cast<T*>(a.out) +
-                 static_cast<int64_t>(x.r0 + r) * a.out_stride +
-                 static_cast<int64_t>(x.h) * D + kh * kDh;
-#pragma unroll
-        for (int c = 0; c < kDh / 32; ++c) {
-          float o[32];
-          tc::ld32(lane_addr + kColO + kh * kDh + c * 32, o);  // whole warp (collective)
-          if (r < x.nrows) {
-#pragma unroll
-            for (int d = 0; d < 32; d += 8) {
-              uint4 w;
-              w.x = pack2<T>(o[d] * inv, o[d + 1] * inv);
-              w.y = pack2<T>(o[d + 2] * inv, o[d + 3] * inv);
-              w.z = pack2<T>(o[d + 4] * inv, o[d + 5] * inv);
-              w.w = pack2<T>(o[d + 6] * inv, o[d + 7] * inv);
-              *reinterpret_cast<uint4*>(dst + c * 32 + d) = w;
-            }
-          }
-        }
-        tc::fence_before_sync();
+      if ((gl & 1) != wg) {
+        // hand this warpgroup's sums, relative to the item's last reference,
+        // to the warpgroup of the last tile
+        float m_fin = m_l;
+        if (wait_all(&ref_full[gl & 1], (gl >> 1) & 1)) m_fin = sref[(gl & 1) * kRows + r];
+        lsum[r] = m_l == m_fin ? l : l * ex2(m_l - m_fin);
+        mbar_arrive(l_ready);
       } else {
-        ok = false;
+        float lo = 0.f;
+        if (wait_all(l_ready, ii & 1)) lo = lsum[r];
+        const float l_row = l + lo;
+        if (wait_all(&p_done[gl & 1], (gl >> 1) & 1)) {
+          tc::fence_after_sync();
+          const float inv = 1.f / l_row;
+          T* dst = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(x.r0 + r) * a.out_stride +
+                   static_cast<int64_t>(x.h) * D;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tc::ld32(lane_addr + kColO + c * 32, o);  // whole warp (collective)
+            if (r < x.nrows) {
+#pragma unroll
+              for (int d = 0; d < 32; d += 8) {
+                uint4 w;
+                w.x = pack2<T>(o[d] * inv, o[d + 1] * inv);
+                w.y = pack2<T>(o[d + 2] * inv, o[d + 3] * inv);
+                w.z = pack2<T>(o[d + 4] * inv, o[d + 5] * inv);
+                w.w = pack2<T>(o[d + 6] * inv, o[d + 7] * inv);
+                *reinterpret_cast<uint4*>(dst + c * 32 + d) = w;
+              }
+            }
+            asm volatile("" ::: "memory");  // one 32-column chunk live at a time
+          }
+          tc::fence_before_sync();
+        }
+        mbar_arrive(o_free);  // the next item's first P.V may overwrite O
       }
-      mbar_arrive(o_free);  // the next item's first P.V may overwrite O
       g += x.n_kv;
+      ++ii;
     }
     if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
     tc::fence_before_sync();
