@@ -14,21 +14,23 @@
 //               block-table lookups are spread over the lanes and done one
 //               tile ahead;
 //   warp 10     MMA issuer (one thread): S = Q.K^T (M=128, N=128 keys,
-//               K=D) into one of three TMEM buffers, two tiles ahead, and
-//               O += P.V (M=128, N=D, K=128 keys) into the TMEM accumulator,
-//               tcgen05.mma kind::f16 with operands in 128-byte-swizzled
-//               shared memory; tcgen05.commit releases stages and signals
-//               the softmax;
+//               K=D) into one of three TMEM buffers, two tiles ahead, with
+//               Q and K from 128-byte-swizzled shared memory; and
+//               O += P.V (M=128, N=D, K=128 keys) into the TMEM accumulator
+//               with P read from tensor memory (the A operand) and V from
+//               shared memory, tcgen05.mma kind::f16; tcgen05.commit
+//               releases stages and buffers and signals the softmax;
 //   warps 0-7   softmax, two warpgroups taking alternate K/V tiles: thread r
 //               of a warpgroup owns query row r (= TMEM lane r) and all 128
 //               keys of its tiles: TMEM loads of its scores, masked max,
-//               exp2 probabilities written as 16-bit P into the warpgroup's
-//               shared-memory P buffer (the A operand of the P.V MMA) and
-//               their running sum. P is taken relative to a reference max
-//               that moves only when the row max grows by more than 2^8
-//               (then the row of O in TMEM is rescaled); the reference is
-//               handed from tile to tile through shared memory, so the two
-//               warps sharing a scheduler work on different tiles at once.
+//               exp2 probabilities and their running sum; P goes back into
+//               the same S buffer as 16-bit pairs (columns 64..127), so no
+//               P passes through shared memory, whose bandwidth the MMAs
+//               need. P is taken relative to a reference max that moves only
+//               when the row max grows by more than 2^8 (then the row of O
+//               in TMEM is rescaled); the reference is handed from tile to
+//               tile through shared memory, so the two warps sharing a
+//               scheduler work on different tiles at once.
 // Every wait is bounded (2 s); on a timeout the CTA flags IR_DEVERR_TIMEOUT,
 // lets its copies and MMAs drain (bounded), frees its tensor memory and ends.
 #include "tcgen05.cuh"
@@ -55,12 +57,10 @@ struct PLayout {
   static constexpr int kQ = kHalves * kHalf;             // Q tile
   static constexpr int kSide = kHalves * kKeys * 128;    // one K or V tile
   static constexpr int NS = D == 128 ? 2 : 4;            // stages per ring
-  static constexpr int kP = 2 * kHalf;                   // P: 2 halves x 128 rows x 128 B
   static constexpr int off_q = 0;
   static constexpr int off_k = kQ;
   static constexpr int off_v = off_k + NS * kSide;
-  static constexpr int off_p = off_v + NS * kSide;       // two P buffers
-  static constexpr int off_bar = off_p + 2 * kP;
+  static constexpr int off_bar = off_v + NS * kSide;
   // q_full, q_empty, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[kSBuf],
   // s_free[kSBuf], p_full[2], p_done[2], o_free, drain, ref_full[2], l_ready
   static constexpr int kBars = 2 + 4 * NS + 2 * kSBuf + 9;
@@ -159,9 +159,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* v_full = k_empty + NS;
   uint64_t* v_empty = v_full + NS;
   uint64_t* s_full = v_empty + NS;    // [kSBuf] S buffer b holds tile g (g % kSBuf == b)
-  uint64_t* s_free = s_full + kSBuf;  // [kSBuf] the softmax has read S buffer b
-  uint64_t* p_full = s_free + kSBuf;  // [2] P buffer b written (and O rescaled)
-  uint64_t* p_done = p_full + 2;      // [2] the P.V MMA reading P buffer b completed
+  uint64_t* s_free = s_full + kSBuf;  // [kSBuf] the P.V reading P from S buffer b completed
+  uint64_t* p_full = s_free + kSBuf;  // [2] P of tile g (g & 1 == b) written, O rescaled
+  uint64_t* p_done = p_full + 2;      // [2] the P.V MMA of tile g (g & 1 == b) completed
   uint64_t* o_free = p_done + 2;      // the softmax has read the item's O
   uint64_t* drain = o_free + 1;
   uint64_t* ref_full = drain + 1;     // [2] the reference max after tile g is in sref[g & 1]
@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < kSBuf; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], kWgThreads);
+      mbar_init(&s_free[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], kWgThreads);
@@ -288,7 +288,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 10) {
     // ---------------------------------------------------------- MMA issuer
     const uint32_t qb = smem_u32(smem + L::off_q);
-    const uint32_t pb = smem_u32(smem + L::off_p);
     constexpr uint32_t kIdS = tc::idesc_f16(kRows, kKeys, kBf16, false);
     constexpr uint32_t kIdO = tc::idesc_f16(kRows, D, kBf16, true);
     bool ok = true;
@@ -317,23 +316,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           return true;
         };
         auto issue_pv = [&](int gg, int j) -> bool {
-          const int st = gg % NS, b = gg & 1;
+          const int st = gg % NS, b = gg & 1, sb = gg % kSBuf;
           // the previous item's O has been read before this item's first P.V
           if (j == 0 && !mbar_wait_bounded(o_free, (ii & 1) ^ 1)) return false;
           if (!mbar_wait_bounded(&v_full[st], (gg / NS) & 1)) return false;
           if (!mbar_wait_bounded(&p_full[b], (gg >> 1) & 1)) return false;
           tc::fence_after_sync();
           const uint32_t vb = smem_u32(smem + L::off_v + st * L::kSide);
-          const uint32_t pbb = pb + b * L::kP;
+          // P (16-bit, two keys per column) sits in columns 64..127 of S buffer sb
+          const uint32_t pt = tmem + sb * kKeys + 64;
 #pragma unroll
-          for (int k = 0; k < kKeys / 16; ++k) {
-            const uint32_t po = (k >> 2) * L::kHalf + (k & 3) * 32;
-            tc::mma_f16_ss(tmem + kColO, tc::sw128_desc(pbb + po, 16, 1024),
+          for (int k = 0; k < kKeys / 16; ++k)
+            tc::mma_f16_ts(tmem + kColO, pt + k * 8,
                            tc::sw128_desc(vb + k * 2048, kKeys * 128, 1024), kIdO,
                            j > 0 || k > 0);
-          }
           tc::commit(&p_done[b]);
           tc::commit(&v_empty[st]);
+          tc::commit(&s_free[sb]);  // S buffer sb (holding P) may take Q.K^T again
           return true;
         };
         // Q.K^T of tile j + 2 is queued ahead of P.V of tile j: the next S
@@ -408,25 +407,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k) t4[k] = fmaxf(t4[k], v[60 + k]);
       return max3(fmaxf(t4[0], t4[1]), t4[2], t4[3]);
     };
-    // p = 2^(s * scale_log2 - m) for 64 keys, written as 16-bit P into the
-    // 64-column half h of P buffer b (128-byte swizzle), summed two at a time
-    auto exp_store = [&](const float (&v)[64], int b, int h, unsigned long long nm2,
+    // p = 2^(s * scale_log2 - m) for 64 keys, summed two at a time and
+    // written as 16-bit P, two keys per column, into this row's TMEM lane at
+    // column `col` (32 columns): the A operand of the P.V MMA
+    auto exp_store = [&](const float (&v)[64], uint32_t col, unsigned long long nm2,
                          unsigned long long (&s2)[4]) {
-      uint8_t* prow = smem + L::off_p + b * L::kP + h * L::kHalf + (r >> 3) * 1024 + (r & 7) * 128;
+      float pk[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16-byte chunks of 8 keys
-        uint32_t pk[4];
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          const float2 xx = f2unpack(fma2(f2pack(v[c * 8 + i], v[c * 8 + i + 1]), sc2, nm2));
-          const float p0 = ex2(xx.x);
-          const float p1 = ex2(xx.y);
-          s2[i >> 1] = add2(s2[i >> 1], f2pack(p0, p1));
-          pk[i >> 1] = pack2<T>(p0, p1);
-        }
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      for (int i = 0; i < 64; i += 2) {
+        const float2 xx = f2unpack(fma2(f2pack(v[i], v[i + 1]), sc2, nm2));
+        const float p0 = ex2(xx.x);
+        const float p1 = ex2(xx.y);
+        s2[(i >> 1) & 3] = add2(s2[(i >> 1) & 3], f2pack(p0, p1));
+        pk[i >> 1] = __uint_as_float(pack2<T>(p0, p1));
       }
+      tc::st32(lane_addr + col, pk);  // waits for the store
     };
     int g = 0, ii = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
@@ -443,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_l = -INFINITY;   // the reference of this warpgroup's last tile
       for (int j = (wg - g) & 1; j < x.n_kv; j += 2) {
         const int gg = g + j;
-        const int b = gg & 1;         // P buffer and reference slot (== wg)
+        const int b = gg & 1;         // barrier parity slot and reference slot (== wg)
         const int sb = gg % kSBuf;    // S buffer
         const int k0 = j * kKeys;
         float v[64];
@@ -474,11 +469,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
         sref[b * kRows + r] = m_use;
         mbar_arrive(&ref_full[b]);
-        // P buffer b is free once the P.V MMA of tile gg - 2 has completed
-        if (gg >= 2) wait_all(&p_done[b], ((gg - 2) >> 1) & 1);
+        // P goes to columns 64..127 of S buffer sb: keys 64-127 (in registers)
+        // first, into columns 96..127, whose scores are no longer needed;
+        // then keys 0-63, read again from columns 0..63, into 64..95
+        const uint32_t pcol = sb * kKeys + 64;
         const unsigned long long nm2 = f2pack(-m_use, -m_use);
         unsigned long long s2[4] = {0ull, 0ull, 0ull, 0ull};
-        exp_store(v, b, 1, nm2, s2);
+        exp_store(v, pcol + 32, nm2, s2);
         asm volatile("" ::: "memory");  // keys 64-127 are stored before anything below
         // rows whose reference moved: O *= 2^(prev - m_use), after the P.V of
         // tile gg - 1 (this item's) and before this tile's
@@ -501,9 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // values are unused garbage in allocated tensor memory)
         tc::ld64(lane_addr + sb * kKeys, v);
         mask(v, k0, lim);
-        exp_store(v, b, 0, nm2, s2);
-        tc::fence_before_sync();
-        mbar_arrive(&s_free[sb]);
+        exp_store(v, pcol, nm2, s2);
         if (j == x.n_kv - 1 && k0 + r >= x.ctx) {
           // key row r of the last tile lies past the context: zero its V row
           // so that 0 * (stale pool bits) cannot reach the output
