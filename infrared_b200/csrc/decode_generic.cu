@@ -184,17 +184,17 @@ __global__ void __launch_bounds__(kGenThreads)
 }
 
 // Combine the pieces of the split sequences: CTA (kv head x query head in
-// group, sequence) of 4 warps; warp w folds pieces w, w+4, ... with an online
+// group, sequence) of W warps; warp w folds pieces w, w+W, ... with an online
 // log-sum-exp, each lane owning 4 consecutive head-dim columns (16-byte
-// loads), then the 4 warp states are combined through shared memory. The
+// loads), then the W warp states are combined through shared memory. The
 // pieces' loads are independent, so a merge costs a few L2 round trips even
-// when a sequence spans dozens of CTAs.
-template <typename T>
-__global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
+// when a sequence spans dozens of CTAs (W = 8 there, 4 otherwise).
+template <typename T, int W>
+__global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a) {
   launch_dependents();   // the next kernel may start its own prologue now
   wait_prerequisites();  // the decode grid's pieces and prefix are complete
-  __shared__ float4 s_acc[4][32];
-  __shared__ float s_m[4], s_s[4];
+  __shared__ float4 s_acc[W][32];
+  __shared__ float s_m[W], s_s[W];
   const int kvh = blockIdx.x / a.n_rep, n = blockIdx.x % a.n_rep, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t pb = a.ws_prefix[b];
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   float M = -INFINITY, S = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
-  for (int i = warp; i < parts; i += 4) {
+  for (int i = warp; i < parts; i += W) {
     const float li = lse[i * a.n_rep];
     const float4 oi = active ? *reinterpret_cast<const float4*>(o + i * ostride + lane * 4)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -234,11 +234,13 @@ __global__ void __launch_bounds__(128) split_merge_kernel(const DecodeArgs a) {
   }
   __syncthreads();
   if (warp != 0) return;
-  float Mt = fmaxf(fmaxf(s_m[0], s_m[1]), fmaxf(s_m[2], s_m[3]));
+  float Mt = s_m[0];
+#pragma unroll
+  for (int w = 1; w < W; ++w) Mt = fmaxf(Mt, s_m[w]);
   float St = 0.f;
   float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
+  for (int w = 0; w < W; ++w) {
     if (s_s[w] == 0.f) continue;
     const float c = ex2(s_m[w] - Mt);
     const float4 x = s_acc[w][lane];
@@ -321,23 +323,34 @@ int decode_generic_occupancy(int dtype, int D) {
   }
 }
 
-int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
+template <typename T, int W>
+int launch_merge_t(const DecodeArgs& a, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv * a.n_rep, a.B);
-  cfg.blockDim = dim3(128);  // 4 warps; split_merge_kernel assumes exactly 4
+  cfg.blockDim = dim3(32 * W);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, split_merge_kernel<T, W>, a));
+}
+
+template <typename T>
+int launch_merge_w(const DecodeArgs& a, cudaStream_t s) {
+  // a sequence of average length spans about G / B shares: with 8 or more
+  // pieces per row, 8 warps fold them in half the rounds
+  if (a.G >= 16 * a.B) return launch_merge_t<T, 16>(a, s);
+  return a.G >= 8 * a.B ? launch_merge_t<T, 8>(a, s) : launch_merge_t<T, 4>(a, s);
+}
+
+int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
   switch (dtype) {
-    case IR_DTYPE_F32: e = cudaLaunchKernelEx(&cfg, split_merge_kernel<float>, a); break;
-    case IR_DTYPE_BF16: e = cudaLaunchKernelEx(&cfg, split_merge_kernel<__nv_bfloat16>, a); break;
-    default: e = cudaLaunchKernelEx(&cfg, split_merge_kernel<__half>, a); break;
+    case IR_DTYPE_F32: return launch_merge_w<float>(a, s);
+    case IR_DTYPE_BF16: return launch_merge_w<__nv_bfloat16>(a, s);
+    default: return launch_merge_w<__half>(a, s);
   }
-  return static_cast<int>(e);
 }
 
 int launch_lse_merge(void* out, int64_t out_stride, const float* o_parts,

@@ -107,6 +107,8 @@ class PeerExchange:
         self.rank = dist.get_rank(group)
         self.batch, self.num_heads, self.head_dim = batch, num_heads, head_dim
         self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device(self.device.type, torch.cuda.current_device())
         rows = batch * num_heads
         nbytes = self._lib.ir_peer_exchange_bytes(self.world, rows, head_dim)
         if nbytes == 0:
@@ -135,6 +137,19 @@ class PeerExchange:
         write the combined result of all ranks into ``out [B, H, D]``."""
         from .ops import _dev_index, _stream, dtype_code, error_flag
 
+        b, h, d = self.batch, self.num_heads, self.head_dim
+        for name, t, shape in (("o", o, (b, h, d)), ("lse", lse, (b, h)), ("out", out, (b, h, d))):
+            if tuple(t.shape) != shape:
+                raise ValueError(f"{name} must have shape {shape}, got {tuple(t.shape)}")
+            if t.device != self.device:
+                raise ValueError(f"{name} is on {t.device}, the exchange on {self.device}")
+        if o.dtype != torch.float32 or lse.dtype != torch.float32:
+            raise TypeError("o and lse must be float32")
+        if not (o.is_contiguous() and lse.is_contiguous()) or out.stride(2) != 1 or \
+                out.stride(1) != d:
+            raise ValueError("o / lse must be contiguous and out's rows [H, D] dense")
+        if self._ptrs is None:
+            raise RuntimeError("the exchange has been closed")
         dev = _dev_index(o)
         err = error_flag(dev).data_ptr()
         stream = _stream(dev)

@@ -119,6 +119,20 @@ def test_sweep(cfg, dtype):
         assert_close_bf16(host_f32(out), want)
 
 
+@pytest.mark.parametrize("b", [3, 12, 40])
+def test_split_merge_warp_tiers(b):
+    """The split-sequence merge folds a row's pieces with 16, 8 or 4 warps
+    by the shares per sequence (148 shares at this geometry: B = 3, 12, 40
+    take 16, 8 and 4 warps); every tier matches the oracle."""
+    w = wl.custom(300 + b, b, 28, 4, 128, 16, 1000, 3000, "bfloat16")
+    vals = wl.numpy_values(w, 6)
+    q, kp, vp, _, _ = dev_values(vals, torch.bfloat16)
+    bt, ctx, _ = dev_meta(w)
+    want = oracle_decode(w, *[host_f32(t) for t in (q, kp, vp)])
+    out = irb.paged_decode(q, kp, vp, bt, ctx, w.scale, 16)
+    assert_close_bf16(host_f32(out), want)
+
+
 # ----------------------------------------------------------- full-size configs
 
 
