@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   // Every role walks the same items in the same order; g counts the CTA's
-  // K/V tiles over all its items (ring stages and S/P buffers follow g), ii
+  // K/V tiles over all its items (ring stages and S buffers follow g), ii
   // its items (Q buffer and O accumulator phases follow ii).
 
   if (warp == 8 || warp == 9) {
