@@ -113,20 +113,32 @@ class PeerExchange:
         nbytes = self._lib.ir_peer_exchange_bytes(self.world, rows, head_dim)
         if nbytes == 0:
             raise ValueError("unsupported world size or shape for the peer exchange")
+        self._ptrs = None
         own = ctypes.c_void_p()
-        check(self._lib.ir_peer_alloc(nbytes, ctypes.byref(own)))
-        handle = (ctypes.c_char * 64)()
-        check(self._lib.ir_peer_handle(own, handle))
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        ptrs = []
-        for r, hd in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(own.value)
-            else:
-                pp = ctypes.c_void_p()
-                check(self._lib.ir_peer_open(ctypes.c_char_p(hd), ctypes.byref(pp)))
-                ptrs.append(pp.value)
+        opened = []
+        with torch.cuda.device(self.device):  # the buffer lives on the exchange's GPU
+            check(self._lib.ir_peer_alloc(nbytes, ctypes.byref(own)))
+            try:
+                handle = (ctypes.c_char * 64)()
+                check(self._lib.ir_peer_handle(own, handle))
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+                ptrs = []
+                for r, hd in enumerate(handles):
+                    if r == self.rank:
+                        ptrs.append(own.value)
+                    else:
+                        pp = ctypes.c_void_p()
+                        check(self._lib.ir_peer_open(ctypes.c_char_p(hd), ctypes.byref(pp)))
+                        opened.append(pp.value)
+                        ptrs.append(pp.value)
+            except BaseException:
+                # give back what this rank holds; the peers' waits then fail
+                # at their barrier (process-group timeout) instead of hanging
+                for ptr in opened:
+                    self._lib.ir_peer_close(ptr)
+                self._lib.ir_peer_free(own)
+                raise
         self._own = own.value
         self._ptrs = ptrs
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
@@ -164,11 +176,12 @@ class PeerExchange:
             return
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
-        for r, ptr in enumerate(self._ptrs):
-            if r != self.rank:
-                self._check(self._lib.ir_peer_close(ptr))
-        dist.barrier(group=self.group)
-        self._check(self._lib.ir_peer_free(self._own))
+        with torch.cuda.device(self.device):
+            for r, ptr in enumerate(self._ptrs):
+                if r != self.rank:
+                    self._check(self._lib.ir_peer_close(ptr))
+            dist.barrier(group=self.group)
+            self._check(self._lib.ir_peer_free(self._own))
         self._ptrs = None
 
 
