@@ -674,8 +674,9 @@ def run_model(args):
     ctx_all = ms.random_context_lens(global_batch, 1024, 2048, seed=0)
     lo, hi = irdist.shard_sequences(ctx_all, world)[rank]
     warm = max(args.warmup, 3)
-    model = ms.Qwen2DecodeStep(ms.QWEN25_7B, ctx_all[lo:hi], max_new=2 * warm + args.steps + min(args.steps, 100) + 8,
-                               device=dev, seed=rank)
+    max_new = 2 * warm + args.steps + min(args.steps, 100) + 8
+    model = ms.Qwen2DecodeStep(ms.QWEN25_7B, ctx_all[lo:hi], max_new=max_new, device=dev,
+                               seed=rank)
     w_bytes = model.weight_bytes()
     for _ in range(warm):                      # eager steps (plans, workspaces, cuBLAS)
         model.step()

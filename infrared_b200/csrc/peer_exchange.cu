@@ -89,8 +89,8 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
       const int c = lane + 32 * k;
-      mine[k] = c < C ? *reinterpret_cast<const float2*>(o + static_cast<int64_t>(row) * p.D + 2 * c)
-                      : make_float2(0.f, 0.f);
+      const float* src = o + static_cast<int64_t>(row) * p.D + 2 * c;
+      mine[k] = c < C ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
     }
     const float my_lse = lse[row];
     for (int q = 0; q < p.world; ++q) {
