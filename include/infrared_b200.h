@@ -275,7 +275,9 @@ int ir_paged_decode_lse(float* o, float* lse, const void* q,
  *
  * - The first call on a device looks up the array's device address with
  *   that device current (this may load the library's GPU code), so make that
- *   first call before capturing a CUDA graph.
+ *   first call before capturing a CUDA graph. The address is looked up
+ *   again when the device's context has changed since (after a device
+ *   reset), so make the first call after a reset outside capture too.
  * - Shapes whose scratch (ir_paged_decode_workspace_size) exceeds
  *   IR_NOALLOC_WORKSPACE_BYTES are rejected with IR_ERR_WORKSPACE.
  * - All calls on a device share the one array and it keeps whatever the
@@ -385,10 +387,15 @@ int ir_derive_varlen_metadata(const int64_t* gather_slots, int64_t num_keys, con
  * counterpart: infrared is single-GPU. Buffers come from ir_peer_alloc
  * (zeroed) and are mapped into the other processes with ir_peer_handle /
  * ir_peer_open; bufs[] lists all world buffers as seen by the calling
- * process, bufs[rank] being its own. Every rank must make the same sequence
- * of calls with the same shapes on one stream; the calls may be captured in
- * a CUDA graph. A peer that stops calling makes the waits run out after 2 s
- * with IR_DEVERR_TIMEOUT, after which the buffers must be allocated anew.
+ * process, bufs[rank] being its own. Every rank allocates the same number of
+ * bytes (ir_peer_exchange_bytes for the largest batch * num_heads and the
+ * head_dim it will use) and passes that size as buffer_bytes: rows are laid
+ * out by that capacity, so later calls may use fewer rows (a smaller batch)
+ * and a call with more rows than the buffers hold is refused. Every rank must
+ * make the same sequence of calls with the same batch, heads and head_dim on
+ * one stream; the calls may be captured in a CUDA graph. A peer that stops
+ * calling makes the waits run out after 2 s with IR_DEVERR_TIMEOUT, after
+ * which the buffers must be allocated anew.
  */
 #define IR_PEER_HANDLE_BYTES 64
 int ir_peer_alloc(size_t bytes, void** ptr);
@@ -401,10 +408,12 @@ size_t ir_peer_exchange_bytes(int world, int rows, int head_dim);
 /* o [batch * num_heads, head_dim] fp32 (16-byte aligned) and lse
  * [batch * num_heads] fp32 of this rank in; out [batch, num_heads, head_dim]
  * (row stride out_stride, dtype) = all ranks' partials of this call merged.
- * head_dim a multiple of 4 up to 128, world 1..8. */
+ * head_dim a multiple of 4 up to 128, world 1..8; buffer_bytes = the size
+ * every rank's exchange buffer was allocated with. */
 int ir_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse,
-                     void* const* bufs, int world, int rank, int batch, int num_heads,
-                     int head_dim, int dtype, int32_t* err_flag, ir_stream_t stream);
+                     void* const* bufs, size_t buffer_bytes, int world, int rank, int batch,
+                     int num_heads, int head_dim, int dtype, int32_t* err_flag,
+                     ir_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -95,7 +95,8 @@ _SIGNATURES = {
     "ir_peer_close": (c_int, [c_void_p]),
     "ir_peer_exchange_bytes": (c_size_t, [c_int, c_int, c_int]),
     "ir_peer_exchange": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, POINTER(c_void_p),
-                                 c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
+                                 c_size_t, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                 c_void_p]),
     "ir_derive_varlen_metadata": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int, c_int,
                                           c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
                                           c_void_p, c_void_p, c_void_p]),

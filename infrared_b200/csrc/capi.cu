@@ -455,25 +455,58 @@ int prefill_rows_bytes(const ir_prefill_shape* s, size_t* tables, size_t* ctx, s
 static __device__ __align__(256) unsigned char g_noalloc_ws[IR_NOALLOC_WORKSPACE_BYTES];
 
 std::mutex g_noalloc_mu;
-std::map<int, void*> g_noalloc_ptr;  // device -> address of g_noalloc_ws
+// device -> (id of the context the address was found in, address of g_noalloc_ws)
+std::map<int, std::pair<unsigned long long, void*>> g_noalloc_ptr;
 
-// Device address of g_noalloc_ws on the current device (looked up once per
-// device, with that device current).
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
+
+// Unique id of the calling thread's current context (0 if none or unknown).
+// A device reset ends the context; the next one has a new id, and with it a
+// new copy of the library's device image at a possibly different address.
+unsigned long long current_context_id() {
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  if (!g_ctx_current || !g_ctx_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  if (g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_noalloc_ws on the current device, looked up with that
+// device current on its first use and again whenever the device's context
+// has changed since (after a device reset), so a stale address is never used.
 int noalloc_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(static_cast<int>(e), "cudaGetDevice");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  const unsigned long long ctx = current_context_id();
   auto it = g_noalloc_ptr.find(dev);
-  if (it == g_noalloc_ptr.end()) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_ws);
-    if (e != cudaSuccess || p == nullptr)
-      return cuda_status(e != cudaSuccess ? static_cast<int>(e) : 1,
-                         "cudaGetSymbolAddress(no-alloc scratch)");
-    it = g_noalloc_ptr.emplace(dev, p).first;
+  if (it != g_noalloc_ptr.end() && ctx != 0 && it->second.first == ctx) {
+    *out = it->second.second;
+    return IR_OK;
   }
-  *out = it->second;
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_ws);
+  if (e != cudaSuccess || p == nullptr)
+    return cuda_status(e != cudaSuccess ? static_cast<int>(e) : 1,
+                       "cudaGetSymbolAddress(no-alloc scratch)");
+  // the lookup makes the primary context current if no context was
+  g_noalloc_ptr[dev] = {ctx != 0 ? ctx : current_context_id(), p};
+  *out = p;
   return IR_OK;
 }
 
@@ -481,22 +514,37 @@ int noalloc_scratch(void** out) {
 
 namespace {
 
-// Kernel arguments of the peer exchange from the C ABI's arrays.
-int peer_args(void* const* bufs, int world, int rank, int rows, int head_dim, int32_t* err,
-              irb::PeerArgs* a) {
+// Kernel arguments of the peer exchange from the C ABI's arrays. rows is
+// batch * heads in 64 bits; it must fit the row capacity of the buffers
+// (their size, which every rank allocates alike).
+int peer_args(void* const* bufs, size_t buffer_bytes, int world, int rank, int64_t rows,
+              int head_dim, int32_t* err, irb::PeerArgs* a) {
   if (!bufs || world <= 0 || world > 8 || rank < 0 || rank >= world)
     return fail(IR_ERR_INVALID_ARG, "world must be 1..8 and rank < world");
   if (head_dim <= 0 || head_dim > 128 || head_dim % 4 != 0 || rows < 0)
     return fail(IR_ERR_INVALID_ARG, "head_dim must be a multiple of 4 up to 128");
+  const int64_t cap = irb::peer_exchange_capacity(buffer_bytes, world, head_dim);
+  if (cap > INT32_MAX)
+    return fail(IR_ERR_INVALID_ARG, "exchange buffer larger than 2^31 rows");
+  if (rows > cap)
+    return fail(IR_ERR_INVALID_ARG,
+                "batch * num_heads = " + std::to_string(rows) + " rows exceed the " +
+                    std::to_string(cap) + " rows an exchange buffer of " +
+                    std::to_string(buffer_bytes) + " bytes holds (ir_peer_exchange_bytes)");
   *a = irb::PeerArgs{};
   for (int i = 0; i < world; ++i) {
     if (!bufs[i] || !aligned(bufs[i], 256)) return fail(IR_ERR_INVALID_ARG, "bad peer buffer");
     a->bufs[i] = static_cast<uint8_t*>(bufs[i]);
   }
+  int sms = 1;
+  const int e = cached(-1, sm_count_now, 0, &sms);
+  if (e) return cuda_status(e, "SM count");
   a->world = world;
   a->rank = rank;
-  a->rows = rows;
+  a->rows = static_cast<int>(rows);
   a->D = head_dim;
+  a->cap = static_cast<int>(cap);
+  a->sms = sms;
   a->err = err;
   return IR_OK;
 }
@@ -893,11 +941,13 @@ size_t ir_peer_exchange_bytes(int world, int rows, int head_dim) {
 }
 
 int ir_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse,
-                     void* const* bufs, int world, int rank, int batch, int num_heads,
-                     int head_dim, int dtype, int32_t* err_flag, ir_stream_t stream) {
+                     void* const* bufs, size_t buffer_bytes, int world, int rank, int batch,
+                     int num_heads, int head_dim, int dtype, int32_t* err_flag,
+                     ir_stream_t stream) {
   irb::PeerArgs a;
   if (batch < 0 || num_heads <= 0) return fail(IR_ERR_INVALID_ARG, "bad batch / num_heads");
-  int rc = peer_args(bufs, world, rank, batch * num_heads, head_dim, err_flag, &a);
+  int rc = peer_args(bufs, buffer_bytes, world, rank,
+                     static_cast<int64_t>(batch) * num_heads, head_dim, err_flag, &a);
   if (rc) return rc;
   if (!o || !lse || !aligned(o, 16)) return fail(IR_ERR_INVALID_ARG, "o must be 16-byte aligned");
   if (!out || elem_bytes(dtype) == 0 || out_stride < static_cast<int64_t>(num_heads) * head_dim)

@@ -39,10 +39,14 @@ int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUte
 struct PeerArgs {
   uint8_t* bufs[8];  // every rank's exchange buffer as mapped in this process
   int world, rank;
-  int rows, D;       // rows = batch * heads
+  int rows, D;       // rows = batch * heads of this call
+  int cap;           // rows the buffers are laid out for (from their size)
+  int sms;           // SM count of this device (bounds the grid)
   int32_t* err;
 };
 size_t peer_exchange_bytes(int world, int rows, int D);
+int64_t peer_exchange_capacity(size_t bytes, int world, int D);
+int peer_exchange_grid(int64_t cap, int sms);
 int launch_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse, int H,
                          int dtype, const PeerArgs& p, cudaStream_t s);
 

@@ -14,25 +14,26 @@
 // counters, one NVLink trip from store to use (the "LL" idea of NCCL's
 // low-latency protocol, in a layout of this file's own).
 //
-// Call n on rank r (n = r's epoch; parity n & 1): each warp takes one row,
-// stores r's (o, lse) of that row into slot [n & 1][r] of every peer's buffer,
-// then polls the chunks of the same row from every peer in its own buffer
-// until their flags read n + 1, and combines the world's partials in rank
-// order (ir_lse_merge's arithmetic, so every rank writes identical rows).
-// The last CTA to finish advances the epoch.
+// Call n on rank r (n = r's epoch; parity n & 1): each warp takes rows
+// row = warp_id, warp_id + total_warps, ...; it first stores r's (o, lse) of
+// all its rows into slot [n & 1][r] of every peer's buffer, then polls the
+// chunks of the same rows from every peer in its own buffer until their flags
+// read n + 1, and combines the world's partials in rank order (ir_lse_merge's
+// arithmetic, so every rank writes identical rows). The last CTA to finish
+// advances the epoch.
 //
-// Slot reuse needs no acknowledgement: peer q's store of call n + 2 into a
-// slot of parity n & 1 happens after q's call n + 1 saw this rank's call n + 1
-// stores, which this rank issued only after its call n (the reads of that
-// slot) had ended. Consecutive calls on one stream never overlap in memory:
-// this kernel, and every kernel of this library launched with programmatic
-// dependent launch, touches no global memory before griddepcontrol.wait,
-// which returns only once the kernel before it has completed; a kernel the
-// next call depends on therefore completes after this call does.
+// Forward progress: a warp waits only for rows that the warp with the same
+// index on each peer stores before it waits for anything, and the grid is at
+// most one CTA per SM (a 128-thread CTA with no shared-memory demand), so
+// every CTA of every rank is resident at once and no wait depends on a CTA
+// that cannot be scheduled. The grid is a function of the buffer's row
+// capacity and the SM count only, so it is the same on every call on a
+// buffer, which the epoch counter relies on.
 //
-// No TMA, no multicast, no library kernel touches peer memory. Every wait is
-// bounded (2 s) and reports IR_DEVERR_TIMEOUT; the epochs of the ranks are
-// then out of step, and the buffers must be freed and allocated anew.
+// Slot layout: rows are placed by the buffer's row capacity (from its size),
+// not by the call's row count, so calls with fewer rows (a smaller batch)
+// use the same slots; every rank must allocate the same size.
+//
 #include "common.cuh"
 #include "decode_common.cuh"
 #include "kernels.h"
@@ -65,10 +66,22 @@ __device__ __forceinline__ uint8_t* row_slot(uint8_t* buf, const PeerArgs& p, in
                                              int row) {
   const int64_t chunks = p.D / 2 + 1;
   return buf + kHeader +
-         ((static_cast<int64_t>(par) * p.world + src) * p.rows + row) * chunks * 16;
+         ((static_cast<int64_t>(par) * p.world + src) * p.cap + row) * chunks * 16;
 }
 
 // CPL = chunks (value pairs) per lane: 1 for D <= 64, 2 for D <= 128.
+template <int CPL>
+__device__ __forceinline__ void load_row(const float* o, const PeerArgs& p, int row, int lane,
+                                         float2 (&v)[CPL]) {
+  const int C = p.D / 2;
+#pragma unroll
+  for (int k = 0; k < CPL; ++k) {
+    const int c = lane + 32 * k;
+    const float* src = o + static_cast<int64_t>(row) * p.D + 2 * c;
+    v[k] = c < C ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
+  }
+}
+
 template <typename T, int CPL>
 __global__ void __launch_bounds__(kThreads)
     exchange_kernel(T* __restrict__ out, int64_t out_stride, const float* __restrict__ o,
@@ -82,16 +95,13 @@ __global__ void __launch_bounds__(kThreads)
   const uint32_t n = s_n, flag = n + 1;
   const int par = n & 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kWarps + warp;
+  const int first = blockIdx.x * kWarps + warp;
+  const int step = gridDim.x * kWarps;
   const int C = p.D / 2;
-  if (row < p.rows) {
+  // 1. this rank's partial of every row of the warp, into every peer's buffer
+  for (int row = first; row < p.rows; row += step) {
     float2 mine[CPL];
-#pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      const int c = lane + 32 * k;
-      const float* src = o + static_cast<int64_t>(row) * p.D + 2 * c;
-      mine[k] = c < C ? *reinterpret_cast<const float2*>(src) : make_float2(0.f, 0.f);
-    }
+    load_row<CPL>(o, p, row, lane, mine);
     const float my_lse = lse[row];
     for (int q = 0; q < p.world; ++q) {
       if (q == p.rank) continue;
@@ -103,17 +113,21 @@ __global__ void __launch_bounds__(kThreads)
       }
       if (lane == 0) st_chunk(dst + C * 16, my_lse, 0.f, flag);
     }
-    // gather every source's row (this rank's from registers), in rank order
+  }
+  // 2. every source's rows (this rank's from its own o / lse), merged in rank
+  // order; a source whose wait ran out once is left out of the warp's later
+  // rows, so a silent peer costs one wait limit per warp, not one per row
+  unsigned missing = 0;
+  for (int row = first; row < p.rows; row += step) {
     float l_src[8];
     float2 v_src[8][CPL];
 #pragma unroll
     for (int s = 0; s < 8; ++s) {
       l_src[s] = -INFINITY;
-      if (s >= p.world) continue;
+      if (s >= p.world || ((missing >> s) & 1u)) continue;
       if (s == p.rank) {
-        l_src[s] = my_lse;
-#pragma unroll
-        for (int k = 0; k < CPL; ++k) v_src[s][k] = mine[k];
+        l_src[s] = lse[row];
+        load_row<CPL>(o, p, row, lane, v_src[s]);
         continue;
       }
       const uint8_t* src = row_slot(own, p, par, s, row);
@@ -143,8 +157,12 @@ __global__ void __launch_bounds__(kThreads)
         }
         if (++spins == 64) t0 = globaltimer_ns();
         if (spins > 64) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          // lane 0's clock decides for the whole warp
+          const bool out_of_time =
+              __shfl_sync(0xffffffffu, globaltimer_ns() - t0 > kWaitLimitNs, 0);
+          if (out_of_time) {
             if (lane == 0) set_err(p.err, IR_DEVERR_TIMEOUT);
+            missing |= 1u << s;
             l_src[s] = -INFINITY;  // leave the missing partial out
             break;
           }
@@ -192,8 +210,9 @@ template <typename T>
 int launch_t(void* out, int64_t out_stride, const float* o, const float* lse, int H,
              const PeerArgs& p, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
-  // a grid fixed by rows: the epoch protocol counts this kernel's CTAs per call
-  cfg.gridDim = dim3((p.rows + kWarps - 1) / kWarps);
+  // the same grid on every call on a buffer: the epoch protocol counts this
+  // kernel's CTAs per call
+  cfg.gridDim = dim3(peer_exchange_grid(p.cap, p.sms));
   cfg.blockDim = dim3(kThreads);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -214,6 +233,18 @@ int launch_t(void* out, int64_t out_stride, const float* o, const float* lse, in
 
 size_t peer_exchange_bytes(int world, int rows, int D) {
   return kHeader + static_cast<size_t>(2) * world * rows * (D / 2 + 1) * 16;
+}
+
+int64_t peer_exchange_capacity(size_t bytes, int world, int D) {
+  if (bytes <= static_cast<size_t>(kHeader)) return 0;
+  return static_cast<int64_t>((bytes - kHeader) /
+                              (static_cast<size_t>(2) * world * (D / 2 + 1) * 16));
+}
+
+int peer_exchange_grid(int64_t cap, int sms) {
+  const int64_t need = (cap + kWarps - 1) / kWarps;
+  const int64_t g = need < sms ? need : sms;
+  return static_cast<int>(g < 1 ? 1 : g);
 }
 
 int launch_peer_exchange(void* out, int64_t out_stride, const float* o, const float* lse, int H,

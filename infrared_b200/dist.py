@@ -91,9 +91,10 @@ class PeerExchange:
     buffer, the buffers are mapped into every process with CUDA IPC (handles
     traded once with ``all_gather_object``), and every call stores this
     rank's ``(o, lse)`` into all peers' buffers over NVLink and merges the
-    world's partials as their flags arrive, in one kernel. All ranks must call
-    :meth:`merge` the same number of times; :meth:`close` unmaps and frees
-    (collective)."""
+    world's partials as their flags arrive, in one kernel. The buffers hold
+    ``batch`` sequences; a call may pass fewer (the same number on every
+    rank). All ranks must call :meth:`merge` the same number of times with
+    the same shapes; :meth:`close` unmaps and frees (collective)."""
 
     def __init__(self, batch: int, num_heads: int, head_dim: int, device, group=None):
         import ctypes
@@ -140,16 +141,20 @@ class PeerExchange:
                 self._lib.ir_peer_free(own)
                 raise
         self._own = own.value
+        self._nbytes = nbytes
         self._ptrs = ptrs
         self._bufs = (ctypes.c_void_p * self.world)(*ptrs)
         dist.barrier(group=group)
 
     def merge(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """Push ``o [B, H, D]`` / ``lse [B, H]`` (fp32, contiguous) of this rank and
-        write the combined result of all ranks into ``out [B, H, D]``."""
+        """Push ``o [B, H, D]`` / ``lse [B, H]`` (fp32, contiguous; ``B`` at most
+        the exchange's batch) of this rank and write the combined result of
+        all ranks into ``out [B, H, D]``."""
         from .ops import _dev_index, _stream, dtype_code, error_flag
 
-        b, h, d = self.batch, self.num_heads, self.head_dim
+        b, h, d = o.shape[0] if o.dim() == 3 else -1, self.num_heads, self.head_dim
+        if not 0 <= b <= self.batch:
+            raise ValueError(f"o must be [B <= {self.batch}, {h}, {d}], got {tuple(o.shape)}")
         for name, t, shape in (("o", o, (b, h, d)), ("lse", lse, (b, h)), ("out", out, (b, h, d))):
             if tuple(t.shape) != shape:
                 raise ValueError(f"{name} must have shape {shape}, got {tuple(t.shape)}")
@@ -166,9 +171,10 @@ class PeerExchange:
         err = error_flag(dev).data_ptr()
         stream = _stream(dev)
         self._check(self._lib.ir_peer_exchange(out.data_ptr(), out.stride(0), o.data_ptr(),
-                                               lse.data_ptr(), self._bufs, self.world, self.rank,
-                                               self.batch, self.num_heads, self.head_dim,
-                                               dtype_code(out.dtype), err, stream))
+                                               lse.data_ptr(), self._bufs, self._nbytes,
+                                               self.world, self.rank, b, self.num_heads,
+                                               self.head_dim, dtype_code(out.dtype), err,
+                                               stream))
         return out
 
     def close(self) -> None:

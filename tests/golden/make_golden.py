@@ -1,7 +1,8 @@
 """Generate the golden fixtures by running the REFERENCE engine's own code.
 
-Run in a checkout where the infrared reference is importable (default
-location ``/root/reference``; override with ``INFRARED_REF``):
+Run where the infrared reference is importable (``tests/infrared_ref.py``:
+``INFRARED_REF`` names a checkout; by default the repository's own
+``baseline/_ref`` install from ``oracle/reference_install.py``):
 
     python tests/golden/make_golden.py
 
@@ -16,7 +17,6 @@ read that file; they never import the reference.
 
 from __future__ import annotations
 
-import os
 import sys
 from pathlib import Path
 
@@ -26,8 +26,12 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(HERE))
-REF = os.environ.get("INFRARED_REF", "/root/reference")
-sys.path.insert(0, REF)
+sys.path.insert(0, str(HERE.parent))
+import infrared_ref  # noqa: E402
+
+if not infrared_ref.importable():
+    sys.exit("infrared not found: set INFRARED_REF to a checkout or run "
+             "python -m oracle.reference_install")
 
 import torch  # noqa: E402
 

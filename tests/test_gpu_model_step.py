@@ -7,7 +7,8 @@ import torch
 from infrared_b200 import model_step as ms
 from infrared_b200 import ops
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")]
 
 
 class _Checked(ms.Qwen2DecodeStep):

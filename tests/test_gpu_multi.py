@@ -1,11 +1,14 @@
-"""KV-chunk decode over 2-4 GPUs (as many as the box has, at most 4): the
-peer-store exchange against the NCCL all-gather path and the single-GPU
-decode (needs 2 GPUs; skipped otherwise).
+"""KV-chunk decode over 2-8 GPUs (as many as the box has): the peer-store
+exchange against the NCCL all-gather path and the single-GPU decode (needs
+2 GPUs; skipped otherwise).
 
 Each rank is a spawned process on its own GPU. Bars: the peer exchange equals
 the NCCL path within fp32 merge rounding (1e-3) and the single-GPU decode
 within the bf16 bar (2e-2); repeated calls (the exchange's epoch counters
-advancing) and CUDA-graph replays give the same result every time.
+advancing) and CUDA-graph replays give the same result every time. A wide
+batch (256 sequences x 28 heads = 7168 rows, many rows per exchange warp)
+checks the exchange's bounded grid: no timeout, and the same bits as the
+NCCL path, whose merge kernel does the same arithmetic in the same order.
 """
 
 import datetime
@@ -72,8 +75,25 @@ def _worker(rank, world, port, results):
         res["graph_equal"] = eq
         del g
         ops.check_device_errors()
-        res["errors"] = 0
         ex.close()
+        # a wide batch: far more rows than one wave of exchange CTAs
+        w2 = wl.c4(seed=1, batch=256, ctx_len=1104)
+        q2, kp2, vp2, _, _ = wl.torch_values(w2, 9, dev)
+        t2_np, c2_np, _ = irdist.kv_chunk_tables(w2.block_tables, w2.context_lens,
+                                                 w2.block_size, world, rank)
+        t2 = torch.from_numpy(t2_np).to(dev)
+        c2 = torch.from_numpy(c2_np).to(dev)
+        ref2 = irdist.chunked_decode(q2, kp2, vp2, t2, c2, w2.scale, w2.block_size)
+        ex2 = irdist.PeerExchange(w2.batch, w2.num_heads, w2.head_dim, dev)
+        got2 = [irdist.chunked_decode(q2, kp2, vp2, t2, c2, w2.scale, w2.block_size,
+                                      exchange=ex2) for _ in range(3)]
+        torch.cuda.synchronize()
+        res["wide_max_diff"] = max((g2.float() - ref2.float()).abs().max().item()
+                                   for g2 in got2)
+        res["wide_equal"] = all(torch.equal(g2, ref2) for g2 in got2)
+        ops.check_device_errors()
+        ex2.close()
+        res["errors"] = 0
     except Exception as e:  # noqa: BLE001 - reported to the parent test
         res["exception"] = repr(e)
     finally:
@@ -82,7 +102,7 @@ def _worker(rank, world, port, results):
 
 
 def test_peer_exchange_gpus():
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     ctx = torch.multiprocessing.get_context("spawn")
     results = ctx.Queue()
     port = _free_port()
@@ -100,3 +120,4 @@ def test_peer_exchange_gpus():
         assert res["p2p_vs_nccl"] < 1e-3, res
         assert res["p2p_vs_full"] < 2e-2, res
         assert res["repeat_equal"] and res["graph_equal"], res
+        assert res["wide_equal"], res

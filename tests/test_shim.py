@@ -1,7 +1,7 @@
 """The shim that installs the B200 kernels behind infrared's own seam.
 
-CPU part: with infrared importable (its checkout at INFRARED_REF, default
-/root/reference; skipped elsewhere), installing the shim leaves every CPU
+CPU part: with infrared importable (``tests/infrared_ref.py``: INFRARED_REF or
+the repository's ``baseline/_ref`` install; skipped elsewhere), installing the shim leaves every CPU
 call on infrared's naive path, bit for bit, and uninstalling restores the
 original functions. GPU part: the same shim installed into a stand-in seam
 with infrared's call contract (a dispatcher that writes through
@@ -9,27 +9,21 @@ with infrared's call contract (a dispatcher that writes through
 ``_paged_attention_triton``), checked against the oracle.
 """
 
-import os
-import sys
 import types
 
 import numpy as np
 import pytest
 import torch
 
+import infrared_ref
 from infrared_b200 import shim
 from infrared_b200 import workloads as wl
 from oracle import paged_attention_np as orc
 
-REF = os.environ.get("INFRARED_REF", "/root/reference")
-
-
 @pytest.fixture
 def infrared():
-    if not os.path.isdir(os.path.join(REF, "infrared")):
-        pytest.skip("infrared reference checkout not available")
-    if REF not in sys.path:
-        sys.path.insert(0, REF)
+    if not infrared_ref.importable():
+        pytest.skip("infrared (the reference) is not installed")
     import infrared.cache.paged_kv_cache as pk
     import infrared.engine.cuda_graph as cg
     import infrared.model.triton_attention as ta

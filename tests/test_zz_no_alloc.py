@@ -6,10 +6,13 @@ running inside another runtime's process, or a binding from a language with
 no device allocator of its own. They cannot provide the workspace that
 ``ir_paged_decode`` needs, so ``ir_paged_decode_noalloc`` keeps that scratch
 in an array built into the library. These tests call it through the C ABI
-(as such a caller would, with no workspace argument) and compare it with
-``ir_paged_decode`` on two calls in a row, at the bf16 bar of the other
-parity tests (atol = rtol = 2e-2); and they check that a shape whose scratch
-exceeds the built-in array is refused with a clear error.
+(as such a caller would, with no workspace argument) on two calls in a row
+with different queries, and check each result against the fp32 oracle at
+the bf16 bar of the other parity tests (atol = rtol = 2e-2) and against
+``ir_paged_decode``. The C2 shape splits sequences across CTAs, so the merge
+kernel reads the pieces the decode kernel left in the shared array, and the
+second call reads them over what the first call left there. A shape whose
+scratch exceeds the built-in array is refused with a clear error.
 
 This file sorts last so that a run stopping at the first failure has run
 every other test before it; it also passes on its own in a fresh process.
@@ -21,6 +24,7 @@ import numpy as np
 import pytest
 import torch
 
+from gpu_helpers import assert_close_bf16, oracle_decode_device
 from infrared_b200 import _lib, ops
 from infrared_b200 import workloads as wl
 
@@ -56,8 +60,11 @@ def test_noalloc_matches_regular_decode_on_two_calls_in_a_row():
     ctx = torch.from_numpy(w.context_lens).cuda()
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    _, _, need = ops.decode_plan(q1, kp, bt, w.block_size, w.scale)
+    _, ctas, need = ops.decode_plan(q1, kp, bt, w.block_size, w.scale)
     assert 0 < need <= _lib.IR_NOALLOC_WORKSPACE_BYTES
+    # more CTAs per kv-head group than sequences: sequences are cut into
+    # pieces whose partials go through the scratch array to the merge kernel
+    assert ctas > w.batch
     for q in (q1, q2):
         out = torch.empty_like(q)
         rc = lib.ir_paged_decode_noalloc(out.data_ptr(), q.data_ptr(), kp.data_ptr(),
@@ -65,10 +72,12 @@ def test_noalloc_matches_regular_decode_on_two_calls_in_a_row():
                                          ctypes.byref(_shape(w, q, out)), err.data_ptr(),
                                          stream)
         assert rc == _lib.IR_OK, lib.ir_last_error()
+        torch.cuda.synchronize()
+        got = out.float().cpu().numpy()
+        assert_close_bf16(got, oracle_decode_device(w, q, kp, vp), TOL)
         ref = ops.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size)
         torch.cuda.synchronize()
-        np.testing.assert_allclose(out.float().cpu().numpy(), ref.float().cpu().numpy(),
-                                   atol=TOL, rtol=TOL)
+        np.testing.assert_allclose(got, ref.float().cpu().numpy(), atol=TOL, rtol=TOL)
     assert int(err.item()) == 0
 
 
