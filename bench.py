@@ -27,8 +27,16 @@ divided by the slowest rank's time.
   on two copy streams; kernels run in order).
 * ``roofline``: the decode call's bytes / its measured duration against the
   measured HBM copy bandwidth in MEASURED_PEAKS.json.
-* ``cpu_baseline`` / ``--impl reference``: the reference's naive CPU path
-  (restated in oracle/, numpy) on a bounded sample of the same workload.
+* ``kv_chunk`` (default config, every N): config C4 (4 x 32k contexts)
+  with each sequence's KV split across the same N GPUs, partials exchanged
+  by peer stores over NVLink in one kernel (``p2p``) and by an NCCL
+  all-gather + merge (``nccl``); strong scaling of one fixed batch.
+* ``cpu_baseline`` / ``--impl reference``: infrared's own naive CPU path,
+  ``paged_attention(..., PagedContext(use_triton=False))``
+  (infrared/model/triton_attention.py:81-129), over the whole batch of the
+  workload per call, on all host cores (infrared from the git-ignored
+  ``baseline/_ref`` install); where that install is absent, the numpy
+  restatement in oracle/ on one sequence per call (``kind: "port"``).
 """
 
 from __future__ import annotations
@@ -62,6 +70,10 @@ def parse_args():
     p.add_argument("--sets", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--engine", action="store_true",
+                   help="c5 through infrared's own PagedBatchEngine (CUDA graphs, shim)")
+    p.add_argument("--no-kv-chunk", action="store_true",
+                   help="leave out the C4 KV-chunk leg of the default config")
     p.add_argument("--soak", type=float, default=1.5,
                    help="seconds of untimed replays before timing (clock sampling)")
     p.add_argument("--no-e2e", action="store_true")
@@ -108,6 +120,95 @@ def cpu_sample_workload(w, seqs, seed=0):
                       wl.tail_slots(bt, ctx, bs))
     q, kp, vp, _, _ = wl.numpy_values(sub, seed)
     return sub, q, kp[None], vp[None]
+
+
+def infrared_importable() -> bool:
+    """infrared (the reference) from the repository's git-ignored install."""
+    path = ROOT / "baseline" / "_ref"
+    if not (path / "infrared" / "__init__.py").exists():
+        return False
+    if str(path) not in sys.path:
+        sys.path.insert(0, str(path))
+    try:
+        import infrared.model.triton_attention  # noqa: F401
+    except Exception:  # noqa: BLE001
+        return False
+    return True
+
+
+def time_infrared_decode(w, steps, warmup, budget_s, with_write=False):
+    """infrared's own naive paged decode (pool write, gather, repeat_kv, masked
+    attention; infrared/model/triton_attention.py:81-129) over the whole batch
+    of ``w`` per call, on every host core; stops after ``steps`` calls or
+    ``budget_s`` seconds of timed calls (at least one). Returns (GB/s of the
+    workload's useful bytes, seconds, calls, threads)."""
+    import torch
+    from infrared.cache.paged_kv_cache import PagedContext, PagedKVPool
+    from infrared.model.triton_attention import paged_attention
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    dt = getattr(torch, w.dtype)
+    g = torch.Generator().manual_seed(0)
+
+    def randn(*shape):
+        return (torch.randn(*shape, generator=g) * w.std).to(dt)
+
+    pool = PagedKVPool(num_layers=1, num_blocks=w.num_blocks, block_size=w.block_size,
+                       num_kv_heads=w.num_kv_heads, head_dim=w.head_dim, dtype=dt)
+    pool.k[0].copy_(randn(w.num_slots, w.num_kv_heads, w.head_dim))
+    pool.v[0].copy_(randn(w.num_slots, w.num_kv_heads, w.head_dim))
+    q = randn(w.batch, 1, w.num_heads, w.head_dim)
+    k_new = randn(w.batch, 1, w.num_kv_heads, w.head_dim)
+    v_new = randn(w.batch, 1, w.num_kv_heads, w.head_dim)
+    # the engine's decode inputs (infrared/engine/paged_engine.py:300-314, 630-638)
+    ctx = torch.from_numpy(w.context_lens.astype(np.int64))
+    t = int(ctx.max())
+    pos = torch.arange(t)
+    bt = torch.from_numpy(w.block_tables.astype(np.int64))
+    gather = bt[:, pos // w.block_size] * w.block_size + pos % w.block_size
+    valid = pos[None, :] < ctx[:, None]
+    gather = torch.where(valid, gather, torch.zeros_like(gather))
+    mask = torch.zeros(w.batch, 1, 1, t, dtype=dt)
+    mask = mask.masked_fill(~valid[:, None, None, :], torch.finfo(dt).min)
+    paged = PagedContext(pool, torch.from_numpy(w.slot_mapping.astype(np.int64)), gather,
+                         use_triton=False)
+
+    def call():
+        paged_attention(q, k_new, v_new, paged, mask, 0, w.scale, w.n_rep)
+
+    for _ in range(max(0, warmup)):
+        call()
+    n, t0 = 0, time.perf_counter()
+    while n < max(steps, 1):
+        call()
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    secs = time.perf_counter() - t0
+    nbytes = w.algorithmic_bytes(with_write=with_write)
+    return nbytes * n / secs / 1e9, secs, n, torch.get_num_threads()
+
+
+def cpu_baseline_leg(w, config, steps, warmup, budget_s):
+    """``cpu_baseline`` object: infrared's own path where it is installed,
+    else the numpy restatement on one sequence per call."""
+    if infrared_importable():
+        gbs, secs, n, threads = time_infrared_decode(w, steps, warmup, budget_s,
+                                                     with_write=config == "c3")
+        return {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
+                "kind": "reference",
+                "sample": f"infrared's paged_attention(use_triton=False) (pool write, gather, "
+                          f"repeat_kv, masked attention; torch CPU, {w.dtype}) over the full "
+                          f"{config} batch of {w.batch} sequences per call: {n} call(s), "
+                          f"{secs:.1f} s, torch threads {threads}",
+                "host_cpus": os.cpu_count(), "same_config": True}
+    gbs, secs, n = time_cpu_oracle(w, steps=10 ** 6, warmup=1, budget_s=budget_s)
+    return {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"oracle naive path (gather+repeat_kv+softmax, numpy fp32) on {n} "
+                      f"single-sequence samples of {config} ({secs:.1f} s), bytes counted at "
+                      f"the workload's bf16 size (infrared not installed)",
+            "host_cpus": os.cpu_count(), "same_config": False}
 
 
 def cpu_threads():
@@ -229,7 +330,9 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60),
                                 device_id=dev)
     ops.set_decode_path(args.decode_path)
-    w = make_workload(args.config, rank, args.batch)
+    # every rank decodes a batch of the same shape (workload seed 0: the same
+    # context lengths and bytes), its own values (seeded by rank)
+    w = make_workload(args.config, 0, args.batch)
     fused = args.config == "c3"
     bt = torch.from_numpy(w.block_tables).to(dev)
     ctx = torch.from_numpy(w.context_lens).to(dev)
@@ -358,7 +461,12 @@ def run_ours(args):
     path, ctas, _ = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale)
     peak, peak_kind = measured_peaks()
     per_step_ms = ms / args.steps
-    value = world * nbytes * args.steps / (ms / 1e3) / 1e9
+    job_bytes = nbytes
+    if world > 1:   # the bytes every rank moved, summed
+        t = torch.tensor([nbytes], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        job_bytes = int(t.item())
+    value = job_bytes * args.steps / (ms / 1e3) / 1e9
     per_gpu = nbytes / (per_step_ms / 1e3) / 1e9
     line = {
         "metric": METRIC,
@@ -384,6 +492,8 @@ def run_ours(args):
             "batch_per_gpu": w.batch,
             "tokens_per_gpu": int(w.context_lens.sum()),
             "bytes_per_step_per_gpu": nbytes,
+            "bytes_per_step_job": job_bytes,
+            "shards": "every rank: the same context lengths (equal bytes), its own values",
             "parallelism": f"sequence-sharded x{world}, no collective",
             "l2": "inputs larger than L2: >=200 MB of K/V per step, 3 rotating pool sets",
             "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
@@ -404,7 +514,7 @@ def run_ours(args):
             "scope": "one decode call (decode kernel + merge kernel), per GPU",
         },
         "e2e": None if e2e_ms is None else {
-            "value": round(world * nbytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
+            "value": round(job_bytes * args.steps / (e2e_ms / 1e3) / 1e9, 1),
             "unit": "GB/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
@@ -413,17 +523,12 @@ def run_ours(args):
         "clocks": clk,
         "gpu_launches": 2 * args.steps,
     }
+    del graph
+    if args.config == "c2" and not args.no_kv_chunk:
+        line["kv_chunk"] = kv_chunk_leg(args, dev, world, rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, secs, n = time_cpu_oracle(w, steps=10 ** 6, warmup=1, budget_s=args.cpu_seconds)
-        line["cpu_baseline"] = {
-            "value": round(gbs, 4), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
-            "sample": f"oracle naive path (gather+repeat_kv+softmax, numpy fp32) on {n} "
-                      f"single-sequence samples of {args.config} ({secs:.1f} s), bytes "
-                      f"counted at the workload's bf16 size",
-            "host_cpus": os.cpu_count(),
-        }
+        line["cpu_baseline"] = cpu_baseline_leg(w, args.config, 10 ** 6, 1, args.cpu_seconds)
     if world > 1:
-        del graph
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
@@ -453,8 +558,26 @@ def run_reference(args):
     if args.config == "p1":
         run_reference_prefill(args)
         return
-    w = make_workload(args.config, 0)
-    gbs, secs, n = time_cpu_oracle(w, steps=args.steps, warmup=args.warmup)
+    w = make_workload(args.config, 0, args.batch)
+    if infrared_importable():
+        # each step: one call of infrared's own naive path over the whole batch;
+        # warm-up capped at one call and the timed calls at about a minute so
+        # the run ends within minutes whatever --steps says
+        gbs, secs, n, threads = time_infrared_decode(w, args.steps, min(args.warmup, 1), 60.0,
+                                                     with_write=args.config == "c3")
+        kind = "reference"
+        sample = (f"infrared's paged_attention(use_triton=False) (pool write, gather, "
+                  f"repeat_kv, masked attention; torch CPU, {w.dtype}) over the full "
+                  f"{args.config} batch of {w.batch} sequences per step; {n} step(s) timed")
+        workload = f"{args.config} at full size (the GPU arm's config), infrared's own code"
+        dtype = {"bfloat16": "bf16", "float16": "f16"}.get(w.dtype, "f32")
+        same = True
+    else:
+        gbs, secs, n = time_cpu_oracle(w, steps=args.steps, warmup=args.warmup)
+        threads, kind, dtype, same = 1, "port", "f32", False
+        sample = ("reference naive CPU path restated in oracle/ (numpy): one sequence of "
+                  "the workload per step (infrared not installed)")
+        workload = f"{args.config} geometry, one sequence per step (bounded sample)"
     per_step = secs / max(n, 1)
     line = {
         "impl": "reference",
@@ -463,19 +586,16 @@ def run_reference(args):
         "unit": "GB/s",
         "n_gpus": world,
         "steps": n,
-        "warmup": args.warmup,
+        "warmup": min(args.warmup, 1) if kind == "reference" else args.warmup,
         "ms_per_step": round(per_step * 1e3, 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": dtype,
         "data": "synthetic (same generator and geometry as the GPU arm)",
-        "config": {"workload": f"{args.config} geometry, one sequence per step (bounded sample)",
-                   "global_batch": w.batch},
-        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": cpu_threads(),
-                         "kind": "port",
-                         "sample": "reference naive CPU path restated in oracle/ (numpy): "
-                                   "one sequence of the workload per step"},
+        "config": {"workload": workload, "global_batch": w.batch, "same_config": same},
+        "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads,
+                         "kind": kind, "sample": sample, "host_cpus": os.cpu_count()},
         "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -526,6 +646,114 @@ def run_reference_prefill(args):
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def _graph_ms(step, steps, dev, world, soak_s=0.3):
+    """Per-replay time (ms) of ``steps`` calls of ``step`` captured in one CUDA
+    graph, max over ranks; every rank replays the same number of times."""
+    import torch
+    import torch.distributed as dist
+
+    from infrared_b200 import dist as irdist
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with torch.cuda.stream(stream):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(steps):
+                step(i)
+        ev[0].record(stream)
+        graph.replay()
+        ev[1].record(stream)
+        ev[1].synchronize()
+        est = ev[0].elapsed_time(ev[1])
+        if world > 1:
+            est = irdist.max_over_ranks(est, device=dev)
+        for _ in range(int(min(500, soak_s * 1e3 / max(est, 1e-3)))):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        ev[0].record(stream)
+        graph.replay()
+        ev[1].record(stream)
+        ev[1].synchronize()
+    ms = ev[0].elapsed_time(ev[1])
+    if world > 1:
+        ms = irdist.max_over_ranks(ms, device=dev)
+    del graph
+    return ms
+
+
+def kv_chunk_leg(args, dev, world, rank, steps=100):
+    """C4 (4 sequences x 32768 tokens) with every sequence's KV split across
+    the job's N GPUs: per step each rank decodes its chunk (partial out +
+    log-sum-exp), the partials cross NVLink and every rank merges them; at
+    N = 1 the plain decode of the whole KV. Strong scaling of one fixed batch;
+    GB/s = the batch's useful bytes / step time (max over ranks)."""
+    import torch
+
+    import infrared_b200 as irb
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import workloads as wl
+
+    w = wl.c4(seed=0)
+    total = w.algorithmic_bytes()
+    res = {"workload": "C4: B=4 x ctx 32768 (Qwen2.5-7B attention), each sequence's KV "
+                       "split over the N GPUs", "n_gpus": world, "scaling": "strong",
+           "bytes_per_step_total": total, "steps": steps,
+           "timing": "K steps in one CUDA graph, CUDA events, max over ranks"}
+    if world == 1:
+        bt = torch.from_numpy(w.block_tables).to(dev)
+        ctx = torch.from_numpy(w.context_lens).to(dev)
+        sets = [wl.torch_values(w, 7 + s, dev) for s in range(3)]
+        out = torch.empty_like(sets[0][0])
+
+        def one(i):
+            q, kp, vp, _, _ = sets[i % 3]
+            irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size, out=out)
+
+        ms = _graph_ms(one, steps, dev, world) / steps
+        res["single_gpu"] = {"ms_per_step": round(ms, 5),
+                             "value": round(total / (ms / 1e3) / 1e9, 1), "unit": "GB/s"}
+        del sets
+        return res
+    tables_np, ctx_np, _ = irdist.kv_chunk_tables(w.block_tables, w.context_lens,
+                                                  w.block_size, world, rank)
+    tables = torch.from_numpy(tables_np).to(dev)
+    ctx = torch.from_numpy(ctx_np).to(dev)
+    local_bytes = int(ctx_np.astype(np.int64).sum()) * 2 * w.num_kv_heads * w.head_dim * 2
+    nsets = max(3, -(-3 * 126 * 2 ** 20 // max(local_bytes, 1)))
+    sets = [wl.torch_values(w, 7 + s, dev) for s in range(nsets)]   # same q on every rank
+    res["bytes_per_step_per_gpu"] = local_bytes
+    for kind in ("p2p", "nccl"):
+        ex = None
+        if kind == "p2p":
+            try:
+                ex = irdist.PeerExchange(w.batch, w.num_heads, w.head_dim, dev)
+            except RuntimeError as exc:   # every rank raises together
+                res[kind] = {"error": str(exc)[:200]}
+                continue
+
+        def one(i, ex=ex):
+            q, kp, vp, _, _ = sets[i % nsets]
+            irdist.chunked_decode(q, kp, vp, tables, ctx, w.scale, w.block_size, exchange=ex)
+
+        ms = _graph_ms(one, steps, dev, world) / steps
+        res[kind] = {"ms_per_step": round(ms, 5),
+                     "value": round(total / (ms / 1e3) / 1e9, 1), "unit": "GB/s",
+                     "exchange": "peer stores over NVLink + merge, one kernel" if ex else
+                                 "NCCL all-gather + ir_lse_merge"}
+        if ex is not None:
+            ex.close()
+    del sets
+    return res
 
 
 def run_chunked(args):
@@ -767,6 +995,194 @@ def run_model(args):
         print(json.dumps(line), flush=True)
 
 
+def build_infrared_qwen7b(dev, dtype, seed=0, std=0.02):
+    """infrared's own ``Qwen2ForCausalLM`` (infrared/model/qwen2.py:71-118) at
+    the Qwen2.5-7B geometry with random weights N(0, std) (norm weights 1),
+    built on the meta device and materialised on ``dev`` in ``dtype`` (no
+    host copy of 15 GB). The RoPE frequencies are recomputed after
+    materialising and cast to the model dtype, as ``from_pretrained``'s
+    ``.to(dtype)`` leaves them."""
+    import torch
+    from infrared.model.config import Qwen2Config
+    from infrared.model.qwen2 import Qwen2ForCausalLM
+
+    cfg = Qwen2Config(vocab_size=152064, hidden_size=3584, intermediate_size=18944,
+                      num_hidden_layers=28, num_attention_heads=28, num_key_value_heads=4,
+                      head_dim=128, rms_norm_eps=1e-6, rope_theta=1_000_000.0,
+                      max_position_embeddings=32768, tie_word_embeddings=False,
+                      bos_token_id=151643, eos_token_ids=())
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        with torch.device("meta"):
+            model = Qwen2ForCausalLM(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    model = model.to_empty(device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    with torch.no_grad():
+        for name, prm in model.named_parameters():
+            if name.endswith("norm.weight"):
+                prm.fill_(1.0)
+            else:
+                prm.normal_(0.0, std, generator=g)
+        d = cfg.head_dim
+        inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, device=dev,
+                                                     dtype=torch.float32) / d))
+        model.rotary.inv_freq = inv.to(dtype)
+    return model.eval(), cfg
+
+
+def run_model_engine(args):
+    """C5 through infrared's own engine: a random-init Qwen2.5-7B in infrared's
+    ``Qwen2ForCausalLM``, served by infrared's ``PagedBatchEngine`` with
+    CUDA-graph decode (infrared/engine/paged_engine.py:248-288,
+    infrared/engine/cuda_graph.py:202-287), the B200 kernels installed behind
+    its seam (``shim.install``: RoPE + cache write + decode in one kernel,
+    prefill on the tensor-core kernel, graph inputs built on the device).
+    128 requests (prompts of U[1024, 2048] random tokens) are submitted; the
+    engine prefills each, then decodes them as one batch. tok/s = decoded
+    tokens / wall time of the engine's decode steps (its own loop: graph
+    replay, per-sequence greedy sampling on the host, scheduling), after
+    warm-up steps that include the graph capture. At N GPUs every rank runs
+    its own engine over its share of the 128 requests (no collective)."""
+    import torch
+    import torch.distributed as dist
+
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import model_step as ms
+    from infrared_b200 import shim
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=dev)
+    if not infrared_importable():
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "unavailable": "infrared is not installed in "
+                              "baseline/_ref (python -m oracle.reference_install)"}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    from infrared.engine.paged_engine import PagedBatchEngine
+    from infrared.engine.static_batch import BatchRequest
+
+    global_batch = args.batch or 128
+    ctx_all = ms.random_context_lens(global_batch, 1024, 2048, seed=0)
+    lo, hi = irdist.shard_sequences(ctx_all, world)[rank]
+    ctx = [int(c) for c in ctx_all[lo:hi]]
+    b = len(ctx)
+    warm = max(args.warmup, 3)
+    max_new = warm + args.steps + 1          # the first token comes from the prefill
+    model, cfg = build_infrared_qwen7b(dev, torch.bfloat16, seed=rank)
+    handle = shim.install(graph_inputs=True, fuse_rope=True, prefill=True)
+    t_max = -(-(max(ctx) + max_new + 1) // 16) * 16
+    engine = PagedBatchEngine(model, max_num_seqs=b, block_size=16,
+                              num_blocks=b * (t_max // 16) + 16, enable_prefix_caching=False,
+                              enable_cuda_graph=True, graph_max_seq_len=t_max)
+    steps_log = []
+    orig_step = engine._decode_step
+
+    def timed_decode_step():
+        n = len(engine.scheduler.running)
+        t0 = time.perf_counter()
+        orig_step()
+        steps_log.append((t0, time.perf_counter(), n))
+
+    engine._decode_step = timed_decode_step
+    orig_run = engine._run
+
+    def run_on_device():          # the engine's worker thread on this rank's GPU
+        torch.cuda.set_device(dev)
+        orig_run()
+
+    engine._run = run_on_device
+    rng = np.random.default_rng(100 + rank)
+    pends = [engine.submit(BatchRequest([int(x) for x in rng.integers(0, cfg.vocab_size, c)],
+                                        max_new_tokens=max_new, eos_token_ids=()))
+             for c in ctx]
+    clocks = ClockSampler(local)
+    t_start = time.perf_counter()
+    engine.start()
+    error = None
+    try:
+        for pd in pends:
+            pd.result(timeout=1800)
+    except Exception as exc:  # noqa: BLE001 - reported in the line
+        error = repr(exc)[:300]
+    finally:
+        engine.stop()
+        handle.uninstall()
+    t_total = time.perf_counter() - t_start
+    clk = clocks.stop()
+    timed = steps_log[warm:warm + args.steps]
+    ok = error is None and len(timed) == args.steps and all(n == b for _, _, n in timed)
+    secs = (timed[-1][1] - timed[0][0]) if ok else float("nan")
+    tokens = sum(n for _, _, n in timed)
+    prefill_s = (steps_log[0][0] - t_start) if steps_log else float("nan")
+    if world > 1:
+        t = torch.tensor([secs if ok else -1.0, float(tokens), float(ok)], dtype=torch.float64,
+                         device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        mn = t.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        sm = t.clone()
+        dist.all_reduce(sm)
+        ok = bool(mn[2].item())
+        secs, tokens = float(mx[0].item()), int(sm[1].item())
+    per_step_ms = secs / args.steps * 1e3 if ok else None
+    tok_s = tokens / secs if ok else None
+    kv_tokens = sum(ctx) + b * (warm + args.steps // 2)
+    w_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    kv_bytes = kv_tokens * 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
+    peak, peak_kind = measured_peaks()
+    step_gbs = (w_bytes + kv_bytes) / (per_step_ms / 1e3) / 1e9 if ok else None
+    line = {
+        "metric": METRIC, "value": round(tok_s, 1) if ok else None, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": warm,
+        "ms_per_step": round(per_step_ms, 4) if ok else None, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: random-init weights N(0,0.02), random prompt token ids (no "
+                "checkpoint or dataset)",
+        "config": {"workload": "C5 through infrared's PagedBatchEngine: Qwen2.5-7B (28 layers, "
+                               "hidden 3584, 28/4 heads, inter 18944, vocab 152064) in "
+                               "infrared's Qwen2ForCausalLM, prompts U[1024,2048], block 16, "
+                               "greedy, CUDA-graph decode",
+                   "global_batch": global_batch, "batch_per_gpu": b,
+                   "parallelism": f"sequence-sharded x{world}: one engine per GPU, weights "
+                                  "replicated",
+                   "shim": "install(graph_inputs=True, fuse_rope=True, prefill=True)",
+                   "l2": "inputs larger than L2: ~15 GB of weights + KV read per step",
+                   "timing": "wall time of the engine's decode steps (its own loop), max "
+                             "over ranks"},
+        "engine": {"prefill_s": round(prefill_s, 2), "total_s": round(t_total, 2),
+                   "decode_steps_logged": len(steps_log), "error": error},
+        "roofline": {"bound": "hbm", "achieved": round(step_gbs, 1) if ok else None,
+                     "peak": peak, "unit": "GB/s",
+                     "frac": round(step_gbs / peak, 4) if ok else None, "peak_kind": peak_kind,
+                     "traffic": None, "weight_bytes": w_bytes, "kv_bytes": kv_bytes,
+                     "scope": "whole engine decode step on one GPU (weights + KV history "
+                              "read per wall-clock step, host work included)"},
+        "e2e": {"value": round(tok_s, 1) if ok else None, "unit": "tok/s",
+                "h2d_bytes_per_step": b * (t_max // 16) * 4 + b * 12,
+                "d2h_bytes_per_step": b * 8,
+                "note": "the engine loop is end to end: host block tables in, sampled ids "
+                        "out, every step"},
+        "clocks": clk,
+        "gpu_launches": (2 * cfg.num_hidden_layers + 2) * args.steps,
+    }
+    del engine, model
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_prefill(args):
     """P1: causal prefill of 8 x 4096-token prompts at the Qwen2.5-7B attention
     geometry on the tcgen05 kernel (one launch per step); TFLOP/s of useful
@@ -882,6 +1298,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "c5" and args.engine:
+        run_model_engine(args)
     elif args.config == "c5":
         run_model(args)
     elif args.config == "p1":

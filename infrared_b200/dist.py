@@ -117,14 +117,15 @@ class PeerExchange:
         self._ptrs = None
         own = ctypes.c_void_p()
         opened = []
+        failure = None
         with torch.cuda.device(self.device):  # the buffer lives on the exchange's GPU
             check(self._lib.ir_peer_alloc(nbytes, ctypes.byref(own)))
+            ptrs = []
             try:
                 handle = (ctypes.c_char * 64)()
                 check(self._lib.ir_peer_handle(own, handle))
                 handles = [None] * self.world
                 dist.all_gather_object(handles, bytes(handle), group=group)
-                ptrs = []
                 for r, hd in enumerate(handles):
                     if r == self.rank:
                         ptrs.append(own.value)
@@ -133,13 +134,19 @@ class PeerExchange:
                         check(self._lib.ir_peer_open(ctypes.c_char_p(hd), ctypes.byref(pp)))
                         opened.append(pp.value)
                         ptrs.append(pp.value)
-            except BaseException:
-                # give back what this rank holds; the peers' waits then fail
-                # at their barrier (process-group timeout) instead of hanging
+            except Exception as exc:  # noqa: BLE001 - every rank learns of it below
+                failure = exc
+            # every rank takes part in this vote, so a rank that could not map a
+            # peer's buffer makes all ranks give up together instead of waiting
+            ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=self.device)
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+            if failure is not None or int(ok.item()) == 0:
                 for ptr in opened:
                     self._lib.ir_peer_close(ptr)
                 self._lib.ir_peer_free(own)
-                raise
+                raise RuntimeError("peer exchange setup failed on "
+                                   + ("this rank: " + repr(failure) if failure else
+                                      "another rank")) from failure
         self._own = own.value
         self._nbytes = nbytes
         self._ptrs = ptrs
@@ -170,11 +177,12 @@ class PeerExchange:
         dev = _dev_index(o)
         err = error_flag(dev).data_ptr()
         stream = _stream(dev)
-        self._check(self._lib.ir_peer_exchange(out.data_ptr(), out.stride(0), o.data_ptr(),
-                                               lse.data_ptr(), self._bufs, self._nbytes,
-                                               self.world, self.rank, b, self.num_heads,
-                                               self.head_dim, dtype_code(out.dtype), err,
-                                               stream))
+        with torch.cuda.device(dev):   # the launch goes to this device's stream
+            self._check(self._lib.ir_peer_exchange(out.data_ptr(), out.stride(0), o.data_ptr(),
+                                                   lse.data_ptr(), self._bufs, self._nbytes,
+                                                   self.world, self.rank, b, self.num_heads,
+                                                   self.head_dim, dtype_code(out.dtype), err,
+                                                   stream))
         return out
 
     def close(self) -> None:

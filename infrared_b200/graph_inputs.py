@@ -66,8 +66,9 @@ def build_decode_static_inputs(block_tables: list[list[int]], num_cached: list[i
     gather_slots = torch.empty((bucket_b, t_max), dtype=torch.long, device=device)
     mask = torch.empty((bucket_b, 1, 1, t_max), dtype=dtype, device=device)
     dev = _dev_index(ids)
-    check(_lib.load().ir_build_decode_inputs(
-        bt.data_ptr(), width, nc.data_ptr(), last.data_ptr(), b, bucket_b, t_max, block_size,
-        ids.data_ptr(), positions.data_ptr(), write_slots.data_ptr(), gather_slots.data_ptr(),
-        mask.data_ptr(), dtype_code(dtype), _stream(dev)))
+    with torch.cuda.device(dev):   # the launch goes to this device's stream
+        check(_lib.load().ir_build_decode_inputs(
+            bt.data_ptr(), width, nc.data_ptr(), last.data_ptr(), b, bucket_b, t_max,
+            block_size, ids.data_ptr(), positions.data_ptr(), write_slots.data_ptr(),
+            gather_slots.data_ptr(), mask.data_ptr(), dtype_code(dtype), _stream(dev)))
     return decode_inputs_cls(ids, positions, write_slots, gather_slots, mask)

@@ -12,6 +12,7 @@ There is no CPU path: CPU tensors raise ``ValueError``.
 
 from __future__ import annotations
 
+import functools
 import threading
 
 import torch
@@ -38,6 +39,25 @@ class DeviceError(RuntimeError):
 _state_lock = threading.Lock()
 _err_flags: dict[int, torch.Tensor] = {}
 _workspaces: dict[int, torch.Tensor] = {}
+
+
+def _on_tensor_device(fn):
+    """Run ``fn`` with its first tensor argument's device current.
+
+    A kernel launch into a stream of a device other than the calling thread's
+    current one fails, and callers such as infrared's engine run their loop
+    in a worker thread whose current device is the process default (0);
+    this switches to the tensors' device for the call when they differ."""
+
+    @functools.wraps(fn)
+    def wrapper(first, *args, **kwargs):
+        idx = first.device.index if isinstance(first, torch.Tensor) and first.is_cuda else None
+        if idx is not None and idx != torch.cuda.current_device():
+            with torch.cuda.device(idx):
+                return fn(first, *args, **kwargs)
+        return fn(first, *args, **kwargs)
+
+    return wrapper
 
 
 def dtype_code(dtype: torch.dtype) -> int:
@@ -123,6 +143,7 @@ def _check_pool(pool: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be a contiguous [num_slots, Hkv, D] tensor")
 
 
+@_on_tensor_device
 def cache_write(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
                 v_pool: torch.Tensor, slot_mapping: torch.Tensor) -> None:
     """``k_pool[slot_mapping] = k; v_pool[slot_mapping] = v`` (one layer's pools)."""
@@ -152,6 +173,7 @@ def cache_write(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
         dtype_code(k_pool.dtype), error_flag(dev).data_ptr(), _stream(dev)))
 
 
+@_on_tensor_device
 def cache_gather(pool: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
     """``pool[slots]`` for a 1-D or 2-D int64 slot tensor -> ``[*slots.shape, Hkv, D]``."""
     dev = _dev_index(pool)
@@ -170,6 +192,7 @@ def cache_gather(pool: torch.Tensor, slots: torch.Tensor) -> torch.Tensor:
     return out.reshape(*slots.shape, pool.shape[1], pool.shape[2])
 
 
+@_on_tensor_device
 def derive_block_metadata(gather_slots: torch.Tensor, mask: torch.Tensor, block_size: int,
                           block_tables: torch.Tensor | None = None,
                           context_lens: torch.Tensor | None = None):
@@ -289,6 +312,7 @@ def _decode_key(q, k_pool, v_pool, block_tables, context_lens, out, block_size, 
             block_size, float(scale))
 
 
+@_on_tensor_device
 def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                  block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                  block_size: int, out: torch.Tensor | None = None,
@@ -328,6 +352,7 @@ def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     return out
 
 
+@_on_tensor_device
 def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                        k_pool: torch.Tensor, v_pool: torch.Tensor,
                        slot_mapping: torch.Tensor, block_tables: torch.Tensor,
@@ -365,6 +390,7 @@ def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor
     return out
 
 
+@_on_tensor_device
 def paged_decode_rope_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                             k_pool: torch.Tensor, v_pool: torch.Tensor,
                             slot_mapping: torch.Tensor, block_tables: torch.Tensor,
@@ -414,6 +440,7 @@ def paged_decode_rope_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
     return out
 
 
+@_on_tensor_device
 def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                      block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,
                      block_size: int, o: torch.Tensor | None = None,
@@ -438,6 +465,7 @@ def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor
     return o, lse
 
 
+@_on_tensor_device
 def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor,
               dtype: torch.dtype = torch.float32,
               out: torch.Tensor | None = None) -> torch.Tensor:
@@ -501,6 +529,7 @@ def prefill_plan(q, k_pool, block_tables, q_start, block_size, scale=1.0):
     return path.value, lib.ir_paged_prefill_workspace_size(s)
 
 
+@_on_tensor_device
 def paged_prefill(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                   block_tables: torch.Tensor, context_lens: torch.Tensor,
                   q_start: torch.Tensor, scale: float, block_size: int,
@@ -550,6 +579,7 @@ def paged_prefill(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     return out
 
 
+@_on_tensor_device
 def derive_varlen_metadata(gather_slots: torch.Tensor, mask: torch.Tensor, block_size: int):
     """``(block_tables [S, max_blocks], context_lens [S], q_start [S + 1])`` of
     one packed frame in infrared's form (``gather_slots [1, K]`` int64 and

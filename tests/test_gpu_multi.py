@@ -121,3 +121,29 @@ def test_peer_exchange_gpus():
         assert res["p2p_vs_full"] < 2e-2, res
         assert res["repeat_equal"] and res["graph_equal"], res
         assert res["wide_equal"], res
+
+
+def test_kernels_follow_the_tensors_device():
+    """A call whose tensors live on another GPU than the calling thread's
+    current device (infrared's engine loop runs in a worker thread whose
+    current device is 0) runs on the tensors' GPU and gives the same result."""
+    import infrared_b200 as irb
+    from infrared_b200 import ops
+    from infrared_b200 import workloads as wl
+
+    dev = torch.device("cuda", 1)
+    w = wl.custom(3, 5, 28, 4, 128, 16, 100, 900, "bfloat16")
+    q, kp, vp, kn, vn = wl.torch_values(w, 3, dev)
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    ctx = torch.from_numpy(w.context_lens).to(dev)
+    sm = torch.from_numpy(w.slot_mapping).to(dev)
+    with torch.cuda.device(1):
+        want = irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size)
+        torch.cuda.synchronize()
+    with torch.cuda.device(0):
+        got = irb.paged_decode(q, kp, vp, bt, ctx, w.scale, w.block_size)
+        ops.cache_write(kn, vn, kp, vp, sm)
+        torch.cuda.synchronize(dev)
+    assert torch.equal(got, want)
+    assert torch.equal(kp[sm], kn) and torch.equal(vp[sm], vn)
+    ops.check_device_errors(1)
