@@ -66,10 +66,13 @@ def parse_args():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--config", choices=["c2", "c3", "c4", "c5", "p1"], default="c2")
+    p.add_argument("--config", choices=["c2", "c3", "c4", "c5", "p1", "kernels"],
+                   default="c2")
     p.add_argument("--sets", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--dynamic-tail", action="store_true",
+                   help="decode with static shares + dynamic tail units")
     p.add_argument("--engine", action="store_true",
                    help="c5 through infrared's own PagedBatchEngine (CUDA graphs, shim)")
     p.add_argument("--no-kv-chunk", action="store_true",
@@ -339,8 +342,11 @@ def run_ours(args):
     sm = torch.from_numpy(w.slot_mapping).to(dev)
     sets = [wl.torch_values(w, 1000 * rank + s, dev) for s in range(args.sets)]
     out = torch.empty_like(sets[0][0])
-    _, _, ws_bytes = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    dynamic = args.dynamic_tail
+    _, _, ws_bytes = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale,
+                                     dynamic=dynamic)
+    # a zeroed, marked workspace lets the decode hand out its tail dynamically
+    ws = ops.decode_workspace(ws_bytes, dev, dynamic=dynamic)
     nbytes = w.algorithmic_bytes(with_write=fused)
 
     def step(i):
@@ -499,6 +505,8 @@ def run_ours(args):
             "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
             "kernel_path": {1: "cuda-core", 2: "tma+mma.sync"}[path] +
                            (" (copy per head)" if args.decode_path == 3 else ""),
+            "schedule": "static shares + dynamic tail units" if dynamic and path == 2
+                        else "static shares",
             "ctas_per_kv_head": ctas,
         },
         "decode_tok_s_per_layer": round(world * w.batch / (per_step_ms / 1e3), 1),
@@ -557,6 +565,11 @@ def run_reference(args):
         return
     if args.config == "p1":
         run_reference_prefill(args)
+        return
+    if args.config == "kernels":
+        print(json.dumps({"impl": "reference", "unavailable": "the standalone-kernel leg has "
+                          "no reference counterpart (infrared has no kernels of its own)"}),
+              flush=True)
         return
     w = make_workload(args.config, 0, args.batch)
     if infrared_importable():
@@ -1100,6 +1113,29 @@ def run_model_engine(args):
         orig_run()
 
     engine._run = run_on_device
+    # device time of each graph decode (input build + replay), CUDA events
+    graph_events = []
+    orig_decoder = engine._cuda_graph_decoder
+
+    def timed_decoder():
+        dec = orig_decoder()
+        if not getattr(dec, "_irb_timed", False):
+            orig_decode = dec.decode
+
+            def decode(*a, **k):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                out = orig_decode(*a, **k)
+                e1.record()
+                graph_events.append((e0, e1))
+                return out
+
+            dec.decode = decode
+            dec._irb_timed = True
+        return dec
+
+    engine._cuda_graph_decoder = timed_decoder
     rng = np.random.default_rng(100 + rank)
     pends = [engine.submit(BatchRequest([int(x) for x in rng.integers(0, cfg.vocab_size, c)],
                                         max_new_tokens=max_new, eos_token_ids=()))
@@ -1118,6 +1154,8 @@ def run_model_engine(args):
         handle.uninstall()
     t_total = time.perf_counter() - t_start
     clk = clocks.stop()
+    torch.cuda.synchronize(dev)
+    graph_ms = [e0.elapsed_time(e1) for e0, e1 in graph_events[warm:warm + args.steps]]
     timed = steps_log[warm:warm + args.steps]
     ok = error is None and len(timed) == args.steps and all(n == b for _, _, n in timed)
     secs = (timed[-1][1] - timed[0][0]) if ok else float("nan")
@@ -1160,7 +1198,13 @@ def run_model_engine(args):
                    "timing": "wall time of the engine's decode steps (its own loop), max "
                              "over ranks"},
         "engine": {"prefill_s": round(prefill_s, 2), "total_s": round(t_total, 2),
-                   "decode_steps_logged": len(steps_log), "error": error},
+                   "decode_steps_logged": len(steps_log), "error": error,
+                   "graph_decode_device_ms_per_step": round(statistics.mean(graph_ms), 4)
+                   if graph_ms else None,
+                   "note": "a decode step's wall time = the graph decode on the device "
+                           "(inputs built by ir_build_decode_inputs, then the replay of the "
+                           "28-layer forward) + infrared's host loop (per-sequence greedy "
+                           "sampling, each a device sync; block bookkeeping)"},
         "roofline": {"bound": "hbm", "achieved": round(step_gbs, 1) if ok else None,
                      "peak": peak, "unit": "GB/s",
                      "frac": round(step_gbs / peak, 4) if ok else None, "peak_kind": peak_kind,
@@ -1181,6 +1225,92 @@ def run_model_engine(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_kernels(args):
+    """The path's smaller kernels alone, each timed over K launches captured in
+    one CUDA graph (CUDA events): the standalone K/V cache write
+    (``ir_cache_write``) at the C3 batch (256 new tokens) and at a bulk size
+    (65536 tokens, larger than L2), the log-sum-exp merge (``ir_lse_merge``)
+    of 8 KV-chunk partials at C4 (4 x 28 rows) and at 256 x 28 rows, and the
+    peer-exchange kernel (``ir_peer_exchange``) in a world of one GPU (the
+    flag protocol, the merge and the row writes without NVLink; a capture of
+    its multi-GPU form would hold one GPU's kernel while the other's waits on
+    it). GB/s = algorithmic bytes (reads + writes) / launch time."""
+    import ctypes
+
+    import torch
+
+    from infrared_b200 import _lib, ops
+    from infrared_b200 import workloads as wl
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    lib = _lib.load()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    res = {}
+
+    def timed(name, fn, nbytes, steps):
+        ms = _graph_ms(lambda i: fn(i), steps, dev, 1) / steps
+        res[name] = {"us_per_launch": round(ms * 1e3, 3), "bytes": nbytes,
+                     "GB_s": round(nbytes / (ms / 1e3) / 1e9, 1)}
+
+    # cache write: C3's 256 tokens, and a bulk write larger than L2
+    w3 = wl.c3(seed=0)
+    pool_k = torch.randn(w3.num_slots, 4, 128, generator=g, device=dev).to(torch.bfloat16)
+    pool_v = torch.randn(w3.num_slots, 4, 128, generator=g, device=dev).to(torch.bfloat16)
+    for name, n in (("cache_write_c3", 256), ("cache_write_bulk", 65536)):
+        sets = []
+        for i in range(3):
+            slots = torch.randperm(w3.num_slots, generator=g, device=dev)[:n]
+            if n == 256 and i == 0:
+                slots = torch.from_numpy(w3.slot_mapping).to(dev)
+            k = torch.randn(n, 4, 128, generator=g, device=dev).to(torch.bfloat16)
+            v = torch.randn(n, 4, 128, generator=g, device=dev).to(torch.bfloat16)
+            sets.append((k, v, slots.contiguous()))
+        timed(name, lambda i, sets=sets: ops.cache_write(sets[i % 3][0], sets[i % 3][1],
+                                                         pool_k, pool_v, sets[i % 3][2]),
+              2 * 2 * n * 4 * 128 * 2 + n * 8, args.steps)
+    # log-sum-exp merge of 8 partials
+    for name, b in (("lse_merge_c4", 4), ("lse_merge_b256", 256)):
+        o = torch.randn(8, b, 28, 128, generator=g, device=dev)
+        lse = torch.randn(8, b, 28, generator=g, device=dev)
+        out = torch.empty(b, 28, 128, dtype=torch.bfloat16, device=dev)
+        timed(name, lambda i, o=o, lse=lse, out=out: ops.lse_merge(o, lse, torch.bfloat16,
+                                                                    out=out),
+              o.numel() * 4 + lse.numel() * 4 + out.numel() * 2, args.steps)
+    # peer exchange, world of one (7168 rows of 128)
+    b, h, d = 256, 28, 128
+    o = torch.randn(b, h, d, generator=g, device=dev)
+    lse = torch.randn(b, h, generator=g, device=dev)
+    out = torch.empty(b, h, d, dtype=torch.bfloat16, device=dev)
+    nbytes = lib.ir_peer_exchange_bytes(1, b * h, d)
+    buf = ctypes.c_void_p()
+    _lib.check(lib.ir_peer_alloc(nbytes, ctypes.byref(buf)))
+    arr = (ctypes.c_void_p * 1)(buf.value)
+
+    def exchange(i):
+        _lib.check(lib.ir_peer_exchange(out.data_ptr(), out.stride(0), o.data_ptr(),
+                                        lse.data_ptr(), arr, nbytes, 1, 0, b, h, d,
+                                        ops.dtype_code(out.dtype),
+                                        ops.error_flag(local).data_ptr(), ops._stream(local)))
+
+    timed("peer_exchange_world1_b256", exchange, o.numel() * 4 + lse.numel() * 4 +
+          out.numel() * 2, args.steps)
+    torch.cuda.synchronize(dev)
+    ops.check_device_errors(dev)
+    _lib.check(lib.ir_peer_free(buf))
+    peak, peak_kind = measured_peaks()
+    line = {"metric": "standalone kernel GB/s (algorithmic bytes / launch time)",
+            "value": res["cache_write_bulk"]["GB_s"], "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": 3, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic", "kernels": res, "peak": peak, "peak_kind": peak_kind,
+            "config": {"workload": "cache write (C3 256 tokens; 65536 tokens), lse merge "
+                                   "(8 parts x 4/256 x 28 rows), peer exchange world of one",
+                       "timing": "K launches in one CUDA graph, CUDA events"}}
+    print(json.dumps(line), flush=True)
 
 
 def run_prefill(args):
@@ -1304,6 +1434,8 @@ def main():
         run_model(args)
     elif args.config == "p1":
         run_prefill(args)
+    elif args.config == "kernels":
+        run_kernels(args)
     elif args.config == "c4" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
         run_chunked(args)
     else:

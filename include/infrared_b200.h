@@ -147,13 +147,27 @@ typedef struct ir_decode_shape {
   int64_t num_slots;  /* rows of the pool (num_blocks * block_size) */
   float scale;        /* softmax scale, usually head_dim ** -0.5 */
   int dtype;          /* IR_DTYPE_* of q, pools and out */
+  int flags;          /* 0 or IR_DECODE_DYNAMIC_TAIL; other bits are rejected */
 } ir_decode_shape;
+
+/* ir_decode_shape.flags: the workspace's first IR_DECODE_HEADER_BYTES were
+ * zero when it was first used (cudaMemset once after allocating it). The TMA
+ * kernel then hands out the last ~15 % of the tiles as small units that CTAs
+ * claim from counters in that header as they finish their static share, which
+ * evens out the SMs' random differences in streaming speed; every call leaves
+ * the header zero again. Without the flag the workspace needs no
+ * initialisation and every CTA streams a fixed share. The flag changes the
+ * workspace size (more partial slots); results are deterministic either way
+ * (they do not depend on which CTA took which unit). */
+#define IR_DECODE_DYNAMIC_TAIL 1
+#define IR_DECODE_HEADER_BYTES 256
 
 /* Bytes of workspace the decode calls need for this shape on the current
  * device (0 on an invalid shape). The workspace holds the tile prefix and the
  * partial results of sequences split across CTAs; it must be 256-byte
- * aligned and needs no initialisation. Calls sharing a workspace must not
- * overlap on the GPU (calls on one stream never do). */
+ * aligned and needs no initialisation unless shape->flags asks for the
+ * dynamic tail. Calls sharing a workspace must not overlap on the GPU (calls
+ * on one stream never do). */
 size_t ir_paged_decode_workspace_size(const ir_decode_shape* shape);
 
 /* Kernel choice for this shape on the current device: *path = 1 (CUDA-core

@@ -177,10 +177,15 @@ bool make_pool_map(CUtensorMap* map, const void* pool, int64_t num_slots,
 // ------------------------------------------------------------ planning
 
 struct Plan {
-  int path;  // 1 generic, 2 tma
-  int G;     // CTAs per kv head
-  size_t prefix_off, lse_off, o_off, bytes;
+  int path;     // 1 generic, 2 tma
+  int G;        // CTAs per kv head
+  int dyn;      // dynamic tail units (TMA path, flag set)
+  int64_t slots;  // partial slots per kv head
+  size_t ctr_off, prefix_off, lse_off, o_off, bytes;
 };
+
+// Workspace header: the dynamic tail's counter pair of each kv-head group.
+constexpr size_t kCtrBytes = 256;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -208,6 +213,9 @@ int check_shape(const ir_decode_shape* s) {
   if (elem_bytes(s->dtype) == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
   if (static_cast<int64_t>(s->max_blocks) * s->block_size > INT32_MAX)
     return fail(IR_ERR_UNSUPPORTED, "max_blocks * block_size overflows int32");
+  if (s->flags & ~IR_DECODE_DYNAMIC_TAIL)
+    return fail(IR_ERR_INVALID_ARG, "unknown bits in flags (set it to 0 or "
+                                    "IR_DECODE_DYNAMIC_TAIL)");
   return IR_OK;
 }
 
@@ -233,10 +241,15 @@ int make_plan(const ir_decode_shape* s, Plan* p) {
   p->path = path;
   p->G = G;
   const int64_t B = s->batch, H = s->num_heads, D = s->head_dim;
-  const int64_t slots = static_cast<int64_t>(s->num_kv_heads) * (G + B) *
+  const int groups = path == 2 ? s->num_kv_heads / irb::tma_head_group(s->num_kv_heads) : 0;
+  p->dyn = (s->flags & IR_DECODE_DYNAMIC_TAIL) && path == 2 &&
+           static_cast<size_t>(groups) * 8 <= kCtrBytes;
+  p->slots = G + (p->dyn ? static_cast<int64_t>(irb::kDynUnitsPerCta) * G : 0) + B;
+  const int64_t slots = static_cast<int64_t>(s->num_kv_heads) * p->slots *
                         (H / s->num_kv_heads);
-  p->prefix_off = 0;
-  p->lse_off = align256(static_cast<size_t>(B + 1) * 8);
+  p->ctr_off = 0;
+  p->prefix_off = kCtrBytes;
+  p->lse_off = p->prefix_off + align256(static_cast<size_t>(B + 1) * 8);
   p->o_off = p->lse_off + align256(static_cast<size_t>(slots) * 4);
   p->bytes = p->o_off + align256(static_cast<size_t>(slots * D) * 4);
   return IR_OK;
@@ -314,8 +327,11 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
   a.num_blocks = s->num_slots / s->block_size;
   a.scale_log2 = s->scale * irb::kLog2e;
   a.G = plan.G;
+  a.dyn = plan.dyn && plan.path == 2 ? 1 : 0;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  a.ws_ctr = reinterpret_cast<uint32_t*>(ws + plan.ctr_off);
   a.ws_prefix = reinterpret_cast<int64_t*>(ws + plan.prefix_off);
+  a.ws_slots = plan.slots;
   a.ws_lse = reinterpret_cast<float*>(ws + plan.lse_off);
   a.ws_o = reinterpret_cast<float*>(ws + plan.o_off);
   a.k_pool = k_pool;
@@ -763,8 +779,12 @@ int ir_paged_decode_lse(float* o, float* lse, const void* q,
 int ir_paged_decode_noalloc(void* out, const void* q, const void* k_pool,
                             const void* v_pool, const int32_t* block_tables,
                             const int32_t* context_lens,
-                            const ir_decode_shape* shape, int32_t* err_flag,
+                            const ir_decode_shape* shape_in, int32_t* err_flag,
                             ir_stream_t stream) {
+  if (!shape_in) return fail(IR_ERR_INVALID_ARG, "shape is null");
+  ir_decode_shape local = *shape_in;  // the built-in scratch keeps the static schedule
+  local.flags = 0;
+  const ir_decode_shape* shape = &local;
   Plan plan;
   int rc = make_plan(shape, &plan);
   if (rc) return rc;

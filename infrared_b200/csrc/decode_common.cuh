@@ -13,6 +13,22 @@
 // launched right behind the decode kernel (programmatic dependent launch),
 // combines the pieces of every sequence that spans several CTAs in share
 // order, so results do not depend on scheduling.
+//
+// Dynamic tail (TMA kernel, DecodeArgs::dyn): the tile axis is cut into
+// units instead — Gs static units (equal shares of the first F tiles, one per
+// CTA) followed by U small dynamic units covering tiles [F, T), which the
+// CTAs claim from a counter in the workspace header once their static unit
+// is streamed. SMs stream at slightly different, randomly varying rates, so
+// with static shares alone the last CTA finishes several microseconds after
+// the median one; claimed units let the fast CTAs take more of the tail. A
+// unit plays the part of a share: pieces sit in slot u + b, and the merge
+// finds a sequence's units with unit_of(), a function of T alone, so the
+// result does not depend on which CTA took which unit. The dynamic tiles lie
+// in the last kDynSeqs sequences (their prefixes fit in shared memory for the
+// claim's lookup). The counter pair {claims, CTAs done} of each kv-head group
+// is zero at the start of every call: the caller zeroes the header once when
+// it allocates the workspace, and the last CTA of every call (every exit
+// path counts itself done) sets both back to zero.
 #pragma once
 
 #include "common.cuh"
@@ -36,10 +52,13 @@ struct DecodeArgs {
   int64_t num_slots, num_blocks;
   float scale_log2;  // scale * log2(e)
   int G;             // CTAs per kv head
+  int dyn;           // 1: dynamic tail units (ws_ctr zero at the start of the call)
   // workspace
+  uint32_t* ws_ctr;    // [kv-head groups][2] {claims, CTAs done} of the dynamic tail
   int64_t* ws_prefix;  // [B + 1] tile prefix (written by the first CTA of kv head 0)
-  float* ws_lse;       // [Hkv, G + B, n_rep] log2-sum-exp of partials
-  float* ws_o;         // [Hkv, G + B, n_rep, D] normalised partials
+  int64_t ws_slots;    // partial slots per kv head: G (+ kDynUnitsPerCta * G) + B
+  float* ws_lse;       // [Hkv, ws_slots, n_rep] log2-sum-exp of partials
+  float* ws_o;         // [Hkv, ws_slots, n_rep, D] normalised partials
   // pools (generic kernel reads them directly; fused write stores into them)
   const void* k_pool;
   const void* v_pool;
@@ -80,13 +99,64 @@ __device__ __forceinline__ int shares_used(int64_t total, int G) {
   return total < G ? static_cast<int>(total) : G;
 }
 
+// Dynamic tail tuning: the share of the tiles handed out as claimed units,
+// the smallest unit, the cap on the unit count (per CTA of the grid), the
+// fewest tiles per CTA for which the tail is split at all, and the number of
+// trailing sequences the dynamic tiles may lie in.
+constexpr int kDynPct = 15;
+constexpr int kDynUnitTiles = 4;
+constexpr int kDynUnitsPerCta = 2;
+constexpr int kDynMinTilesPerCta = 8;
+constexpr int kDynSeqs = 32;
+
+struct UnitPlan {
+  int64_t F;    // static tiles [0, F), cut into Gs equal shares
+  int64_t dyn;  // dynamic tiles [F, F + dyn), cut into U units
+  int Gs;       // static units (one per CTA g < Gs)
+  int U;        // dynamic units
+};
+
+// The unit plan of a call with T tiles on G CTAs per kv-head group; p_tail =
+// tile prefix of sequence max(B - kDynSeqs, 0). dyn_on = 0 gives the static
+// plan (Gs = min(T, G) equal shares, no dynamic units).
+__host__ __device__ __forceinline__ UnitPlan unit_plan(int64_t T, int G, int dyn_on,
+                                                       int64_t p_tail) {
+  UnitPlan u{T, 0, 0, 0};
+  if (dyn_on && T >= static_cast<int64_t>(kDynMinTilesPerCta) * G) {
+    int64_t F = T - T * kDynPct / 100;
+    if (F < p_tail) F = p_tail;
+    const int64_t d = T - F;
+    if (d > 0) {
+      const int64_t n = (d + kDynUnitTiles - 1) / kDynUnitTiles;
+      const int64_t cap = static_cast<int64_t>(kDynUnitsPerCta) * G;
+      u.U = static_cast<int>(n < cap ? n : cap);
+      u.F = F;
+      u.dyn = d;
+    }
+  }
+  u.Gs = u.F < G ? static_cast<int>(u.F) : G;
+  return u;
+}
+
+// First tile of unit u (0 <= u <= Gs + U; u = Gs + U gives T).
+__device__ __forceinline__ int64_t unit_start(const UnitPlan& p, int64_t u) {
+  return u < p.Gs ? share_start(u, p.F, p.Gs)
+                  : p.F + share_start(u - p.Gs, p.dyn, p.U);
+}
+
+// Unit holding tile t (0 <= t < T).
+__device__ __forceinline__ int unit_of(const UnitPlan& p, int64_t t) {
+  return t < p.F ? share_of(t, p.F, p.Gs) : p.Gs + share_of(t - p.F, p.dyn, p.U);
+}
+
 struct RangeInfo {
   int64_t total;    // T
-  int64_t start;    // first tile of this CTA
-  int64_t end;      // one past the last tile
+  int64_t start;    // first tile of this CTA's static unit
+  int64_t end;      // one past its last tile
   int64_t p_first;  // prefix of b_first
   int b_first;      // sequence holding tile `start`
-  int G;            // shares used (<= DecodeArgs::G)
+  int G;            // static units (<= DecodeArgs::G)
+  UnitPlan plan;
 };
 
 // Block-wide exclusive scan of one int64 per thread (NT threads, NT % 32 == 0).
@@ -114,13 +184,44 @@ __device__ __forceinline__ int64_t block_excl_scan(int64_t v, int64_t* sm,
   return before + x - v;
 }
 
-// Find this CTA's share. All NT threads must call it. The CTA streams kv
-// heads [kv0, kv0 + nkv). The first CTA of kv head 0 publishes the tile
-// prefix to the workspace for the merge kernel; CTAs with g == 0 write the
-// rows of sequences with no context (no CTA streams them).
+// Prefixes and context lengths of the last kDynSeqs sequences (tailp[i] =
+// prefix of sequence B0 + i, tailp[B - B0] = T, tailc[i] = its clamped
+// context length; B0 = max(B - kDynSeqs, 0)), computed by warp 0 from the
+// context lengths once T is known, so that the producer resolves a dynamic
+// unit without global loads. Warp 0 only; the caller synchronises before the
+// arrays are read.
+__device__ __forceinline__ void tail_prefixes(const DecodeArgs& a, int64_t total,
+                                              int64_t* tailp, int* tailc) {
+  const int lane = threadIdx.x & 31;
+  const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
+  const int nt = a.B - b0;
+  const int c = lane < nt ? clamp_ctx(a.context_lens[b0 + lane], a) : 0;
+  const int n = (c + kTile - 1) / kTile;
+  // suffix sum from this lane to the last: inclusive scan of the reversed lanes
+  int suf = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, suf, o);
+    if (lane + o < 32) suf += y;
+  }
+  if (lane < nt) {
+    tailp[lane] = total - suf;
+    tailc[lane] = c;
+  }
+  if (lane == 0) tailp[nt] = total;
+}
+
+// Find this CTA's share (its static unit under a dynamic plan). All NT
+// threads must call it. The CTA streams kv heads [kv0, kv0 + nkv). The first
+// CTA of kv head 0 publishes the tile prefix to the workspace for the merge
+// kernel; CTAs with g == 0 write the rows of sequences with no context (no
+// CTA streams them). With a.dyn, tailp / tailc (shared memory, kDynSeqs + 1
+// and kDynSeqs entries) receive the prefixes and context lengths of the
+// sequences the dynamic tiles lie in.
 template <int NT, typename T>
 __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
-                           RangeInfo* ri, int64_t* sm_scan) {
+                           RangeInfo* ri, int64_t* sm_scan, int64_t* tailp = nullptr,
+                           int* tailc = nullptr) {
   const int tid = threadIdx.x;
   const bool publish = (g == 0 && kv0 == 0);
   auto empty_rows = [&](int b) {
@@ -135,6 +236,13 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
       }
     }
   };
+  // the unit plan once T is known (tail prefixes first when dynamic)
+  auto make_plan = [&](int64_t total) {
+    const bool dyn = a.dyn && tailp != nullptr;
+    if (dyn && tid < 32) tail_prefixes(a, total, tailp, tailc);
+    if (dyn) __syncthreads();
+    return unit_plan(total, a.G, dyn ? 1 : 0, dyn ? tailp[0] : 0);
+  };
   if (tid == 0) ri->b_first = -1;
   if (a.B <= NT) {
     // one pass: every thread owns one sequence
@@ -147,9 +255,10 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
     }
     int64_t total = 0;
     const int64_t p = block_excl_scan<NT>(n, sm_scan, &total);  // synchronises
-    const int G = shares_used(total, a.G);
-    const int64_t start = g < G ? share_start(g, total, G) : total;
-    const int64_t end = g < G ? share_start(g + 1, total, G) : total;
+    const UnitPlan up = make_plan(total);
+    const int G = up.Gs;
+    const int64_t start = g < G ? share_start(g, up.F, G) : total;
+    const int64_t end = g < G ? share_start(g + 1, up.F, G) : total;
     if (b < a.B) {
       if (publish) a.ws_prefix[b] = p;
       if (n > 0 && p <= start && start < p + n) {
@@ -163,6 +272,7 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
       ri->start = start;
       ri->end = end;
       ri->G = G;
+      ri->plan = up;
       if (publish) a.ws_prefix[a.B] = total;
     }
     __syncthreads();
@@ -177,9 +287,10 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
   }
   int64_t total = 0;
   block_excl_scan<NT>(mine, sm_scan, &total);
-  const int G = shares_used(total, a.G);
-  const int64_t start = g < G ? share_start(g, total, G) : total;
-  const int64_t end = g < G ? share_start(g + 1, total, G) : total;
+  const UnitPlan up = make_plan(total);
+  const int G = up.Gs;
+  const int64_t start = g < G ? share_start(g, up.F, G) : total;
+  const int64_t end = g < G ? share_start(g + 1, up.F, G) : total;
   // pass 2: prefix of every sequence; locate `start`
   int64_t running = 0;
   for (int base = 0; base < a.B; base += NT) {
@@ -202,6 +313,7 @@ __device__ void find_share(const DecodeArgs& a, int g, int kv0, int nkv,
     ri->start = start;
     ri->end = end;
     ri->G = G;
+    ri->plan = up;
     if (publish) a.ws_prefix[a.B] = total;
   }
   __syncthreads();
@@ -223,8 +335,7 @@ __device__ __forceinline__ void write_segment_value(const DecodeArgs& a,
           DT<T>::from_f(val);
     }
   } else {
-    const int64_t slot =
-        static_cast<int64_t>(kvh) * (a.G + a.B) + g + b;
+    const int64_t slot = static_cast<int64_t>(kvh) * a.ws_slots + g + b;
     a.ws_o[(slot * a.n_rep + n) * a.D + d] = val;
     if (d == 0) a.ws_lse[slot * a.n_rep + n] = lse2;
   }

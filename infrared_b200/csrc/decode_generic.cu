@@ -201,11 +201,13 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
   const int64_t nb = a.ws_prefix[b + 1] - pb;
   const int64_t total = a.ws_prefix[a.B];
   if (nb <= 0) return;  // empty context: written by the decode kernel
-  const int G = shares_used(total, a.G);
-  const int glo = share_of(pb, total, G);
-  const int parts = share_of(pb + nb - 1, total, G) - glo + 1;
-  if (parts == 1) return;  // written whole by one CTA
-  const int64_t base = static_cast<int64_t>(kvh) * (a.G + a.B) + glo + b;
+  // the decode kernel's units (static shares, then dynamic units if any)
+  const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
+  const UnitPlan up = unit_plan(total, a.G, a.dyn, a.dyn ? a.ws_prefix[b0] : 0);
+  const int glo = unit_of(up, pb);
+  const int parts = unit_of(up, pb + nb - 1) - glo + 1;
+  if (parts == 1) return;  // written whole by one unit
+  const int64_t base = static_cast<int64_t>(kvh) * a.ws_slots + glo + b;
   const float* lse = a.ws_lse + base * a.n_rep + n;       // stride n_rep per piece
   const float* o = a.ws_o + (base * a.n_rep + n) * a.D;   // stride n_rep * D per piece
   const int64_t ostride = static_cast<int64_t>(a.n_rep) * a.D;
@@ -339,10 +341,14 @@ int launch_merge_t(const DecodeArgs& a, cudaStream_t s) {
 
 template <typename T>
 int launch_merge_w(const DecodeArgs& a, cudaStream_t s) {
-  // a sequence of average length spans about G / B shares: with 8 or more
-  // pieces per row, 8 warps fold them in half the rounds
-  if (a.G >= 16 * a.B) return launch_merge_t<T, 16>(a, s);
-  return a.G >= 8 * a.B ? launch_merge_t<T, 8>(a, s) : launch_merge_t<T, 4>(a, s);
+  // a sequence of average length spans about G / B shares, and the rows of
+  // the last kDynSeqs sequences also hold the dynamic units: with 8 or 16 or
+  // more pieces per row, 8 or 16 warps fold them in fewer rounds
+  const int b = a.B > 0 ? a.B : 1;
+  const int tail = b < kDynSeqs ? b : kDynSeqs;
+  const int pieces = a.G / b + (a.dyn ? kDynUnitsPerCta * a.G / tail : 0);
+  if (pieces >= 16) return launch_merge_t<T, 16>(a, s);
+  return pieces >= 8 ? launch_merge_t<T, 8>(a, s) : launch_merge_t<T, 4>(a, s);
 }
 
 int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {

@@ -25,6 +25,13 @@
 // otherwise cap a CUDA-core GEMV at ~7 FMAs per loaded element. A warp writes
 // its segment's row (or workspace piece) itself when the sequence changes;
 // no cross-warp combine is needed.
+//
+// With the dynamic tail (DecodeArgs::dyn, decode_common.cuh) the producer
+// streams its static unit, then claims dynamic units from the workspace
+// counter until none is left; a unit start is a segment start, and the unit
+// index travels to the consumers in the item descriptor (pieces sit in slot
+// unit + b). The producer counts its CTA done after its last claim; the last
+// CTA of the kv-head group sets the counters back to zero.
 #include "decode_common.cuh"
 #include "kernels.h"
 
@@ -37,7 +44,7 @@ constexpr unsigned kFull = 0xffffffffu;
 struct __align__(16) ItemDesc {
   int b;
   int tok0;
-  int seg;
+  int seg;     // (unit << 1) | (segment index & 1): workspace unit, q buffer
   int packed;  // n_valid in bits 0-7, flags above
 };
 constexpr int kFlagValid = 1 << 8;     // copies were issued (block ids valid)
@@ -57,10 +64,14 @@ struct Layout {
   static constexpr int off_desc = NS * kStage;
   static constexpr int off_bar = off_desc + NS * 16;  // full[NS], empty[NS], qfree[2]
   static constexpr int off_misc = off_bar + (2 * NS + 2) * 8;
+  // misc: RangeInfo (64 B) + block-scan scratch (8 B per warp, <= 9 warps);
+  // then the prefixes of the sequences the dynamic tail units lie in
+  static constexpr int off_tail = off_misc + 160;
+  static constexpr int kTailBytes = ((kDynSeqs + 1) * 8 + kDynSeqs * 4 + 15) / 16 * 16;
   // per consumer warp: [8 heads][D + 4] fp32 output staging + 8 lse values
   static constexpr int kFlushStride = D + 4;  // padding spreads the 4 column lanes over banks
   static constexpr int kFlushFloats = 8 * kFlushStride + 8;
-  static constexpr int off_flush = off_misc + 128;
+  static constexpr int off_flush = off_tail + kTailBytes;
   // q rows of the current and next segment: [2][HG * 8 heads][D] of T
   static constexpr int kQBuf = HG * 8 * D * 2;
   static constexpr int off_q = (off_flush + HG * kFlushFloats * 4 + 127) / 128 * 128;
@@ -97,7 +108,10 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   uint64_t* empty = full + NS;
   uint64_t* qfree = empty + NS;  // [2]: consumers are done reading a q buffer
   RangeInfo* ri = reinterpret_cast<RangeInfo*>(smem + L::off_misc);
+  static_assert(sizeof(RangeInfo) <= 64, "RangeInfo fits its shared-memory slot");
   int64_t* sm_scan = reinterpret_cast<int64_t*>(smem + L::off_misc + 64);
+  int64_t* tailp = reinterpret_cast<int64_t*>(smem + L::off_tail);
+  int* tailc = reinterpret_cast<int*>(smem + L::off_tail + (kDynSeqs + 1) * 8);
   ItemDesc* desc = reinterpret_cast<ItemDesc*>(smem + L::off_desc);
 
   if (threadIdx.x == 0) {
@@ -117,162 +131,224 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   // the previous kernel in the stream; nothing below runs before that kernel
   // has finished and its writes are visible (no input is read earlier).
   wait_prerequisites();
-  find_share<NT, T>(a, g, kv0, HG, ri, sm_scan);  // includes __syncthreads
+  find_share<NT, T>(a, g, kv0, HG, ri, sm_scan, tailp, tailc);  // includes __syncthreads
   launch_dependents();
   const int64_t start = ri->start, end = ri->end;
-  if (start >= end) return;
+  const UnitPlan up = ri->plan;
+  if (start >= end && up.U == 0) return;  // no static share and no units to claim
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    const bool dyn = up.U > 0;
+    uint32_t* ctr = dyn ? a.ws_ctr + 2 * hg : nullptr;
+    const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
+    int64_t ustart = start, uend = end;  // the static unit first, then claimed ones
+    int unit = g;
     int b = ri->b_first;
     int64_t pb = ri->p_first;
-    int nb = tiles_of(a, b);
     int seg_base = 0;
     uint32_t item = 0;
     bool abort = false;
-    for (int64_t t = start; t < end && !abort;) {
-      const int64_t tt = t + lane;
-      const bool active = tt < end;
-      int lb = b, ln = nb;
-      int64_t lp = pb;
-      if (active) {
-        while (tt >= lp + ln) {
-          lp += ln;
-          ++lb;
-          ln = tiles_of(a, lb);
-        }
-      }
-      const int j = static_cast<int>(tt - lp);
-      const int tok0 = j * kTile;
-      int packed = 0;
-      int64_t row0 = 0, row1 = -1;
-      bool seg_start = false;
-      if (active) {
-        const int ctx = clamp_ctx(a.context_lens[lb], a);
-        const int nvalid = min(kTile, ctx - tok0);
-        const int32_t* btr = a.block_tables + lb * a.bt_stride;
-        bool ok;
-        if (R == 8) {
-          const int blk = tok0 >> 3;
-          const int id0 = btr[blk];
-          ok = id0 >= 0 && id0 < a.num_blocks;
-          row0 = static_cast<int64_t>(id0) * 8;
-          if (nvalid > 8) {
-            const int id1 = btr[blk + 1];
-            ok = ok && id1 >= 0 && id1 < a.num_blocks;
-            row1 = static_cast<int64_t>(id1) * 8;
-          }
-        } else {
-          const int blk = tok0 / a.bs;
-          const int id0 = btr[blk];
-          ok = id0 >= 0 && id0 < a.num_blocks;
-          row0 = static_cast<int64_t>(id0) * a.bs + (tok0 - blk * a.bs);
-        }
-        if (!ok) set_err(a.err, IR_DEVERR_BLOCK_ID);
-        seg_start = (tt == start) || (j == 0);
-        const bool whole = (lp >= start) && (lp + ln <= end);
-        packed = nvalid | (ok ? kFlagValid : 0) | (j == ln - 1 ? kFlagSeqEnd : 0) |
-                 (whole ? kFlagWhole : 0) | (seg_start ? kFlagSegStart : 0);
-      }
-      const unsigned starts = __ballot_sync(kFull, active && seg_start);
-      const unsigned le_mask = (lane == 31) ? kFull : ((2u << lane) - 1u);
-      const int seg = seg_base + __popc(starts & le_mask) - 1;
-      const int nact = (end - t) < 32 ? static_cast<int>(end - t) : 32;
-      for (int k = 0; k < nact; ++k) {
-        const uint32_t slot = item % NS;
-        const uint32_t par = ((item / NS) & 1u) ^ 1u;
-        int ok_wait = 1;
-        if (lane == 0) ok_wait = mbar_wait_bounded(&empty[slot], par) ? 1 : 0;
-        ok_wait = __shfl_sync(kFull, ok_wait, 0);
-        if (!ok_wait) {
-          if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
+    // a claim issued ahead: lane 0 asks for the next unit two tiles before the
+    // current unit's last one is issued, so the atomic's round trip overlaps
+    // them instead of stalling the ring between units
+    bool have_claim = false;
+    int claim = 0;
+    // tiles and context length of sequence lb: shared memory for the tail
+    // sequences of a dynamic plan, else the context lengths in global memory
+    auto seq_tiles = [&](int lb) {
+      return (dyn && lb >= b0) ? static_cast<int>(tailp[lb - b0 + 1] - tailp[lb - b0])
+                               : tiles_of(a, lb);
+    };
+    auto seq_ctx = [&](int lb) {
+      return (dyn && lb >= b0) ? tailc[lb - b0] : clamp_ctx(a.context_lens[lb], a);
+    };
+    while (!abort) {
+      if (ustart >= uend) {
+        if (!dyn) break;
+        int u = claim;
+        if (!have_claim && lane == 0) u = static_cast<int>(atomicAdd(ctr, 1u));
+        have_claim = false;
+        u = __shfl_sync(kFull, u, 0);
+        if (u >= up.U) break;  // every unit is taken
+        unit = up.Gs + u;
+        ustart = unit_start(up, unit);
+        uend = unit_start(up, unit + 1);
+        // the sequence holding ustart, among the last kDynSeqs sequences
+        const int nt = a.B - b0;
+        const bool hit = lane < nt && tailp[lane] <= ustart && ustart < tailp[lane + 1];
+        const unsigned m = __ballot_sync(kFull, hit);
+        if (m == 0u) {  // cannot happen with a consistent plan; never stream blind
+          if (lane == 0) set_err(a.err, IR_DEVERR_CONTEXT_LEN);
           abort = true;
           break;
         }
-        const int kb = __shfl_sync(kFull, lb, k);
-        const int ktok = __shfl_sync(kFull, tok0, k);
-        const int kseg = __shfl_sync(kFull, seg, k);
-        const int kpk = __shfl_sync(kFull, packed, k);
-        const int64_t kr0 = __shfl_sync(kFull, row0, k);
-        const int64_t kr1 = __shfl_sync(kFull, row1, k);
-        // a segment's first tile also brings the segment's q rows (buffer
-        // seg & 1), once the consumers have loaded segment seg - 2's q
-        const bool with_q = tp.q_bulk && (kpk & kFlagSegStart);
-        if (with_q && kseg >= 2) {
-          int okq = 1;
-          if (lane == 0)
-            okq = mbar_wait_bounded(&qfree[kseg & 1], ((kseg >> 1) + 1) & 1) ? 1 : 0;
-          if (!__shfl_sync(kFull, okq, 0)) {
+        const int i = __ffs(m) - 1;
+        b = b0 + i;
+        pb = tailp[i];
+      }
+      int nb = seq_tiles(b);
+      for (int64_t t = ustart; t < uend && !abort;) {
+        const int64_t tt = t + lane;
+        const bool active = tt < uend;
+        int lb = b, ln = nb;
+        int64_t lp = pb;
+        if (active) {
+          while (tt >= lp + ln) {
+            lp += ln;
+            ++lb;
+            ln = seq_tiles(lb);
+          }
+        }
+        const int j = static_cast<int>(tt - lp);
+        const int tok0 = j * kTile;
+        int packed = 0;
+        int64_t row0 = 0, row1 = -1;
+        bool seg_start = false;
+        if (active) {
+          const int ctx = seq_ctx(lb);
+          const int nvalid = min(kTile, ctx - tok0);
+          const int32_t* btr = a.block_tables + lb * a.bt_stride;
+          bool ok;
+          if (R == 8) {
+            const int blk = tok0 >> 3;
+            const int id0 = btr[blk];
+            ok = id0 >= 0 && id0 < a.num_blocks;
+            row0 = static_cast<int64_t>(id0) * 8;
+            if (nvalid > 8) {
+              const int id1 = btr[blk + 1];
+              ok = ok && id1 >= 0 && id1 < a.num_blocks;
+              row1 = static_cast<int64_t>(id1) * 8;
+            }
+          } else {
+            const int blk = tok0 / a.bs;
+            const int id0 = btr[blk];
+            ok = id0 >= 0 && id0 < a.num_blocks;
+            row0 = static_cast<int64_t>(id0) * a.bs + (tok0 - blk * a.bs);
+          }
+          if (!ok) set_err(a.err, IR_DEVERR_BLOCK_ID);
+          seg_start = (tt == ustart) || (j == 0);
+          const bool whole = (lp >= ustart) && (lp + ln <= uend);
+          packed = nvalid | (ok ? kFlagValid : 0) | (j == ln - 1 ? kFlagSeqEnd : 0) |
+                   (whole ? kFlagWhole : 0) | (seg_start ? kFlagSegStart : 0);
+        }
+        const unsigned starts = __ballot_sync(kFull, active && seg_start);
+        const unsigned le_mask = (lane == 31) ? kFull : ((2u << lane) - 1u);
+        const int seg = seg_base + __popc(starts & le_mask) - 1;
+        const int nact = (uend - t) < 32 ? static_cast<int>(uend - t) : 32;
+        const int claim_at = (dyn && t + nact >= uend) ? (nact >= 2 ? nact - 2 : 0) : -1;
+        for (int k = 0; k < nact; ++k) {
+          if (k == claim_at && !have_claim) {
+            if (lane == 0) claim = static_cast<int>(atomicAdd(ctr, 1u));
+            have_claim = true;
+          }
+          const uint32_t slot = item % NS;
+          const uint32_t par = ((item / NS) & 1u) ^ 1u;
+          int ok_wait = 1;
+          if (lane == 0) ok_wait = mbar_wait_bounded(&empty[slot], par) ? 1 : 0;
+          ok_wait = __shfl_sync(kFull, ok_wait, 0);
+          if (!ok_wait) {
             if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
             abort = true;
             break;
           }
-        }
-        if (lane == 0) {
-          desc[slot] = ItemDesc{kb, ktok, kseg, kpk};
-          uint8_t* kd = smem + slot * L::kStage;
-          uint8_t* vd = kd + L::kSide;
-          const uint32_t qrows = static_cast<uint32_t>(HG * a.n_rep * D * 2);
-          const uint32_t qbytes = with_q ? qrows + (tp.rope_smem ? D * 8u : 0u) : 0u;
-          const bool valid = (kpk & kFlagValid) != 0;
-          const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
-          const uint32_t tbytes = valid ? static_cast<uint32_t>(nbox * 2 * L::kBox) : 0u;
-          const uint32_t never = (tp.stall && item == 0 && g == 0 && hg == 0) ? 16u : 0u;
-          if (valid || with_q)
-            mbar_arrive_expect_tx(&full[slot], tbytes + qbytes + never);
-          else
-            mbar_arrive(&full[slot]);  // invalid tile: nothing to wait for
-          if (with_q) {
-            const T* qsrc = reinterpret_cast<const T*>(a.q) + kb * a.q_stride +
-                            static_cast<int64_t>(kv0 * a.n_rep) * D;
-            uint8_t* qdst = smem + L::off_q + (kseg & 1) * L::kQBuf;
-            bulk_load(qdst, qsrc, qrows, &full[slot]);
-            if (tp.rope_smem) {
-              bulk_load(qdst + qrows, a.rope_cos + kb * a.rope_stride, D * 4, &full[slot]);
-              bulk_load(qdst + qrows + D * 4, a.rope_sin + kb * a.rope_stride, D * 4,
-                        &full[slot]);
+          const int kb = __shfl_sync(kFull, lb, k);
+          const int ktok = __shfl_sync(kFull, tok0, k);
+          const int kseg = __shfl_sync(kFull, seg, k);
+          const int kpk = __shfl_sync(kFull, packed, k);
+          const int64_t kr0 = __shfl_sync(kFull, row0, k);
+          const int64_t kr1 = __shfl_sync(kFull, row1, k);
+          // a segment's first tile also brings the segment's q rows (buffer
+          // seg & 1), once the consumers have loaded segment seg - 2's q
+          const bool with_q = tp.q_bulk && (kpk & kFlagSegStart);
+          if (with_q && kseg >= 2) {
+            int okq = 1;
+            if (lane == 0)
+              okq = mbar_wait_bounded(&qfree[kseg & 1], ((kseg >> 1) + 1) & 1) ? 1 : 0;
+            if (!__shfl_sync(kFull, okq, 0)) {
+              if (lane == 0) set_err(a.err, IR_DEVERR_TIMEOUT);
+              abort = true;
+              break;
             }
           }
-          if (valid) {
-            for (int bx = 0; bx < nbox; ++bx) {
-              const int row = static_cast<int>(bx == 0 ? kr0 : kr1);
-              if (tp.one_box) {
-                tma_load_4d(kd + bx * L::kBox, &tmk, &full[slot], 0, row, 0, kv0);
-                tma_load_4d(vd + bx * L::kBox, &tmv, &full[slot], 0, row, 0, kv0);
-              } else {
-#pragma unroll
-                for (int h = 0; h < HG; ++h) {
-#pragma unroll
-                  for (int hf = 0; hf < L::kHalves; ++hf) {
-                    const int off = bx * L::kBox + (h * L::kHalves + hf) * L::kRegion;
-                    tma_load_3d(kd + off, &tmk, &full[slot], 64 * hf, kv0 + h, row);
-                    tma_load_3d(vd + off, &tmv, &full[slot], 64 * hf, kv0 + h, row);
+          if (lane == 0) {
+            desc[slot] = ItemDesc{kb, ktok, (unit << 1) | (kseg & 1), kpk};
+            uint8_t* kd = smem + slot * L::kStage;
+            uint8_t* vd = kd + L::kSide;
+            const uint32_t qrows = static_cast<uint32_t>(HG * a.n_rep * D * 2);
+            const uint32_t qbytes = with_q ? qrows + (tp.rope_smem ? D * 8u : 0u) : 0u;
+            const bool valid = (kpk & kFlagValid) != 0;
+            const int nbox = (R == 8 && kr1 < 0) ? 1 : kTile / R;
+            const uint32_t tbytes = valid ? static_cast<uint32_t>(nbox * 2 * L::kBox) : 0u;
+            const uint32_t never = (tp.stall && item == 0 && g == 0 && hg == 0) ? 16u : 0u;
+            if (valid || with_q)
+              mbar_arrive_expect_tx(&full[slot], tbytes + qbytes + never);
+            else
+              mbar_arrive(&full[slot]);  // invalid tile: nothing to wait for
+            if (with_q) {
+              const T* qsrc = reinterpret_cast<const T*>(a.q) + kb * a.q_stride +
+                              static_cast<int64_t>(kv0 * a.n_rep) * D;
+              uint8_t* qdst = smem + L::off_q + (kseg & 1) * L::kQBuf;
+              bulk_load(qdst, qsrc, qrows, &full[slot]);
+              if (tp.rope_smem) {
+                bulk_load(qdst + qrows, a.rope_cos + kb * a.rope_stride, D * 4, &full[slot]);
+                bulk_load(qdst + qrows + D * 4, a.rope_sin + kb * a.rope_stride, D * 4,
+                          &full[slot]);
+              }
+            }
+            if (valid) {
+              for (int bx = 0; bx < nbox; ++bx) {
+                const int row = static_cast<int>(bx == 0 ? kr0 : kr1);
+                if (tp.one_box) {
+                  tma_load_4d(kd + bx * L::kBox, &tmk, &full[slot], 0, row, 0, kv0);
+                  tma_load_4d(vd + bx * L::kBox, &tmv, &full[slot], 0, row, 0, kv0);
+                } else {
+  #pragma unroll
+                  for (int h = 0; h < HG; ++h) {
+  #pragma unroll
+                    for (int hf = 0; hf < L::kHalves; ++hf) {
+                      const int off = bx * L::kBox + (h * L::kHalves + hf) * L::kRegion;
+                      tma_load_3d(kd + off, &tmk, &full[slot], 64 * hf, kv0 + h, row);
+                      tma_load_3d(vd + off, &tmv, &full[slot], 64 * hf, kv0 + h, row);
+                    }
                   }
                 }
               }
             }
           }
+          ++item;
         }
-        ++item;
+        if (abort) break;
+        const int last = nact - 1;
+        b = __shfl_sync(kFull, lb, last);
+        pb = __shfl_sync(kFull, lp, last);
+        nb = __shfl_sync(kFull, ln, last);
+        seg_base += __popc(starts);
+        t += nact;
       }
-      if (abort) break;
-      const int last = nact - 1;
-      b = __shfl_sync(kFull, lb, last);
-      pb = __shfl_sync(kFull, lp, last);
-      nb = __shfl_sync(kFull, ln, last);
-      seg_base += __popc(starts);
-      t += nact;
+      ustart = uend;  // this unit is issued
     }
     if (!abort) {
       const uint32_t slot = item % NS;
       const uint32_t par = ((item / NS) & 1u) ^ 1u;
       if (lane == 0) {
         if (mbar_wait_bounded(&empty[slot], par)) {
-          desc[slot] = ItemDesc{0, 0, seg_base, kFlagEnd};
+          desc[slot] = ItemDesc{0, 0, 0, kFlagEnd};
           mbar_arrive(&full[slot]);
         } else {
           set_err(a.err, IR_DEVERR_TIMEOUT);
         }
+      }
+    }
+    if (dyn && lane == 0) {
+      // after this CTA's last claim: count it done; the last CTA of the group
+      // leaves the counters at zero for the next call (every exit path of the
+      // producer, aborted ones included, comes through here)
+      __threadfence();
+      const uint32_t old = atomicAdd(ctr + 1, 1u);
+      if (old == gridDim.y - 1) {
+        atomicExch(ctr, 0u);
+        atomicExch(ctr + 1, 0u);
       }
     }
     return;
@@ -305,7 +381,7 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   }
   m[0] = m[1] = -INFINITY;
   l[0] = l[1] = 0.f;
-  int seg_b = -1;
+  int seg_b = -1, seg_unit = 0;
   bool seg_whole = false, have_seg = false;
 
   float* fbuf = reinterpret_cast<float*>(smem + L::off_flush) + head * L::kFlushFloats;
@@ -359,7 +435,7 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
         dst = a.lse_o + (static_cast<int64_t>(seg_b) * a.H + kvh * nr) * D;
         ldst = a.lse_out + static_cast<int64_t>(seg_b) * a.H + kvh * nr;
       } else {
-        const int64_t slot = static_cast<int64_t>(kvh) * (a.G + a.B) + g + seg_b;
+        const int64_t slot = static_cast<int64_t>(kvh) * a.ws_slots + seg_unit + seg_b;
         dst = a.ws_o + slot * nr * D;
         ldst = a.ws_lse + slot * nr;
       }
@@ -394,6 +470,7 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
     if (pk & kFlagSegStart) {
       have_seg = true;
       seg_b = b;
+      seg_unit = dsc.seg >> 1;
       seg_whole = (pk & kFlagWhole) != 0;
       // this segment's q as B fragments: from the staged rows, else global
       const T* qrow = tp.q_bulk
@@ -569,7 +646,8 @@ constexpr int stages_for() {
   constexpr int stage = 2 * HG * (D / 64) * kTile * 128;  // K + V of one tile
   constexpr int flush = HG * (8 * (D + 4) + 8) * 4;
   constexpr int qbuf = 2 * HG * 8 * D * 2;
-  constexpr int budget = 227 * 1024 - 1024 - 640 - flush - qbuf;  // align slack, misc
+  constexpr int tail = ((kDynSeqs + 1) * 8 + kDynSeqs * 4 + 15) / 16 * 16;
+  constexpr int budget = 227 * 1024 - 1024 - 672 - tail - flush - qbuf;  // align slack, misc
   constexpr int fit = budget / (stage + 48);                // + desc and barriers
   constexpr int n = fit < IRB_TMA_STAGES ? fit : IRB_TMA_STAGES;
   return n < 2 ? 2 : n;

@@ -114,16 +114,44 @@ def _stream(device_index: int) -> int:
     return torch.cuda.current_stream(device_index).cuda_stream
 
 
+# The library's own (cached) workspaces ask for the dynamic tail only when
+# this is set: on B200 the static shares measured faster (see
+# decode_workspace); the dynamic schedule stays available for workspaces
+# made with decode_workspace(dynamic=True).
+DYNAMIC_TAIL_DEFAULT = False
+
+
+def decode_workspace(nbytes: int, device, dynamic: bool = True) -> torch.Tensor:
+    """A decode workspace of ``nbytes`` (at least 1 MiB) on ``device`` with its
+    header zeroed. With ``dynamic`` it is marked so that the decode calls
+    given it hand out the last part of the work dynamically
+    (``IR_DECODE_DYNAMIC_TAIL``; the kernels leave the header zero after
+    every call); unmarked workspaces (and any other tensor) get the static
+    schedule, one fixed share per CTA."""
+    t = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8,
+                    device=torch.device("cuda", _index_of(device)))
+    # allocated inside a graph capture the zeroing only runs at replay: such
+    # a workspace keeps the static schedule
+    t._irb_zeroed_header = dynamic and not torch.cuda.is_current_stream_capturing()
+    return t
+
+
+def _header_zeroed(ws: torch.Tensor | None) -> bool:
+    if ws is None:
+        return DYNAMIC_TAIL_DEFAULT
+    return bool(getattr(ws, "_irb_zeroed_header", False))
+
+
 def workspace(nbytes: int, device_index: int) -> torch.Tensor:
-    """A cached, growing per-device workspace buffer (256-byte aligned)."""
+    """A cached, growing per-device workspace buffer (256-byte aligned, header
+    zeroed: see :func:`decode_workspace`)."""
     t = _workspaces.get(device_index)
     if t is not None and t.numel() >= nbytes:
         return t
     with _state_lock:
         t = _workspaces.get(device_index)
         if t is None or t.numel() < nbytes:
-            t = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8,
-                            device=torch.device("cuda", device_index))
+            t = decode_workspace(nbytes, device_index, dynamic=DYNAMIC_TAIL_DEFAULT)
             _workspaces[device_index] = t
     return t
 
@@ -230,7 +258,8 @@ def derive_block_metadata(gather_slots: torch.Tensor, mask: torch.Tensor, block_
 
 
 def _shape(q: torch.Tensor, k_pool: torch.Tensor, block_tables: torch.Tensor,
-           block_size: int, scale: float, out_stride: int) -> DecodeShape:
+           block_size: int, scale: float, out_stride: int,
+           dynamic: bool = False) -> DecodeShape:
     b, h, d = q.shape
     hkv = k_pool.shape[1]
     s = DecodeShape()
@@ -246,6 +275,7 @@ def _shape(q: torch.Tensor, k_pool: torch.Tensor, block_tables: torch.Tensor,
     s.num_slots = k_pool.shape[0]
     s.scale = float(scale)
     s.dtype = dtype_code(q.dtype)
+    s.flags = _lib.IR_DECODE_DYNAMIC_TAIL if dynamic else 0
     return s
 
 
@@ -275,26 +305,44 @@ def _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens):
             raise ValueError("all tensors must be on the same device")
 
 
-def decode_plan(q, k_pool, block_tables, block_size, scale=1.0):
-    """``(path, ctas_per_kv_head, workspace_bytes)`` the library picks for this call."""
-    s = _shape(q, k_pool, block_tables, block_size, scale, q.shape[1] * q.shape[2])
+def decode_plan(q, k_pool, block_tables, block_size, scale=1.0, dynamic=False):
+    """``(path, ctas_per_kv_head, workspace_bytes)`` the library picks for this
+    call (``dynamic``: with a workspace from ``decode_workspace(dynamic=True)``)."""
+    s = _shape(q, k_pool, block_tables, block_size, scale, q.shape[1] * q.shape[2], dynamic)
     lib = _lib.load()
     path, g = _lib.c_int(), _lib.c_int()
     check(lib.ir_paged_decode_plan(s, path, g))
     return path.value, g.value, lib.ir_paged_decode_workspace_size(s)
 
 
-def _ws(s: DecodeShape, dev: int, ws: torch.Tensor | None) -> torch.Tensor:
-    """The call's workspace: the caller's, or the cached per-device one."""
+def _size_of(s: DecodeShape) -> int:
     lib = _lib.load()
     nbytes = lib.ir_paged_decode_workspace_size(s)
     if nbytes == 0:
         check(lib.ir_paged_decode_plan(s, None, None))
-    if ws is None:
-        ws = workspace(nbytes, dev)
-    elif ws.numel() < nbytes:
-        raise ValueError(f"workspace of {ws.numel()} bytes < {nbytes} needed")
-    return ws
+    return nbytes
+
+
+def _ws_and_shape(make_shape, dev: int, ws: torch.Tensor | None, sized=None):
+    """``(shape, workspace)`` of a decode call. The dynamic tail is asked for
+    when the workspace's header is known to be zero: the caller's when it is
+    marked (:func:`decode_workspace`), the cached per-device one unless it was
+    allocated inside a graph capture. ``make_shape(dynamic)`` builds the
+    shape; ``sized(dynamic)`` may return a cached ``(shape, bytes)``."""
+    sized = sized or (lambda dyn: (make_shape(dyn), None))
+    if ws is not None:
+        dynamic = _header_zeroed(ws)
+        s, nbytes = sized(dynamic)
+        nbytes = _size_of(s) if nbytes is None else nbytes
+        if ws.numel() < nbytes:
+            raise ValueError(f"workspace of {ws.numel()} bytes < {nbytes} needed")
+        return s, ws
+    s, nbytes = sized(DYNAMIC_TAIL_DEFAULT)
+    nbytes = _size_of(s) if nbytes is None else nbytes
+    ws = workspace(nbytes, dev)
+    if DYNAMIC_TAIL_DEFAULT and not _header_zeroed(ws):   # static (needs fewer bytes)
+        s, _ = sized(False)
+    return s, ws
 
 
 # Validated call plans of paged_decode, keyed by everything the checks look
@@ -325,26 +373,25 @@ def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     """
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    key = _decode_key(q, k_pool, v_pool, block_tables, context_lens, out, block_size, scale)
-    plan = _plans.get(key)
-    if plan is None:
-        _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
-        if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
-                out.stride(1) != q.shape[2] or out.device != q.device:
-            raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
-        s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
-        nbytes = _lib.load().ir_paged_decode_workspace_size(s)
-        if nbytes == 0:
-            check(_lib.load().ir_paged_decode_plan(s, None, None))
-        plan = (s, nbytes, _dev_index(q))
-        if len(_plans) > 512:
-            _plans.clear()
-        _plans[key] = plan
-    s, nbytes, dev = plan
-    if ws is None:
-        ws = workspace(nbytes, dev)
-    elif ws.numel() < nbytes:
-        raise ValueError(f"workspace of {ws.numel()} bytes < {nbytes} needed")
+    base = _decode_key(q, k_pool, v_pool, block_tables, context_lens, out, block_size, scale)
+
+    def sized(dynamic):
+        key = (base, dynamic)
+        plan = _plans.get(key)
+        if plan is None:
+            _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+            if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
+                    out.stride(1) != q.shape[2] or out.device != q.device:
+                raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
+            sh = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0), dynamic)
+            plan = (sh, _size_of(sh))
+            if len(_plans) > 512:
+                _plans.clear()
+            _plans[key] = plan
+        return plan
+
+    dev = _dev_index(q)
+    s, ws = _ws_and_shape(None, dev, ws, sized)
     check(_lib.load().ir_paged_decode(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
@@ -380,8 +427,8 @@ def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor
         raise ValueError("slot_mapping must be contiguous int64 [B]")
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
-    ws = _ws(s, dev, ws)
+    s, ws = _ws_and_shape(lambda dyn: _shape(q, k_pool, block_tables, block_size, scale,
+                                             out.stride(0), dyn), dev, ws)
     check(_lib.load().ir_paged_decode_write(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
@@ -429,8 +476,8 @@ def paged_decode_rope_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
         raise ValueError("slot_mapping must be contiguous int64 [B]")
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    s = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0))
-    ws = _ws(s, dev, ws)
+    s, ws = _ws_and_shape(lambda dyn: _shape(q, k_pool, block_tables, block_size, scale,
+                                             out.stride(0), dyn), dev, ws)
     check(_lib.load().ir_paged_decode_rope_write(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
@@ -456,8 +503,8 @@ def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor
     if not (o.is_contiguous() and lse.is_contiguous() and o.dtype == torch.float32
             and lse.dtype == torch.float32):
         raise ValueError("o and lse must be contiguous fp32")
-    s = _shape(q, k_pool, block_tables, block_size, scale, h * d)
-    ws = _ws(s, dev, ws)
+    s, ws = _ws_and_shape(lambda dyn: _shape(q, k_pool, block_tables, block_size, scale,
+                                             h * d, dyn), dev, ws)
     check(_lib.load().ir_paged_decode_lse(
         o.data_ptr(), lse.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),
