@@ -71,10 +71,17 @@ def parse_args():
     p.add_argument("--sets", type=int, default=3)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--only", default="",
+                   help="--config kernels: run one case (cache_write_c3, cache_write_bulk, "
+                        "lse_merge_c4, lse_merge_b256, peer_exchange_world1_b256)")
+    p.add_argument("--inline-merge", action="store_true",
+                   help="merge rows of <= 4 pieces in the decode kernel (zeroed workspace)")
     p.add_argument("--dynamic-tail", action="store_true",
                    help="decode with static shares + dynamic tail units")
     p.add_argument("--engine", action="store_true",
                    help="c5 through infrared's own PagedBatchEngine (CUDA graphs, shim)")
+    p.add_argument("--no-engine", action="store_true",
+                   help="leave out the C5 leg through infrared's engine (default config)")
     p.add_argument("--no-kv-chunk", action="store_true",
                    help="leave out the C4 KV-chunk leg of the default config")
     p.add_argument("--soak", type=float, default=1.5,
@@ -343,10 +350,12 @@ def run_ours(args):
     sets = [wl.torch_values(w, 1000 * rank + s, dev) for s in range(args.sets)]
     out = torch.empty_like(sets[0][0])
     dynamic = args.dynamic_tail
+    inline = args.inline_merge
     _, _, ws_bytes = ops.decode_plan(sets[0][0], sets[0][1], bt, w.block_size, w.scale,
-                                     dynamic=dynamic)
-    # a zeroed, marked workspace lets the decode hand out its tail dynamically
-    ws = ops.decode_workspace(ws_bytes, dev, dynamic=dynamic)
+                                     dynamic=dynamic, inline_merge=inline)
+    # a zeroed, marked workspace: short rows merged in the decode kernel and,
+    # if asked for, the tail handed out dynamically
+    ws = ops.decode_workspace(ws_bytes, dev, dynamic=dynamic, inline_merge=inline)
     nbytes = w.algorithmic_bytes(with_write=fused)
 
     def step(i):
@@ -505,8 +514,10 @@ def run_ours(args):
             "timing": "K steps in one CUDA graph, CUDA events, max over ranks",
             "kernel_path": {1: "cuda-core", 2: "tma+mma.sync"}[path] +
                            (" (copy per head)" if args.decode_path == 3 else ""),
-            "schedule": "static shares + dynamic tail units" if dynamic and path == 2
-                        else "static shares",
+            "schedule": ("static shares + dynamic tail units" if dynamic and path == 2
+                         else "static shares") +
+                        (", rows of <= 4 pieces merged in the decode kernel"
+                         if inline and path == 2 else ", split rows merged by the merge kernel"),
             "ctas_per_kv_head": ctas,
         },
         "decode_tok_s_per_layer": round(world * w.batch / (per_step_ms / 1e3), 1),
@@ -534,6 +545,8 @@ def run_ours(args):
     del graph
     if args.config == "c2" and not args.no_kv_chunk:
         line["kv_chunk"] = kv_chunk_leg(args, dev, world, rank)
+    if args.config == "c2" and not args.no_engine:
+        line["c5_engine"] = c5_engine_summary(dev, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_leg(w, args.config, 10 ** 6, 1, args.cpu_seconds)
     if world > 1:
@@ -1047,6 +1060,161 @@ def build_infrared_qwen7b(dev, dtype, seed=0, std=0.02):
     return model.eval(), cfg
 
 
+def engine_leg(steps, warmup, dev, world, rank, local, global_batch=128,
+               timeout_s=600.0):
+    """Decode through infrared's own ``PagedBatchEngine`` (see
+    :func:`run_model_engine`) on this rank's share of ``global_batch``
+    requests; every rank takes part in the final reductions whatever happened
+    in its own run (a failure is reported, never left to hang the others).
+    Returns the job's figures (max time, summed tokens over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import model_step as ms
+    from infrared_b200 import shim
+
+    res = {"error": None, "ok": False, "secs": float("nan"), "tokens": 0, "graph_ms": [],
+           "prefill_s": float("nan"), "total_s": float("nan"), "steps_logged": 0,
+           "clocks": None, "b": 0, "t_max": 0, "w_bytes": 0, "kv_bytes": 0}
+    warm = max(warmup, 3)
+    model = engine = handle = None
+    try:
+        from infrared.engine.paged_engine import PagedBatchEngine
+        from infrared.engine.static_batch import BatchRequest
+
+        ctx_all = ms.random_context_lens(global_batch, 1024, 2048, seed=0)
+        lo, hi = irdist.shard_sequences(ctx_all, world)[rank]
+        ctx = [int(c) for c in ctx_all[lo:hi]]
+        b = len(ctx)
+        max_new = warm + steps + 1          # the first token comes from the prefill
+        model, cfg = build_infrared_qwen7b(dev, torch.bfloat16, seed=rank)
+        handle = shim.install(graph_inputs=True, fuse_rope=True, prefill=True)
+        t_max = -(-(max(ctx) + max_new + 1) // 16) * 16
+        engine = PagedBatchEngine(model, max_num_seqs=b, block_size=16,
+                                  num_blocks=b * (t_max // 16) + 16,
+                                  enable_prefix_caching=False, enable_cuda_graph=True,
+                                  graph_max_seq_len=t_max)
+        steps_log = []
+        orig_step = engine._decode_step
+
+        def timed_decode_step():
+            n = len(engine.scheduler.running)
+            t0 = time.perf_counter()
+            orig_step()
+            steps_log.append((t0, time.perf_counter(), n))
+
+        engine._decode_step = timed_decode_step
+        orig_run = engine._run
+
+        def run_on_device():          # the engine's worker thread on this rank's GPU
+            torch.cuda.set_device(dev)
+            orig_run()
+
+        engine._run = run_on_device
+        # device time of each graph decode (input build + replay), CUDA events
+        graph_events = []
+        orig_decoder = engine._cuda_graph_decoder
+
+        def timed_decoder():
+            dec = orig_decoder()
+            if not getattr(dec, "_irb_timed", False):
+                orig_decode = dec.decode
+
+                def decode(*a, **k):
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    out = orig_decode(*a, **k)
+                    e1.record()
+                    graph_events.append((e0, e1))
+                    return out
+
+                dec.decode = decode
+                dec._irb_timed = True
+            return dec
+
+        engine._cuda_graph_decoder = timed_decoder
+        rng = np.random.default_rng(100 + rank)
+        pends = [engine.submit(BatchRequest(
+            [int(x) for x in rng.integers(0, cfg.vocab_size, c)], max_new_tokens=max_new,
+            eos_token_ids=())) for c in ctx]
+        clocks = ClockSampler(local)
+        t_start = time.perf_counter()
+        engine.start()
+        error = None
+        try:
+            for pd in pends:
+                pd.result(timeout=timeout_s)
+        except Exception as exc:  # noqa: BLE001 - reported in the line
+            error = repr(exc)[:300]
+        finally:
+            engine.stop()
+            handle.uninstall()
+        t_total = time.perf_counter() - t_start
+        clk = clocks.stop()
+        torch.cuda.synchronize(dev)
+        graph_ms = [e0.elapsed_time(e1) for e0, e1 in graph_events[warm:warm + steps]]
+        timed = steps_log[warm:warm + steps]
+        ok = error is None and len(timed) == steps and all(n == b for _, _, n in timed)
+        secs = (timed[-1][1] - timed[0][0]) if ok else float("nan")
+        tokens = sum(n for _, _, n in timed)
+        prefill_s = (steps_log[0][0] - t_start) if steps_log else float("nan")
+        kv_tokens = sum(ctx) + b * (warm + steps // 2)
+        res.update(ok=ok, secs=secs, tokens=tokens, graph_ms=graph_ms, prefill_s=prefill_s,
+                   total_s=t_total, steps_logged=len(steps_log), clocks=clk, b=b,
+                   t_max=t_max, error=error,
+                   w_bytes=sum(p.numel() * p.element_size() for p in model.parameters()),
+                   kv_bytes=kv_tokens * 2 * cfg.num_key_value_heads * cfg.head_dim * 2 *
+                   cfg.num_hidden_layers)
+    except Exception as exc:  # noqa: BLE001 - reported, and the reductions still run
+        res["error"] = repr(exc)[:300]
+        res["ok"] = False
+    finally:
+        if handle is not None:
+            handle.uninstall()   # idempotent: restores infrared's functions
+        del engine, model
+        torch.cuda.empty_cache()
+    if world > 1:
+        t = torch.tensor([res["secs"] if res["ok"] else -1.0, float(res["tokens"]),
+                          float(res["ok"])], dtype=torch.float64, device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        mn = t.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        sm = t.clone()
+        dist.all_reduce(sm)
+        res["ok"] = bool(mn[2].item())
+        res["secs"], res["tokens"] = float(mx[0].item()), int(sm[1].item())
+    res["warm"] = warm
+    return res
+
+
+def c5_engine_summary(dev, world, rank, local, steps=20, warmup=3):
+    """The ``c5_engine`` object of the default line: C5 decoded through
+    infrared's own PagedBatchEngine at this job's N GPUs (128 requests
+    sharded over the ranks; see :func:`run_model_engine`)."""
+    if not infrared_importable():
+        return {"unavailable": "infrared is not installed in baseline/_ref "
+                               "(python -m oracle.reference_install)"}
+    r = engine_leg(steps, warmup, dev, world, rank, local, global_batch=128, timeout_s=300.0)
+    ok = r["ok"]
+    return {
+        "workload": "C5: random-init Qwen2.5-7B in infrared's Qwen2ForCausalLM served by "
+                    "infrared's PagedBatchEngine (CUDA-graph decode, shim installed), 128 "
+                    "requests with prompts U[1024,2048], sharded over the GPUs",
+        "metric": "decode tok/s", "n_gpus": world, "global_batch": 128, "steps": steps,
+        "scaling": "strong (fixed 128 sequences; every GPU reads the full weights)",
+        "value": round(r["tokens"] / r["secs"], 1) if ok else None, "unit": "tok/s",
+        "ms_per_step": round(r["secs"] / steps * 1e3, 4) if ok else None,
+        "graph_decode_device_ms_per_step": round(statistics.mean(r["graph_ms"]), 4)
+        if r["graph_ms"] else None,
+        "prefill_s": round(r["prefill_s"], 2), "error": r["error"],
+        "timing": "wall time of the engine's own decode loop, max over ranks; the device "
+                  "part timed with CUDA events around each graph decode",
+    }
+
+
 def run_model_engine(args):
     """C5 through infrared's own engine: a random-init Qwen2.5-7B in infrared's
     ``Qwen2ForCausalLM``, served by infrared's ``PagedBatchEngine`` with
@@ -1080,103 +1248,16 @@ def run_model_engine(args):
         if world > 1:
             dist.destroy_process_group()
         return
-    from infrared.engine.paged_engine import PagedBatchEngine
-    from infrared.engine.static_batch import BatchRequest
-
+    r = engine_leg(args.steps, args.warmup, dev, world, rank, local,
+                   global_batch=args.batch or 128, timeout_s=1800.0)
+    ok, secs, tokens, warm, b = r["ok"], r["secs"], r["tokens"], r["warm"], r["b"]
     global_batch = args.batch or 128
-    ctx_all = ms.random_context_lens(global_batch, 1024, 2048, seed=0)
-    lo, hi = irdist.shard_sequences(ctx_all, world)[rank]
-    ctx = [int(c) for c in ctx_all[lo:hi]]
-    b = len(ctx)
-    warm = max(args.warmup, 3)
-    max_new = warm + args.steps + 1          # the first token comes from the prefill
-    model, cfg = build_infrared_qwen7b(dev, torch.bfloat16, seed=rank)
-    handle = shim.install(graph_inputs=True, fuse_rope=True, prefill=True)
-    t_max = -(-(max(ctx) + max_new + 1) // 16) * 16
-    engine = PagedBatchEngine(model, max_num_seqs=b, block_size=16,
-                              num_blocks=b * (t_max // 16) + 16, enable_prefix_caching=False,
-                              enable_cuda_graph=True, graph_max_seq_len=t_max)
-    steps_log = []
-    orig_step = engine._decode_step
-
-    def timed_decode_step():
-        n = len(engine.scheduler.running)
-        t0 = time.perf_counter()
-        orig_step()
-        steps_log.append((t0, time.perf_counter(), n))
-
-    engine._decode_step = timed_decode_step
-    orig_run = engine._run
-
-    def run_on_device():          # the engine's worker thread on this rank's GPU
-        torch.cuda.set_device(dev)
-        orig_run()
-
-    engine._run = run_on_device
-    # device time of each graph decode (input build + replay), CUDA events
-    graph_events = []
-    orig_decoder = engine._cuda_graph_decoder
-
-    def timed_decoder():
-        dec = orig_decoder()
-        if not getattr(dec, "_irb_timed", False):
-            orig_decode = dec.decode
-
-            def decode(*a, **k):
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record()
-                out = orig_decode(*a, **k)
-                e1.record()
-                graph_events.append((e0, e1))
-                return out
-
-            dec.decode = decode
-            dec._irb_timed = True
-        return dec
-
-    engine._cuda_graph_decoder = timed_decoder
-    rng = np.random.default_rng(100 + rank)
-    pends = [engine.submit(BatchRequest([int(x) for x in rng.integers(0, cfg.vocab_size, c)],
-                                        max_new_tokens=max_new, eos_token_ids=()))
-             for c in ctx]
-    clocks = ClockSampler(local)
-    t_start = time.perf_counter()
-    engine.start()
-    error = None
-    try:
-        for pd in pends:
-            pd.result(timeout=1800)
-    except Exception as exc:  # noqa: BLE001 - reported in the line
-        error = repr(exc)[:300]
-    finally:
-        engine.stop()
-        handle.uninstall()
-    t_total = time.perf_counter() - t_start
-    clk = clocks.stop()
-    torch.cuda.synchronize(dev)
-    graph_ms = [e0.elapsed_time(e1) for e0, e1 in graph_events[warm:warm + args.steps]]
-    timed = steps_log[warm:warm + args.steps]
-    ok = error is None and len(timed) == args.steps and all(n == b for _, _, n in timed)
-    secs = (timed[-1][1] - timed[0][0]) if ok else float("nan")
-    tokens = sum(n for _, _, n in timed)
-    prefill_s = (steps_log[0][0] - t_start) if steps_log else float("nan")
-    if world > 1:
-        t = torch.tensor([secs if ok else -1.0, float(tokens), float(ok)], dtype=torch.float64,
-                         device=dev)
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        mn = t.clone()
-        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
-        sm = t.clone()
-        dist.all_reduce(sm)
-        ok = bool(mn[2].item())
-        secs, tokens = float(mx[0].item()), int(sm[1].item())
+    error, prefill_s, t_total, clk = r["error"], r["prefill_s"], r["total_s"], r["clocks"]
+    graph_ms, t_max = r["graph_ms"], r["t_max"]
+    steps_log = [None] * r["steps_logged"]
     per_step_ms = secs / args.steps * 1e3 if ok else None
     tok_s = tokens / secs if ok else None
-    kv_tokens = sum(ctx) + b * (warm + args.steps // 2)
-    w_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
-    kv_bytes = kv_tokens * 2 * cfg.num_key_value_heads * cfg.head_dim * 2 * cfg.num_hidden_layers
+    w_bytes, kv_bytes = r["w_bytes"], r["kv_bytes"]
     peak, peak_kind = measured_peaks()
     step_gbs = (w_bytes + kv_bytes) / (per_step_ms / 1e3) / 1e9 if ok else None
     line = {
@@ -1217,9 +1298,8 @@ def run_model_engine(args):
                 "note": "the engine loop is end to end: host block tables in, sampled ids "
                         "out, every step"},
         "clocks": clk,
-        "gpu_launches": (2 * cfg.num_hidden_layers + 2) * args.steps,
+        "gpu_launches": (2 * 28 + 2) * args.steps,
     }
-    del engine, model
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1253,6 +1333,8 @@ def run_kernels(args):
     res = {}
 
     def timed(name, fn, nbytes, steps):
+        if args.only and name != args.only:
+            return
         ms = _graph_ms(lambda i: fn(i), steps, dev, 1) / steps
         res[name] = {"us_per_launch": round(ms * 1e3, 3), "bytes": nbytes,
                      "GB_s": round(nbytes / (ms / 1e3) / 1e9, 1)}
@@ -1303,8 +1385,9 @@ def run_kernels(args):
     ops.check_device_errors(dev)
     _lib.check(lib.ir_peer_free(buf))
     peak, peak_kind = measured_peaks()
+    first = res.get("cache_write_bulk") or next(iter(res.values()))
     line = {"metric": "standalone kernel GB/s (algorithmic bytes / launch time)",
-            "value": res["cache_write_bulk"]["GB_s"], "unit": "GB/s", "n_gpus": 1,
+            "value": first["GB_s"], "unit": "GB/s", "n_gpus": 1,
             "steps": args.steps, "warmup": 3, "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic", "kernels": res, "peak": peak, "peak_kind": peak_kind,
             "config": {"workload": "cache write (C3 256 tokens; 65536 tokens), lse merge "

@@ -147,11 +147,12 @@ typedef struct ir_decode_shape {
   int64_t num_slots;  /* rows of the pool (num_blocks * block_size) */
   float scale;        /* softmax scale, usually head_dim ** -0.5 */
   int dtype;          /* IR_DTYPE_* of q, pools and out */
-  int flags;          /* 0 or IR_DECODE_DYNAMIC_TAIL; other bits are rejected */
+  int flags;          /* IR_DECODE_DYNAMIC_TAIL | IR_DECODE_INLINE_MERGE or 0;
+                         other bits are rejected */
 } ir_decode_shape;
 
-/* ir_decode_shape.flags: the workspace's first IR_DECODE_HEADER_BYTES were
- * zero when it was first used (cudaMemset once after allocating it). The TMA
+/* ir_decode_shape.flags: the workspace was zero-filled when it was first
+ * used (cudaMemset once after allocating it). The TMA
  * kernel then hands out the last ~15 % of the tiles as small units that CTAs
  * claim from counters in that header as they finish their static share, which
  * evens out the SMs' random differences in streaming speed; every call leaves
@@ -160,7 +161,16 @@ typedef struct ir_decode_shape {
  * workspace size (more partial slots); results are deterministic either way
  * (they do not depend on which CTA took which unit). */
 #define IR_DECODE_DYNAMIC_TAIL 1
-#define IR_DECODE_HEADER_BYTES 256
+/* ir_decode_shape.flags: the workspace was zero-filled when it was first
+ * used. The TMA kernel then merges a sequence split into at most 4 pieces
+ * inside the decode kernel: the warp that writes the row's last piece folds
+ * the pieces (counted in the workspace header, which every call leaves zero
+ * again) while the other CTAs are still streaming, instead of the separate
+ * merge kernel doing it after the decode has finished (num_kv_heads * batch
+ * up to 16384; larger shapes leave every row to the merge kernel). The
+ * header sits at the start of the workspace in every layout, so one zeroed
+ * workspace may serve calls of any shape and flags. */
+#define IR_DECODE_INLINE_MERGE 2
 
 /* Bytes of workspace the decode calls need for this shape on the current
  * device (0 on an invalid shape). The workspace holds the tile prefix and the

@@ -21,7 +21,8 @@ LIB_PATH = Path(os.environ.get("INFRARED_B200_LIB") or
 
 IR_DTYPE_F32, IR_DTYPE_BF16, IR_DTYPE_F16 = 0, 1, 2
 IR_OK, IR_ERR_INVALID_ARG, IR_ERR_UNSUPPORTED, IR_ERR_CUDA, IR_ERR_WORKSPACE = range(5)
-IR_DECODE_DYNAMIC_TAIL = 1   # ir_decode_shape.flags: workspace header zeroed
+IR_DECODE_DYNAMIC_TAIL = 1   # ir_decode_shape.flags (the workspace zero-filled)
+IR_DECODE_INLINE_MERGE = 2
 IR_NOALLOC_WORKSPACE_BYTES = 8 << 20
 
 DEVERR_BITS = {

@@ -180,12 +180,19 @@ struct Plan {
   int path;     // 1 generic, 2 tma
   int G;        // CTAs per kv head
   int dyn;      // dynamic tail units (TMA path, flag set)
+  int inl;      // short rows merged in the decode kernel (TMA path, flag set)
   int64_t slots;  // partial slots per kv head
-  size_t ctr_off, prefix_off, lse_off, o_off, bytes;
+  size_t ctr_off, seq_off, prefix_off, lse_off, o_off, bytes;
 };
 
-// Workspace header: the dynamic tail's counter pair of each kv-head group.
+// Workspace header, at the same place in every layout (with or without the
+// flags, whatever the shape) so that no call ever writes anything else there
+// and the counters stay zero between calls: the counter pair {claims, CTAs
+// done} of each kv-head group, then one piece counter per (kv head,
+// sequence), for at most kMaxSeqCounters rows.
 constexpr size_t kCtrBytes = 256;
+constexpr int64_t kMaxSeqCounters = 16384;
+constexpr size_t kHeaderBytes = kCtrBytes + kMaxSeqCounters * 4;
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -213,9 +220,9 @@ int check_shape(const ir_decode_shape* s) {
   if (elem_bytes(s->dtype) == 0) return fail(IR_ERR_INVALID_ARG, "bad dtype");
   if (static_cast<int64_t>(s->max_blocks) * s->block_size > INT32_MAX)
     return fail(IR_ERR_UNSUPPORTED, "max_blocks * block_size overflows int32");
-  if (s->flags & ~IR_DECODE_DYNAMIC_TAIL)
-    return fail(IR_ERR_INVALID_ARG, "unknown bits in flags (set it to 0 or "
-                                    "IR_DECODE_DYNAMIC_TAIL)");
+  if (s->flags & ~(IR_DECODE_DYNAMIC_TAIL | IR_DECODE_INLINE_MERGE))
+    return fail(IR_ERR_INVALID_ARG, "unknown bits in flags (set it to 0 or a combination "
+                                    "of IR_DECODE_DYNAMIC_TAIL and IR_DECODE_INLINE_MERGE)");
   return IR_OK;
 }
 
@@ -242,13 +249,16 @@ int make_plan(const ir_decode_shape* s, Plan* p) {
   p->G = G;
   const int64_t B = s->batch, H = s->num_heads, D = s->head_dim;
   const int groups = path == 2 ? s->num_kv_heads / irb::tma_head_group(s->num_kv_heads) : 0;
-  p->dyn = (s->flags & IR_DECODE_DYNAMIC_TAIL) && path == 2 &&
-           static_cast<size_t>(groups) * 8 <= kCtrBytes;
+  const bool hdr = path == 2 && static_cast<size_t>(groups) * 8 <= kCtrBytes;
+  p->dyn = (s->flags & IR_DECODE_DYNAMIC_TAIL) && hdr;
+  p->inl = (s->flags & IR_DECODE_INLINE_MERGE) && hdr &&
+           static_cast<int64_t>(s->num_kv_heads) * B <= kMaxSeqCounters;
   p->slots = G + (p->dyn ? static_cast<int64_t>(irb::kDynUnitsPerCta) * G : 0) + B;
   const int64_t slots = static_cast<int64_t>(s->num_kv_heads) * p->slots *
                         (H / s->num_kv_heads);
   p->ctr_off = 0;
-  p->prefix_off = kCtrBytes;
+  p->seq_off = kCtrBytes;
+  p->prefix_off = kHeaderBytes;
   p->lse_off = p->prefix_off + align256(static_cast<size_t>(B + 1) * 8);
   p->o_off = p->lse_off + align256(static_cast<size_t>(slots) * 4);
   p->bytes = p->o_off + align256(static_cast<size_t>(slots * D) * 4);
@@ -291,6 +301,11 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
     // TMA descriptors need 16-byte aligned pools; q fragments are read as
     // 32-bit words; the fused write moves 16-byte vectors.
     bool ok = aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(q, 4);
+    // finished rows leave in 16-byte stores (fp32 rows in LSE mode)
+    if (mode == Mode::kLse)
+      ok = ok && aligned(lse_o, 16);
+    else
+      ok = ok && aligned(out, 16) && (s->out_stride * eb) % 16 == 0;
     if (mode == Mode::kWrite)
       ok = ok && aligned(k_new, 16) && aligned(v_new, 16) &&
            (kv_stride * eb) % 16 == 0;
@@ -328,8 +343,11 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
   a.scale_log2 = s->scale * irb::kLog2e;
   a.G = plan.G;
   a.dyn = plan.dyn && plan.path == 2 ? 1 : 0;
+  a.inline_merge = plan.inl && plan.path == 2 ? 1 : 0;
+  a.zeroed = a.dyn || a.inline_merge;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   a.ws_ctr = reinterpret_cast<uint32_t*>(ws + plan.ctr_off);
+  a.ws_seq = reinterpret_cast<uint32_t*>(ws + plan.seq_off);
   a.ws_prefix = reinterpret_cast<int64_t*>(ws + plan.prefix_off);
   a.ws_slots = plan.slots;
   a.ws_lse = reinterpret_cast<float*>(ws + plan.lse_off);

@@ -53,8 +53,11 @@ struct DecodeArgs {
   float scale_log2;  // scale * log2(e)
   int G;             // CTAs per kv head
   int dyn;           // 1: dynamic tail units (ws_ctr zero at the start of the call)
+  int inline_merge;  // 1: short rows merged in the decode kernel (ws_seq zero at the start)
+  int zeroed;        // dyn || inline_merge: the header counters are in use
   // workspace
   uint32_t* ws_ctr;    // [kv-head groups][2] {claims, CTAs done} of the dynamic tail
+  uint32_t* ws_seq;    // [Hkv, B] pieces of a (kv head, sequence) row written so far
   int64_t* ws_prefix;  // [B + 1] tile prefix (written by the first CTA of kv head 0)
   int64_t ws_slots;    // partial slots per kv head: G (+ kDynUnitsPerCta * G) + B
   float* ws_lse;       // [Hkv, ws_slots, n_rep] log2-sum-exp of partials
@@ -108,6 +111,10 @@ constexpr int kDynUnitTiles = 4;
 constexpr int kDynUnitsPerCta = 2;
 constexpr int kDynMinTilesPerCta = 8;
 constexpr int kDynSeqs = 32;
+// In-kernel merge (DecodeArgs::inline_merge): a row split into at most this
+// many pieces is merged by the warp that writes its last piece; longer rows
+// are left to the merge kernel.
+constexpr int kInlineMax = 4;
 
 struct UnitPlan {
   int64_t F;    // static tiles [0, F), cut into Gs equal shares

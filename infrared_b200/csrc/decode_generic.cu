@@ -207,6 +207,7 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
   const int glo = unit_of(up, pb);
   const int parts = unit_of(up, pb + nb - 1) - glo + 1;
   if (parts == 1) return;  // written whole by one unit
+  if (a.inline_merge && parts <= kInlineMax) return;  // merged in the decode kernel
   const int64_t base = static_cast<int64_t>(kvh) * a.ws_slots + glo + b;
   const float* lse = a.ws_lse + base * a.n_rep + n;       // stride n_rep per piece
   const float* o = a.ws_o + (base * a.n_rep + n) * a.D;   // stride n_rep * D per piece

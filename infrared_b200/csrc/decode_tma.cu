@@ -30,8 +30,16 @@
 // streams its static unit, then claims dynamic units from the workspace
 // counter until none is left; a unit start is a segment start, and the unit
 // index travels to the consumers in the item descriptor (pieces sit in slot
-// unit + b). The producer counts its CTA done after its last claim; the last
-// CTA of the kv-head group sets the counters back to zero.
+// unit + b). Every CTA counts itself done at its end; the last CTA of the
+// kv-head group sets the counters back to zero.
+//
+// With the in-kernel merge (DecodeArgs::inline_merge) a warp that writes a
+// piece of a row split into at most kInlineMax pieces counts it in the row's
+// counter (ws_seq); the warp that writes the last one merges the row's
+// pieces in unit order right away, while the other CTAs are still
+// streaming, and sets the counter back to zero; the merge kernel then skips
+// those rows. The producer packs the row's piece count and this piece's
+// index into the item descriptor.
 #include "decode_common.cuh"
 #include "kernels.h"
 
@@ -52,6 +60,9 @@ constexpr int kFlagSeqEnd = 1 << 9;    // last tile of the sequence
 constexpr int kFlagWhole = 1 << 10;    // the segment is the whole sequence
 constexpr int kFlagEnd = 1 << 11;      // end-of-stream marker
 constexpr int kFlagSegStart = 1 << 12; // first tile of a segment
+// bits 13-15: pieces of the segment's row (0 = more than 7); bits 16-18: the
+// segment's index among them (segment-start items)
+constexpr int kPartsShift = 13, kPieceShift = 16;
 
 // R = rows per TMA box: 16, or 8 for 8-token blocks (two boxes per tile).
 template <int D, int HG, int NS, int R>
@@ -135,12 +146,15 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   launch_dependents();
   const int64_t start = ri->start, end = ri->end;
   const UnitPlan up = ri->plan;
-  if (start >= end && up.U == 0) return;  // no static share and no units to claim
+  // a CTA with no static share and no units to claim only counts itself done
+  const bool idle = start >= end && up.U == 0;
+  uint32_t* ctr = a.zeroed ? a.ws_ctr + 2 * hg : nullptr;
 
-  if (warp == 0) {
+  if (idle) {
+    // nothing to stream
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     const bool dyn = up.U > 0;
-    uint32_t* ctr = dyn ? a.ws_ctr + 2 * hg : nullptr;
     const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
     int64_t ustart = start, uend = end;  // the static unit first, then claimed ones
     int unit = g;
@@ -231,6 +245,13 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
           const bool whole = (lp >= ustart) && (lp + ln <= uend);
           packed = nvalid | (ok ? kFlagValid : 0) | (j == ln - 1 ? kFlagSeqEnd : 0) |
                    (whole ? kFlagWhole : 0) | (seg_start ? kFlagSegStart : 0);
+          if (seg_start && !whole && a.inline_merge) {
+            const int u_first = unit_of(up, lp);
+            const int parts = unit_of(up, lp + ln - 1) - u_first + 1;
+            const int pidx = unit - u_first;
+            packed |= ((parts <= 7 ? parts : 0) << kPartsShift) |
+                      ((pidx < 7 ? pidx : 7) << kPieceShift);
+          }
         }
         const unsigned starts = __ballot_sync(kFull, active && seg_start);
         const unsigned le_mask = (lane == 31) ? kFull : ((2u << lane) - 1u);
@@ -340,20 +361,7 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
         }
       }
     }
-    if (dyn && lane == 0) {
-      // after this CTA's last claim: count it done; the last CTA of the group
-      // leaves the counters at zero for the next call (every exit path of the
-      // producer, aborted ones included, comes through here)
-      __threadfence();
-      const uint32_t old = atomicAdd(ctr + 1, 1u);
-      if (old == gridDim.y - 1) {
-        atomicExch(ctr, 0u);
-        atomicExch(ctr + 1, 0u);
-      }
-    }
-    return;
-  }
-
+  } else {
   // -------------------------------------------------------------- consumers
   const int head = warp - 1;  // 0..HG-1
   const int kvh = kv0 + head;
@@ -381,10 +389,75 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
   }
   m[0] = m[1] = -INFINITY;
   l[0] = l[1] = 0.f;
-  int seg_b = -1, seg_unit = 0;
+  int seg_b = -1, seg_unit = 0, seg_parts = 0, seg_pidx = 0;
   bool seg_whole = false, have_seg = false;
 
   float* fbuf = reinterpret_cast<float*>(smem + L::off_flush) + head * L::kFlushFloats;
+
+  // This warp has just written piece seg_pidx of the row set (kvh, seg_b),
+  // which has seg_parts pieces in units seg_unit - seg_pidx, ...: count it;
+  // the warp that writes the last one folds the pieces in unit order (as the
+  // merge kernel does), writes the final rows and sets the counter back.
+  auto merge_inline = [&]() {
+    uint32_t* cnt = a.ws_seq + static_cast<int64_t>(kvh) * a.B + seg_b;
+    __threadfence();  // every lane's part of this piece is visible before it is counted
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(cnt, 1u);
+    old = __shfl_sync(kFull, old, 0);
+    if (old != static_cast<uint32_t>(seg_parts - 1)) return;
+    __threadfence();  // the other pieces' writes happened before their counts
+    const int nr = a.n_rep;
+    const int64_t base = static_cast<int64_t>(kvh) * a.ws_slots + (seg_unit - seg_pidx) + seg_b;
+    const bool act = lane * 4 < D;
+    for (int n = 0; n < nr; ++n) {
+      float li[kInlineMax];
+      float4 oi[kInlineMax];
+#pragma unroll
+      for (int i = 0; i < kInlineMax; ++i) {  // independent loads, one round trip
+        li[i] = -INFINITY;
+        oi[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < seg_parts) {
+          const int64_t sl = base + i;
+          li[i] = __ldcg(a.ws_lse + sl * nr + n);
+          if (act) oi[i] = __ldcg(reinterpret_cast<const float4*>(a.ws_o + (sl * nr + n) * D) + lane);
+        }
+      }
+      float M = -INFINITY, S = 0.f;
+      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < kInlineMax; ++i) {
+        if (li[i] == -INFINITY) continue;
+        const float Mn = fmaxf(M, li[i]);
+        const float c = ex2(M - Mn), w = ex2(li[i] - Mn);
+        S = S * c + w;
+        r.x = r.x * c + w * oi[i].x;
+        r.y = r.y * c + w * oi[i].y;
+        r.z = r.z * c + w * oi[i].z;
+        r.w = r.w * c + w * oi[i].w;
+        M = Mn;
+      }
+      const bool empty_row = S == 0.f;
+      const float inv = empty_row ? 0.f : 1.f / S;
+      const int h = kvh * nr + n;
+      if (a.lse_mode) {
+        if (act)
+          reinterpret_cast<float4*>(a.lse_o + (static_cast<int64_t>(seg_b) * a.H + h) * D)[lane] =
+              make_float4(r.x * inv, r.y * inv, r.z * inv, r.w * inv);
+        if (lane == 0)
+          a.lse_out[static_cast<int64_t>(seg_b) * a.H + h] =
+              empty_row ? -INFINITY : (M + log2f(S)) * kLn2;
+      } else if (act) {
+        T* dst = reinterpret_cast<T*>(a.out) + seg_b * a.out_stride + static_cast<int64_t>(h) * D;
+        uint2 v;
+        v.x = pack2<T>(r.x * inv, r.y * inv);
+        v.y = pack2<T>(r.z * inv, r.w * inv);
+        reinterpret_cast<uint2*>(dst)[lane] = v;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) atomicExch(cnt, 0u);
+  };
 
   // Write this warp's finished segment: the final row or a workspace piece.
   // The normalised fragments go through shared memory so that the global
@@ -446,6 +519,8 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
             *reinterpret_cast<const float4*>(fbuf + n * L::kFlushStride + d);
       }
       if (lane < nr) ldst[lane] = seg_whole ? lse2[lane] * kLn2 : lse2[lane];
+      if (!seg_whole && a.inline_merge && seg_parts >= 2 && seg_parts <= kInlineMax)
+        merge_inline();
     }
     __syncwarp();
 #pragma unroll
@@ -472,6 +547,8 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
       seg_b = b;
       seg_unit = dsc.seg >> 1;
       seg_whole = (pk & kFlagWhole) != 0;
+      seg_parts = (pk >> kPartsShift) & 7;
+      seg_pidx = (pk >> kPieceShift) & 7;
       // this segment's q as B fragments: from the staged rows, else global
       const T* qrow = tp.q_bulk
           ? reinterpret_cast<const T*>(smem + L::off_q + (dsc.seg & 1) * L::kQBuf) +
@@ -632,6 +709,31 @@ __global__ void __launch_bounds__(32 * (HG + 1), 1)
     if (wrote) fence_proxy_async_shared();
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  }  // consumers
+  // every warp of the CTA is done (pieces written and merged): count the CTA
+  // done; the last CTA of the kv-head group leaves the header counters at
+  // zero for the next call (every exit path, aborted ones included, comes
+  // through here)
+  if (ctr != nullptr) {
+    __syncthreads();
+    if (warp == 0) {
+      uint32_t old = 0;
+      if (lane == 0) {
+        __threadfence();
+        old = atomicAdd(ctr + 1, 1u);
+      }
+      old = __shfl_sync(kFull, old, 0);
+      if (old == gridDim.y - 1) {
+        __threadfence();
+        if (a.inline_merge)
+          for (int i = lane; i < HG * a.B; i += 32) a.ws_seq[static_cast<int64_t>(kv0) * a.B + i] = 0u;
+        if (lane == 0) {
+          atomicExch(ctr, 0u);
+          atomicExch(ctr + 1, 0u);
+        }
+      }
+    }
   }
 }
 

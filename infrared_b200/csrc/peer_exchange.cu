@@ -44,7 +44,7 @@ namespace {
 
 constexpr int kHeader = 4096;
 constexpr int kEpoch = 0, kDone = 64;
-constexpr int kWarps = 4;  // one row per warp
+constexpr int kWarps = 16;  // rows are spread over the warps of at most one CTA per SM
 constexpr int kThreads = 32 * kWarps;
 
 __device__ __forceinline__ void st_chunk(uint8_t* p, float x, float y, uint32_t flag) {

@@ -114,32 +114,44 @@ def _stream(device_index: int) -> int:
     return torch.cuda.current_stream(device_index).cuda_stream
 
 
-# The library's own (cached) workspaces ask for the dynamic tail only when
-# this is set: on B200 the static shares measured faster (see
-# decode_workspace); the dynamic schedule stays available for workspaces
-# made with decode_workspace(dynamic=True).
+# What a zeroed decode workspace turns on by default (ir_decode_shape.flags).
+# Both features are opt-in (decode_workspace(dynamic=..., inline_merge=...)):
+# on B200 the static shares with the separate merge kernel measured faster
+# on every benchmark shape.
 DYNAMIC_TAIL_DEFAULT = False
+INLINE_MERGE_DEFAULT = False
 
 
-def decode_workspace(nbytes: int, device, dynamic: bool = True) -> torch.Tensor:
-    """A decode workspace of ``nbytes`` (at least 1 MiB) on ``device`` with its
-    header zeroed. With ``dynamic`` it is marked so that the decode calls
-    given it hand out the last part of the work dynamically
-    (``IR_DECODE_DYNAMIC_TAIL``; the kernels leave the header zero after
-    every call); unmarked workspaces (and any other tensor) get the static
-    schedule, one fixed share per CTA."""
+def _default_flags(dynamic: bool | None = None, inline_merge: bool | None = None) -> int:
+    dyn = DYNAMIC_TAIL_DEFAULT if dynamic is None else dynamic
+    inl = INLINE_MERGE_DEFAULT if inline_merge is None else inline_merge
+    return (_lib.IR_DECODE_DYNAMIC_TAIL if dyn else 0) | \
+        (_lib.IR_DECODE_INLINE_MERGE if inl else 0)
+
+
+def decode_workspace(nbytes: int, device, dynamic: bool | None = None,
+                     inline_merge: bool | None = None) -> torch.Tensor:
+    """A decode workspace of ``nbytes`` (at least 1 MiB) on ``device``, zero
+    filled, marked with the features the decode calls given it may use:
+    ``dynamic`` (``IR_DECODE_DYNAMIC_TAIL``: the last part of the tiles handed
+    out as claimed units) and ``inline_merge`` (``IR_DECODE_INLINE_MERGE``:
+    rows of at most 4 pieces merged in the decode kernel); None takes the
+    module defaults. The kernels leave the header they count in zero after
+    every call. Any other tensor given as a workspace gets neither."""
     t = torch.zeros(max(int(nbytes), 1 << 20), dtype=torch.uint8,
                     device=torch.device("cuda", _index_of(device)))
     # allocated inside a graph capture the zeroing only runs at replay: such
-    # a workspace keeps the static schedule
-    t._irb_zeroed_header = dynamic and not torch.cuda.is_current_stream_capturing()
+    # a workspace uses neither feature
+    t._irb_flags = 0 if torch.cuda.is_current_stream_capturing() else \
+        _default_flags(dynamic, inline_merge)
     return t
 
 
-def _header_zeroed(ws: torch.Tensor | None) -> bool:
+def _flags_of(ws: torch.Tensor | None) -> int:
+    """Flags a call may ask for with this workspace (None: the cached one's)."""
     if ws is None:
-        return DYNAMIC_TAIL_DEFAULT
-    return bool(getattr(ws, "_irb_zeroed_header", False))
+        return _default_flags()
+    return int(getattr(ws, "_irb_flags", 0))
 
 
 def workspace(nbytes: int, device_index: int) -> torch.Tensor:
@@ -151,7 +163,7 @@ def workspace(nbytes: int, device_index: int) -> torch.Tensor:
     with _state_lock:
         t = _workspaces.get(device_index)
         if t is None or t.numel() < nbytes:
-            t = decode_workspace(nbytes, device_index, dynamic=DYNAMIC_TAIL_DEFAULT)
+            t = decode_workspace(nbytes, device_index)
             _workspaces[device_index] = t
     return t
 
@@ -259,7 +271,7 @@ def derive_block_metadata(gather_slots: torch.Tensor, mask: torch.Tensor, block_
 
 def _shape(q: torch.Tensor, k_pool: torch.Tensor, block_tables: torch.Tensor,
            block_size: int, scale: float, out_stride: int,
-           dynamic: bool = False) -> DecodeShape:
+           flags: int = 0) -> DecodeShape:
     b, h, d = q.shape
     hkv = k_pool.shape[1]
     s = DecodeShape()
@@ -275,7 +287,7 @@ def _shape(q: torch.Tensor, k_pool: torch.Tensor, block_tables: torch.Tensor,
     s.num_slots = k_pool.shape[0]
     s.scale = float(scale)
     s.dtype = dtype_code(q.dtype)
-    s.flags = _lib.IR_DECODE_DYNAMIC_TAIL if dynamic else 0
+    s.flags = flags
     return s
 
 
@@ -305,10 +317,13 @@ def _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens):
             raise ValueError("all tensors must be on the same device")
 
 
-def decode_plan(q, k_pool, block_tables, block_size, scale=1.0, dynamic=False):
+def decode_plan(q, k_pool, block_tables, block_size, scale=1.0, dynamic=False,
+                inline_merge=None):
     """``(path, ctas_per_kv_head, workspace_bytes)`` the library picks for this
-    call (``dynamic``: with a workspace from ``decode_workspace(dynamic=True)``)."""
-    s = _shape(q, k_pool, block_tables, block_size, scale, q.shape[1] * q.shape[2], dynamic)
+    call with a workspace from ``decode_workspace(dynamic=..., inline_merge=...)``
+    (None: the module default)."""
+    s = _shape(q, k_pool, block_tables, block_size, scale, q.shape[1] * q.shape[2],
+               _default_flags(dynamic, inline_merge))
     lib = _lib.load()
     path, g = _lib.c_int(), _lib.c_int()
     check(lib.ir_paged_decode_plan(s, path, g))
@@ -324,24 +339,25 @@ def _size_of(s: DecodeShape) -> int:
 
 
 def _ws_and_shape(make_shape, dev: int, ws: torch.Tensor | None, sized=None):
-    """``(shape, workspace)`` of a decode call. The dynamic tail is asked for
-    when the workspace's header is known to be zero: the caller's when it is
-    marked (:func:`decode_workspace`), the cached per-device one unless it was
-    allocated inside a graph capture. ``make_shape(dynamic)`` builds the
-    shape; ``sized(dynamic)`` may return a cached ``(shape, bytes)``."""
-    sized = sized or (lambda dyn: (make_shape(dyn), None))
+    """``(shape, workspace)`` of a decode call: the shape asks for the features
+    the workspace is marked with (:func:`decode_workspace`; the cached
+    per-device workspace has the module defaults unless it was allocated
+    inside a graph capture). ``make_shape(flags)`` builds the shape;
+    ``sized(flags)`` may return a cached ``(shape, bytes)``."""
+    sized = sized or (lambda fl: (make_shape(fl), None))
     if ws is not None:
-        dynamic = _header_zeroed(ws)
-        s, nbytes = sized(dynamic)
+        s, nbytes = sized(_flags_of(ws))
         nbytes = _size_of(s) if nbytes is None else nbytes
         if ws.numel() < nbytes:
             raise ValueError(f"workspace of {ws.numel()} bytes < {nbytes} needed")
         return s, ws
-    s, nbytes = sized(DYNAMIC_TAIL_DEFAULT)
+    want = _flags_of(None)
+    s, nbytes = sized(want)
     nbytes = _size_of(s) if nbytes is None else nbytes
     ws = workspace(nbytes, dev)
-    if DYNAMIC_TAIL_DEFAULT and not _header_zeroed(ws):   # static (needs fewer bytes)
-        s, _ = sized(False)
+    got = _flags_of(ws)
+    if got != want:   # fewer features need no more bytes
+        s, _ = sized(got)
     return s, ws
 
 
@@ -375,15 +391,15 @@ def paged_decode(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
     base = _decode_key(q, k_pool, v_pool, block_tables, context_lens, out, block_size, scale)
 
-    def sized(dynamic):
-        key = (base, dynamic)
+    def sized(flags):
+        key = (base, flags)
         plan = _plans.get(key)
         if plan is None:
             _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
             if out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1 or \
                     out.stride(1) != q.shape[2] or out.device != q.device:
                 raise ValueError("out must be [B, H, D] with [H, D] contiguous rows")
-            sh = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0), dynamic)
+            sh = _shape(q, k_pool, block_tables, block_size, scale, out.stride(0), flags)
             plan = (sh, _size_of(sh))
             if len(_plans) > 512:
                 _plans.clear()
@@ -427,8 +443,8 @@ def paged_decode_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor
         raise ValueError("slot_mapping must be contiguous int64 [B]")
     if out is None:
         out = torch.empty_like(q, memory_format=torch.contiguous_format)
-    s, ws = _ws_and_shape(lambda dyn: _shape(q, k_pool, block_tables, block_size, scale,
-                                             out.stride(0), dyn), dev, ws)
+    s, ws = _ws_and_shape(lambda fl: _shape(q, k_pool, block_tables, block_size, scale,
+                                            out.stride(0), fl), dev, ws)
     check(_lib.load().ir_paged_decode_write(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
@@ -476,8 +492,8 @@ def paged_decode_rope_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
         raise ValueError("slot_mapping must be contiguous int64 [B]")
     if out is None:
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    s, ws = _ws_and_shape(lambda dyn: _shape(q, k_pool, block_tables, block_size, scale,
-                                             out.stride(0), dyn), dev, ws)
+    s, ws = _ws_and_shape(lambda fl: _shape(q, k_pool, block_tables, block_size, scale,
+                                            out.stride(0), fl), dev, ws)
     check(_lib.load().ir_paged_decode_rope_write(
         out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) if b else hkv * d,
@@ -503,8 +519,8 @@ def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor
     if not (o.is_contiguous() and lse.is_contiguous() and o.dtype == torch.float32
             and lse.dtype == torch.float32):
         raise ValueError("o and lse must be contiguous fp32")
-    s, ws = _ws_and_shape(lambda dyn: _shape(q, k_pool, block_tables, block_size, scale,
-                                             h * d, dyn), dev, ws)
+    s, ws = _ws_and_shape(lambda fl: _shape(q, k_pool, block_tables, block_size, scale,
+                                            h * d, fl), dev, ws)
     check(_lib.load().ir_paged_decode_lse(
         o.data_ptr(), lse.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(),
         block_tables.data_ptr(), context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(),

@@ -61,7 +61,8 @@ def test_noalloc_matches_regular_decode_on_two_calls_in_a_row():
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
     # the built-in scratch serves the static schedule (no dynamic tail units)
-    _, ctas, need = ops.decode_plan(q1, kp, bt, w.block_size, w.scale)
+    _, ctas, need = ops.decode_plan(q1, kp, bt, w.block_size, w.scale,
+                                    inline_merge=False)
     assert 0 < need <= _lib.IR_NOALLOC_WORKSPACE_BYTES
     # more CTAs per kv-head group than sequences: sequences are cut into
     # pieces whose partials go through the scratch array to the merge kernel
