@@ -27,6 +27,11 @@ divided by the slowest rank's time.
   on two copy streams; kernels run in order).
 * ``roofline``: the decode call's bytes / its measured duration against the
   measured HBM copy bandwidth in MEASURED_PEAKS.json.
+* ``prefill_p1`` (default config): P1 (8 causal 4096-token prompts) on the
+  tcgen05 prefill kernel, TFLOP/s against the measured bf16 peak, per GPU.
+* ``c5_engine`` (default config): config C5 decoded through infrared's own
+  ``PagedBatchEngine`` (CUDA graphs, the shim installed), the 128 requests
+  sharded over the job's GPUs; tok/s from the engine's own loop.
 * ``kv_chunk`` (default config, every N): config C4 (4 x 32k contexts)
   with each sequence's KV split across the same N GPUs, partials exchanged
   by peer stores over NVLink in one kernel (``p2p``) and by an NCCL
@@ -80,6 +85,8 @@ def parse_args():
                    help="decode with static shares + dynamic tail units")
     p.add_argument("--engine", action="store_true",
                    help="c5 through infrared's own PagedBatchEngine (CUDA graphs, shim)")
+    p.add_argument("--no-prefill", action="store_true",
+                   help="leave out the P1 prefill leg of the default config")
     p.add_argument("--no-engine", action="store_true",
                    help="leave out the C5 leg through infrared's engine (default config)")
     p.add_argument("--no-kv-chunk", action="store_true",
@@ -545,6 +552,8 @@ def run_ours(args):
     del graph
     if args.config == "c2" and not args.no_kv_chunk:
         line["kv_chunk"] = kv_chunk_leg(args, dev, world, rank)
+    if args.config == "c2" and not args.no_prefill:
+        line["prefill_p1"] = p1_summary(dev, world, rank)
     if args.config == "c2" and not args.no_engine:
         line["c5_engine"] = c5_engine_summary(dev, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1394,6 +1403,61 @@ def run_kernels(args):
                                    "(8 parts x 4/256 x 28 rows), peer exchange world of one",
                        "timing": "K launches in one CUDA graph, CUDA events"}}
     print(json.dumps(line), flush=True)
+
+
+def p1_summary(dev, world, rank, steps=10, warmup=3):
+    """The ``prefill_p1`` object of the default line: P1 (8 causal 4096-token
+    prompts, Qwen2.5-7B attention geometry) on the tcgen05 prefill kernel,
+    launches timed back to back with CUDA events; TFLOP/s of useful (causal)
+    FLOPs against the measured bf16 peak; every rank runs its own prompts."""
+    import torch
+
+    from infrared_b200 import dist as irdist
+    from infrared_b200 import ops
+    from infrared_b200 import workloads as wl
+
+    w = wl.p1(seed=rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    slots = w.num_blocks * w.block_size
+
+    def randn(*shape):
+        return (torch.randn(*shape, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+
+    kp = randn(slots, w.num_kv_heads, w.head_dim)
+    vp = randn(slots, w.num_kv_heads, w.head_dim)
+    q = randn(w.total_q, w.num_heads, w.head_dim)
+    bt = torch.from_numpy(w.block_tables).to(dev)
+    ctx = torch.from_numpy(w.context_lens).to(dev)
+    qs = torch.from_numpy(w.q_start).to(dev)
+    out = torch.empty_like(q)
+    path, _ = ops.prefill_plan(q, kp, bt, qs, w.block_size, w.scale)
+    for _ in range(warmup):
+        ops.paged_prefill(q, kp, vp, bt, ctx, qs, w.scale, w.block_size, out=out)
+    torch.cuda.synchronize(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for _ in range(steps):
+        ops.paged_prefill(q, kp, vp, bt, ctx, qs, w.scale, w.block_size, out=out)
+    ev[1].record()
+    ev[1].synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / steps
+    ms_job = irdist.max_over_ranks(ms, device=dev) if world > 1 else ms
+    ops.check_device_errors(dev)
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    tflops = w.flops() / (ms / 1e3) / 1e12
+    del kp, vp, q, out
+    return {"workload": "P1: 8 causal prompts x 4096 tokens, Qwen2.5-7B attention (28 q / "
+                        "4 kv heads, head_dim 128), block 16, per GPU",
+            "metric": "paged prefill attention TFLOP/s (causal, useful FLOPs)",
+            "kernel_path": {1: "rows as decode rows", 2: "tcgen05"}.get(path, path),
+            "value": round(w.flops() * world / (ms_job / 1e3) / 1e12, 1), "unit": "TFLOP/s",
+            "ms_per_step": round(ms_job, 4), "steps": steps, "scaling": "weak",
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
+                         "frac": round(tflops / peak, 4),
+                         "peak_kind": "measured" if peaks else "fallback"}}
 
 
 def run_prefill(args):
