@@ -265,6 +265,42 @@ int ir_paged_decode_rope_write(void* out, const void* q, void* k_pool, void* v_p
                                ir_stream_t stream);
 
 /*
+ * ir_paged_decode with RoPE applied to q in the kernel (fp32 cos/sin rows
+ * [B, head_dim] with rope_stride, as infrared's RotaryEmbedding returns them):
+ * for a step whose new K/V are already in the pool (ir_kv_proj_rope_write).
+ * Replaces apply_rotary_pos_emb on q (infrared/model/layers.py:79-89, 165)
+ * and the read of paged_attention (infrared/model/triton_attention.py:81-129).
+ */
+int ir_paged_decode_rope(void* out, const void* q, const void* k_pool, const void* v_pool,
+                         const float* rope_cos, const float* rope_sin, int64_t rope_stride,
+                         const int32_t* block_tables, const int32_t* context_lens,
+                         const ir_decode_shape* shape, void* workspace,
+                         size_t workspace_bytes, int32_t* err_flag, ir_stream_t stream);
+
+/*
+ * K/V projection of num_tokens new tokens with bias, RoPE on K and the cache
+ * write in one kernel (5th-generation tensor cores): for token t,
+ *   k = x[t] @ w_k^T + b_k,  v = x[t] @ w_v^T + b_v   (rounded to dtype once),
+ *   k = k * cos[t] + rotate_half(k) * sin[t]          (dtype rounding per op),
+ *   k_pool[slot_mapping[t]] = k,  v_pool[slot_mapping[t]] = v.
+ * x [num_tokens, hidden] with row stride x_stride; w_k / w_v
+ * [num_kv_heads * head_dim, hidden] row-major (nn.Linear weights); b_k / b_v
+ * [num_kv_heads * head_dim] or null; rope_cos / rope_sin fp32 rows
+ * [num_tokens, head_dim] with rope_stride, or null (no RoPE). bf16 / fp16,
+ * head_dim 64 or 128, hidden a multiple of 64; x, the weights and the pools
+ * 16-byte aligned. A slot outside the pool is skipped and flagged
+ * (IR_DEVERR_SLOT). Replaces k_proj / v_proj, apply_rotary_pos_emb on k of
+ * Attention.forward (infrared/model/layers.py:158-165) and PagedKVPool.write
+ * (infrared/cache/paged_kv_cache.py:48-57).
+ */
+int ir_kv_proj_rope_write(const void* x, int64_t x_stride, int num_tokens, int hidden,
+                          const void* w_k, const void* w_v, const void* b_k,
+                          const void* b_v, const float* rope_cos, const float* rope_sin,
+                          int64_t rope_stride, const int64_t* slot_mapping, void* k_pool,
+                          void* v_pool, int64_t num_slots, int num_kv_heads, int head_dim,
+                          int dtype, int32_t* err_flag, ir_stream_t stream);
+
+/*
  * Decode attention returning the softmax-normalised fp32 output and its
  * log-sum-exp instead of the final row: o [B, H, D] fp32 contiguous,
  * lse [B, H] fp32 natural log (-inf for an empty context, o = 0). These are

@@ -8,6 +8,9 @@ Three hand-written sm_100a CUDA paths behind a C ABI
   GQA decode attention over block tables (optionally fused with the cache
   write, and with the rotary embedding of q and the new K), split across all
   SMs in equal token shares with a log-sum-exp merge;
+* ``kv_proj_rope_write`` — the K/V projections of a step's new tokens with
+  bias, RoPE and the pool write in the epilogue (tcgen05 tensor cores), and
+  ``paged_decode_rope`` — decode with RoPE on q, for such a step;
 * ``paged_decode_lse`` + ``lse_merge`` — partials of a KV range and their
   combination, used to spread one long context over several GPUs;
 * ``paged_prefill`` — causal attention of packed query rows (prefill with a
@@ -21,13 +24,14 @@ decode calls here; ``dist`` shards the work over the GPUs of one node.
 from ._lib import InfraredB200Error, UnsupportedShape
 from .attention import paged_attention
 from .ops import (DeviceError, cache_gather, cache_write, check_device_errors,
-                  derive_block_metadata, lse_merge, paged_decode, paged_decode_lse,
-                  paged_decode_rope_write, paged_decode_write, paged_prefill)
+                  derive_block_metadata, kv_proj_rope_write, lse_merge, paged_decode,
+                  paged_decode_lse, paged_decode_rope, paged_decode_rope_write,
+                  paged_decode_write, paged_prefill)
 from .paged_kv_cache import PagedContext, PagedKVPool
 
 __all__ = [
     "DeviceError", "InfraredB200Error", "PagedContext", "PagedKVPool", "UnsupportedShape",
     "cache_gather", "cache_write", "check_device_errors", "derive_block_metadata",
-    "lse_merge", "paged_attention", "paged_decode", "paged_decode_lse",
-    "paged_decode_rope_write", "paged_decode_write", "paged_prefill",
+    "kv_proj_rope_write", "lse_merge", "paged_attention", "paged_decode", "paged_decode_lse",
+    "paged_decode_rope", "paged_decode_rope_write", "paged_decode_write", "paged_prefill",
 ]

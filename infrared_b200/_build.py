@@ -22,7 +22,7 @@ INCLUDE = ROOT / "include"
 LIB = PKG / "libinfrared_b200.so"
 
 SOURCES = ["capi.cu", "cache_ops.cu", "decode_generic.cu", "decode_tma.cu", "prefill_tc.cu",
-           "peer_exchange.cu"]
+           "peer_exchange.cu", "kv_proj.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -91,6 +91,14 @@ class PrefillShape(ctypes.Structure):
 # (name, restype, argtypes) of every exported function
 _SIGNATURES = {
     "ir_set_prefill_path": (c_int, [c_int]),
+    "ir_paged_decode_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_int64, c_void_p, c_void_p,
+                                     POINTER(DecodeShape), c_void_p, c_size_t, c_void_p,
+                                     c_void_p]),
+    "ir_kv_proj_rope_write": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                      c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                                      c_int, c_void_p, c_void_p]),
     "ir_peer_alloc": (c_int, [c_size_t, POINTER(c_void_p)]),
     "ir_peer_free": (c_int, [c_void_p]),
     "ir_peer_handle": (c_int, [c_void_p, c_void_p]),

@@ -174,6 +174,25 @@ bool make_pool_map(CUtensorMap* map, const void* pool, int64_t num_slots,
   return r == CUDA_SUCCESS;
 }
 
+// A row-major [rows, cols] 16-bit matrix as a 2-D (cols, rows) map with
+// {64, box_rows} boxes and the 128-byte swizzle (the K-major operand tiles of
+// the tensor-core kernels).
+bool make_rows_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols,
+                   int64_t row_stride, int dtype, int box_rows) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == IR_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------ planning
 
 struct Plan {
@@ -780,6 +799,70 @@ int ir_paged_decode_rope_write(void* out, const void* q, void* k_pool, void* v_p
                      k_new, v_new, kv_stride, slot_mapping, block_tables,
                      context_lens, shape, workspace, workspace_bytes, err_flag,
                      stream, rope_cos, rope_sin, rope_stride);
+}
+
+int ir_paged_decode_rope(void* out, const void* q, const void* k_pool, const void* v_pool,
+                         const float* rope_cos, const float* rope_sin, int64_t rope_stride,
+                         const int32_t* block_tables, const int32_t* context_lens,
+                         const ir_decode_shape* shape, void* workspace,
+                         size_t workspace_bytes, int32_t* err_flag, ir_stream_t stream) {
+  if (!rope_cos || !rope_sin) return fail(IR_ERR_INVALID_ARG, "null rope_cos / rope_sin");
+  return decode_impl(Mode::kFinal, out, nullptr, nullptr, q, k_pool, v_pool, nullptr,
+                     nullptr, 0, nullptr, block_tables, context_lens, shape, workspace,
+                     workspace_bytes, err_flag, stream, rope_cos, rope_sin, rope_stride);
+}
+
+int ir_kv_proj_rope_write(const void* x, int64_t x_stride, int num_tokens, int hidden,
+                          const void* w_k, const void* w_v, const void* b_k,
+                          const void* b_v, const float* rope_cos, const float* rope_sin,
+                          int64_t rope_stride, const int64_t* slot_mapping, void* k_pool,
+                          void* v_pool, int64_t num_slots, int num_kv_heads, int head_dim,
+                          int dtype, int32_t* err_flag, ir_stream_t stream) {
+  if (dtype != IR_DTYPE_BF16 && dtype != IR_DTYPE_F16)
+    return fail(IR_ERR_UNSUPPORTED, "the projection kernel takes bf16 or fp16");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(IR_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (num_tokens < 0 || num_kv_heads <= 0 || num_kv_heads > 256)
+    return fail(IR_ERR_INVALID_ARG, "bad num_tokens / num_kv_heads");
+  if (hidden < 64 || hidden % 64 != 0)
+    return fail(IR_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  if (num_tokens == 0) return IR_OK;
+  if (!x || !w_k || !w_v || !slot_mapping || !k_pool || !v_pool)
+    return fail(IR_ERR_INVALID_ARG, "null pointer");
+  if ((rope_cos == nullptr) != (rope_sin == nullptr))
+    return fail(IR_ERR_INVALID_ARG, "rope_cos and rope_sin must both be given");
+  if (rope_cos && (rope_stride < head_dim || !aligned(rope_cos, 4) || !aligned(rope_sin, 4)))
+    return fail(IR_ERR_INVALID_ARG, "rope tables: stride < head_dim or not 4-byte aligned");
+  if (x_stride < hidden || (x_stride * 2) % 16 != 0 || !aligned(x, 16) || !aligned(w_k, 16) ||
+      !aligned(w_v, 16))
+    return fail(IR_ERR_INVALID_ARG,
+                "x, w_k, w_v must be 16-byte aligned with 16-byte row strides");
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || num_slots <= 0)
+    return fail(IR_ERR_INVALID_ARG, "pools must be 16-byte aligned and non-empty");
+  const int64_t n_out = static_cast<int64_t>(num_kv_heads) * head_dim;
+  CUtensorMap tmx, tmwk, tmwv;
+  if (!make_rows_map(&tmx, x, num_tokens, hidden, x_stride, dtype, 128) ||
+      !make_rows_map(&tmwk, w_k, n_out, hidden, hidden, dtype, head_dim) ||
+      !make_rows_map(&tmwv, w_v, n_out, hidden, hidden, dtype, head_dim))
+    return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  irb::KvProjArgs a{};
+  a.M = num_tokens;
+  a.K = hidden;
+  a.Hkv = num_kv_heads;
+  a.D = head_dim;
+  a.bias_k = b_k;
+  a.bias_v = b_v;
+  a.cos = rope_cos;
+  a.sin = rope_sin;
+  a.rope_stride = rope_stride;
+  a.slots = slot_mapping;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_slots = num_slots;
+  a.err = err_flag;
+  return cuda_status(irb::launch_kv_proj(tmx, tmwk, tmwv, a, dtype,
+                                         static_cast<cudaStream_t>(stream)),
+                     "K/V projection launch");
 }
 
 int ir_paged_decode_lse(float* o, float* lse, const void* q,

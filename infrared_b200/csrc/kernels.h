@@ -33,6 +33,26 @@ struct PrefillArgs {
 int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
                       const PrefillArgs& a, int dtype, int sm_count, cudaStream_t stream);
 
+// kv_proj.cu: K/V projection of M new tokens (x [M, K], W_k / W_v [Hkv*D, K]
+// row-major, K % 64 == 0) with bias, RoPE on K and the pool write in the
+// epilogue; tmx views x as (K, M), tmwk / tmwv the weights as (K, Hkv*D),
+// boxes {64, 128} and {64, D}, 128-byte swizzle.
+struct KvProjArgs {
+  int M, K, Hkv, D;
+  const void* bias_k;  // [Hkv * D] of the dtype, or null
+  const void* bias_v;
+  const float* cos;    // [M, D] rows with rope_stride, or null (no RoPE)
+  const float* sin;
+  int64_t rope_stride;
+  const int64_t* slots;  // [M]
+  void* k_pool;          // [num_slots, Hkv, D]
+  void* v_pool;
+  int64_t num_slots;
+  int32_t* err;
+};
+int launch_kv_proj(const CUtensorMap& tmx, const CUtensorMap& tmwk, const CUtensorMap& tmwv,
+                   const KvProjArgs& a, int dtype, cudaStream_t s);
+
 // peer_exchange.cu: KV-chunk partials stored into every GPU of the node
 // (buffers mapped with CUDA IPC) in a flagged 16-byte chunk format and merged,
 // in one kernel; see the file header for the buffer layout and the protocol.

@@ -503,6 +503,89 @@ def paged_decode_rope_write(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.T
     return out
 
 
+def _rope_rows(cos, sin, b, d, device):
+    cos = cos.reshape(b, d) if cos.dim() != 2 else cos
+    sin = sin.reshape(b, d) if sin.dim() != 2 else sin
+    for name, t in (("cos", cos), ("sin", sin)):
+        if t.dtype != torch.float32 or t.device != device or tuple(t.shape) != (b, d) \
+                or t.stride(1) != 1:
+            raise ValueError(f"{name} must be fp32 [B, D] rows on the tensors' device")
+    if cos.stride(0) != sin.stride(0):
+        cos, sin = cos.contiguous(), sin.contiguous()
+    return cos, sin
+
+
+@_on_tensor_device
+def paged_decode_rope(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                      block_tables: torch.Tensor, context_lens: torch.Tensor,
+                      cos: torch.Tensor, sin: torch.Tensor, scale: float, block_size: int,
+                      out: torch.Tensor | None = None,
+                      ws: torch.Tensor | None = None) -> torch.Tensor:
+    """:func:`paged_decode` with RoPE applied to the un-rotated ``q`` in the
+    kernel (``cos``/``sin`` fp32 ``[B, D]``): the step's K/V are already in the
+    pool (:func:`kv_proj_rope_write`)."""
+    _check_decode_inputs(q, k_pool, v_pool, block_tables, context_lens)
+    dev = _dev_index(q)
+    b, _, d = q.shape
+    cos, sin = _rope_rows(cos, sin, b, d, q.device)
+    if out is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    s, ws = _ws_and_shape(lambda fl: _shape(q, k_pool, block_tables, block_size, scale,
+                                            out.stride(0), fl), dev, ws)
+    check(_lib.load().ir_paged_decode_rope(
+        out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), cos.data_ptr(),
+        sin.data_ptr(), cos.stride(0) if b else d, block_tables.data_ptr(),
+        context_lens.data_ptr(), s, ws.data_ptr(), ws.numel(), error_flag(dev).data_ptr(),
+        _stream(dev)))
+    return out
+
+
+@_on_tensor_device
+def kv_proj_rope_write(x: torch.Tensor, w_k: torch.Tensor, w_v: torch.Tensor,
+                       b_k: torch.Tensor | None, b_v: torch.Tensor | None,
+                       cos: torch.Tensor | None, sin: torch.Tensor | None,
+                       slot_mapping: torch.Tensor, k_pool: torch.Tensor,
+                       v_pool: torch.Tensor) -> None:
+    """``k_pool[slot] = rope(x @ w_k^T + b_k)``, ``v_pool[slot] = x @ w_v^T + b_v``
+    for every row of ``x [N, hidden]`` in one tensor-core kernel
+    (``ir_kv_proj_rope_write``): ``w_k`` / ``w_v`` are the ``nn.Linear``
+    weights ``[Hkv * D, hidden]``, ``b_k`` / ``b_v`` their biases (or None),
+    ``cos`` / ``sin`` fp32 ``[N, D]`` RoPE rows (or None: no RoPE), the pools
+    one layer's ``[num_slots, Hkv, D]``; bf16 / fp16."""
+    dev = _dev_index(x)
+    _check_pool(k_pool, "k_pool")
+    _check_pool(v_pool, "v_pool")
+    if k_pool.shape != v_pool.shape or k_pool.dtype != v_pool.dtype:
+        raise ValueError("k_pool and v_pool differ")
+    hkv, d = k_pool.shape[1], k_pool.shape[2]
+    x = x.reshape(-1, x.shape[-1])
+    n, hidden = x.shape
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    for name, w in (("w_k", w_k), ("w_v", w_v)):
+        if tuple(w.shape) != (hkv * d, hidden) or not w.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous [Hkv*D, hidden] weight")
+    for name, t in (("x", x), ("w_k", w_k), ("w_v", w_v)):
+        if t.dtype != k_pool.dtype or t.device != k_pool.device:
+            raise ValueError(f"{name} must match the pool's dtype and device")
+    for name, t in (("b_k", b_k), ("b_v", b_v)):
+        if t is not None and (t.numel() != hkv * d or t.dtype != k_pool.dtype
+                              or not t.is_contiguous() or t.device != k_pool.device):
+            raise ValueError(f"{name} must be a contiguous [Hkv*D] bias of the pool's dtype")
+    slots = slot_mapping.reshape(-1)
+    if slots.dtype != torch.int64 or not slots.is_contiguous() or slots.numel() != n:
+        raise ValueError("slot_mapping must be contiguous int64 [N]")
+    rs = d
+    if cos is not None:
+        cos, sin = _rope_rows(cos, sin, n, d, x.device)
+        rs = cos.stride(0) if n else d
+    check(_lib.load().ir_kv_proj_rope_write(
+        x.data_ptr(), x.stride(0) if n else hidden, n, hidden, w_k.data_ptr(), w_v.data_ptr(),
+        _ptr(b_k), _ptr(b_v), _ptr(cos), _ptr(sin), rs, slots.data_ptr(), k_pool.data_ptr(),
+        v_pool.data_ptr(), k_pool.shape[0], hkv, d, dtype_code(k_pool.dtype),
+        error_flag(dev).data_ptr(), _stream(dev)))
+
+
 @_on_tensor_device
 def paged_decode_lse(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
                      block_tables: torch.Tensor, context_lens: torch.Tensor, scale: float,

@@ -34,7 +34,12 @@ infrared:
   (infrared/model/layers.py:156-182, a class attribute) -> the same
   projections, then ONE ``ir_paged_decode_rope_write`` that applies RoPE to
   q and the new K, writes K/V and attends, for paged CUDA decode calls the
-  gate accepts; every other call runs infrared's own forward.
+  gate accepts; every other call runs infrared's own forward;
+* (optional, ``fuse_kv_proj=True``, implies the above) for bf16 / fp16
+  decode calls with ``hidden % 64 == 0`` the K and V projections themselves
+  run in ``ir_kv_proj_rope_write`` (tensor cores; bias, RoPE and the pool
+  write in its epilogue: the new K/V rows go from the accumulator to their
+  slots), then ``ir_paged_decode_rope`` attends with RoPE applied to q.
 
 The replacement read path trusts the engine's decode metadata: the mask is a
 prefix of zeros and ``gather_slots`` lists whole blocks; a call that breaks
@@ -92,7 +97,7 @@ def _make_write(original):
     return write
 
 
-def _make_attention_forward(original):
+def _make_attention_forward(original, fuse_kv_proj: bool = False):
     def forward(self, x, ctx, layer_idx):
         paged = ctx.paged
         b = x.shape[0]
@@ -103,10 +108,21 @@ def _make_attention_forward(original):
                 or ctx.cos.dtype != torch.float32 or ctx.cos.numel() != b * self.head_dim):
             return original(self, x, ctx, layer_idx)
         q = self.q_proj(x).view(b, self.num_heads, self.head_dim)
-        k = self.k_proj(x).view(b, self.num_kv_heads, self.head_dim)
-        v = self.v_proj(x).view(b, self.num_kv_heads, self.head_dim)
         pool = paged.pool
         bt, cl = block_metadata(paged, ctx.mask)
+        cos = ctx.cos.reshape(b, self.head_dim)
+        sin = ctx.sin.reshape(b, self.head_dim)
+        if fuse_kv_proj and x.dtype != torch.float32 and x.shape[-1] % 64 == 0:
+            # K/V projected, rotated and written to the pool in one kernel
+            ops.kv_proj_rope_write(x.reshape(b, x.shape[-1]), self.k_proj.weight,
+                                   self.v_proj.weight, self.k_proj.bias, self.v_proj.bias,
+                                   cos, sin, paged.write_slots.reshape(-1),
+                                   pool.k[layer_idx], pool.v[layer_idx])
+            out = ops.paged_decode_rope(q, pool.k[layer_idx], pool.v[layer_idx], bt, cl, cos,
+                                        sin, self.scale, pool.block_size)
+            return self.o_proj(out.view(b, 1, self.num_heads * self.head_dim))
+        k = self.k_proj(x).view(b, self.num_kv_heads, self.head_dim)
+        v = self.v_proj(x).view(b, self.num_kv_heads, self.head_dim)
         out = ops.paged_decode_rope_write(q, k, v, pool.k[layer_idx], pool.v[layer_idx],
                                           paged.write_slots.reshape(-1), bt, cl,
                                           ctx.cos.reshape(b, self.head_dim),
@@ -179,7 +195,7 @@ class Installed:
 def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
             graph_inputs: bool = True, layers=None, fuse_rope: bool = False,
             prefill: bool = False, paged_engine=None,
-            eager_inputs: bool = False) -> Installed:
+            eager_inputs: bool = False, fuse_kv_proj: bool = False) -> Installed:
     """Route infrared's paged decode attention to the B200 kernels.
 
     ``triton_attention`` / ``paged_kv_cache`` / ``cuda_graph`` / ``layers``
@@ -191,7 +207,9 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
     that RoPE runs inside the decode kernel; ``prefill=True`` also routes
     packed prefill / mixed frames (``Sq > 1``) to the tensor-core kernel;
     ``eager_inputs=True`` builds the eager decode step's inputs on the device
-    (``paged_engine`` defaults to ``infrared.engine.paged_engine``).
+    (``paged_engine`` defaults to ``infrared.engine.paged_engine``);
+    ``fuse_kv_proj=True`` (implies ``fuse_rope``) also runs the K/V projections
+    of 16-bit decode calls in the tensor-core kernel that writes the pool.
     """
     ta = triton_attention or importlib.import_module("infrared.model.triton_attention")
     pk = paged_kv_cache or importlib.import_module("infrared.cache.paged_kv_cache")
@@ -209,11 +227,11 @@ def install(triton_attention=None, paged_kv_cache=None, cuda_graph=None,
         cg.build_decode_static_inputs = _make_graph_inputs(saved["graph_inputs"],
                                                            cg.DecodeInputs)
     attn_cls = None
-    if fuse_rope:
+    if fuse_rope or fuse_kv_proj:
         ly = layers or importlib.import_module("infrared.model.layers")
         attn_cls = ly.Attention
         saved["forward"] = attn_cls.forward
-        attn_cls.forward = _make_attention_forward(saved["forward"])
+        attn_cls.forward = _make_attention_forward(saved["forward"], fuse_kv_proj)
     eng_cls = None
     if eager_inputs:
         pe = paged_engine or importlib.import_module("infrared.engine.paged_engine")

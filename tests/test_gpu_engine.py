@@ -134,7 +134,8 @@ def spy(monkeypatch):
     counts = {}
     targets = [(ops, n) for n in ("cache_write", "paged_decode", "paged_decode_rope_write",
                                   "paged_prefill", "derive_block_metadata",
-                                  "derive_varlen_metadata")]
+                                  "derive_varlen_metadata", "kv_proj_rope_write",
+                                  "paged_decode_rope")]
     targets.append((graph_inputs, "build_decode_static_inputs"))
     for mod, name in targets:
         fn = getattr(mod, name)
@@ -303,3 +304,21 @@ def test_bf16_engine_matches_infrared_own_path(installed, spy, graphs):
     assert spy.get("paged_prefill", 0) + spy.get("derive_varlen_metadata", 0) > 0, spy
     if not graphs:
         assert spy.get("paged_decode_rope_write", 0) > 0, spy
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_bf16_engine_with_the_projection_kernel(installed, spy, graphs):
+    """``shim.install(fuse_kv_proj=True)``: each decode step's K/V projections,
+    RoPE and cache write run in ir_kv_proj_rope_write and the decode applies
+    RoPE to q (ir_paged_decode_rope); against infrared's own bf16 path."""
+    model = _qwen7b_attention_bf16()
+    prompts = _long_prompts(6, 20, 300, 512, seed=7)
+    max_new = [16] * 6
+    kw = dict(max_num_seqs=8, block_size=16, num_blocks=256, graph_max_seq_len=512,
+              enable_cuda_graph=graphs, record=True)
+    _, ref_eng = _run_engine(model, prompts, max_new, enable_triton_attention=False, **kw)
+    installed(fuse_kv_proj=True, prefill=True)
+    _, new_eng = _run_engine(model, prompts, max_new, enable_triton_attention=True, **kw)
+    _assert_tokens_match_up_to_near_tie(ref_eng.sampler.rows, new_eng.sampler.rows,
+                                        f"infrared bf16 vs projection kernel (graphs={graphs})")
+    assert spy.get("kv_proj_rope_write", 0) > 0 and spy.get("paged_decode_rope", 0) > 0, spy
