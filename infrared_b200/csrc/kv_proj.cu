@@ -15,7 +15,8 @@
 // takes the r-th slice of the hidden dimension (split-K), so a decode step's
 // weights are streamed by kSplit x 2 Hkv CTAs at once:
 //   warp 0, one lane: TMA copies of x [128 x 64] and W [N x 64] per stage
-//                     (128-byte swizzle, a ring of kNS stages);
+//                     (128-byte swizzle, a ring of kNS stages, whose shared
+//                     memory then holds the partial sums);
 //   warp 1, one lane: tcgen05.mma kind::f16, M = 128 tokens, N = head_dim,
 //                     K = 16 per instruction, accumulating in TMEM;
 //   warps 0-3:        each thread reads its token row of the accumulator and
@@ -41,7 +42,7 @@ namespace {
 constexpr int kM = 128;        // token rows per tile (MMA M)
 constexpr int kKc = 64;        // hidden elements per stage (one 128-byte row)
 constexpr int kSplit = 8;      // CTAs per cluster (portable cluster size)
-constexpr int kNS = 4;         // ring stages
+constexpr int kNS = 6;         // ring stages (a 3584-wide hidden is 7 chunks per CTA)
 constexpr int kThreads = 128;  // 4 warps
 constexpr int kRowsPer = kM / kSplit;  // rows each CTA reduces and writes
 
@@ -52,8 +53,11 @@ struct KvLayout {
   static constexpr int kPartStride = D + 4;                // fp32 row of the partial
   static constexpr int off_a = 0;
   static constexpr int off_b = kNS * kStageA;
-  static constexpr int off_part = off_b + kNS * kStageB;
-  static constexpr int off_bar = off_part + kM * kPartStride * 4;  // full, empty, acc
+  // the partial sums reuse the ring once every MMA (the ring's last reader)
+  // has completed
+  static constexpr int off_part = 0;
+  static_assert(kM * kPartStride * 4 <= kNS * (kStageA + kStageB), "partial fits the ring");
+  static constexpr int off_bar = off_b + kNS * kStageB;  // full, empty, acc
   static constexpr int off_slot = off_bar + (2 * kNS + 1) * 8;
   static constexpr int kBytes = off_slot + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
@@ -179,6 +183,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncwarp();
 
+  // this thread's rows and columns of the reduction, and the epilogue inputs
+  // for them, loaded while the MMAs finish
+  const int rl = threadIdx.x / 8, seg = threadIdx.x % 8;
+  const int r = static_cast<int>(rank) * kRowsPer + rl;  // row of the tile
+  const int m = m0 + r;                                  // token
+  const int c0 = seg * kSegCols;
+  float blo[kSegCols], bhi[kSegCols], clo[kSegCols], chi[kSegCols], slo[kSegCols],
+      shi[kSegCols];
+  const bool rope = is_k && a.cos != nullptr;
+  int64_t slot = -1;
+  if (m < a.M) {
+    const T* bias = reinterpret_cast<const T*>(is_k ? a.bias_k : a.bias_v);
+    const float* cs = rope ? a.cos + static_cast<int64_t>(m) * a.rope_stride : nullptr;
+    const float* sn = rope ? a.sin + static_cast<int64_t>(m) * a.rope_stride : nullptr;
+#pragma unroll
+    for (int j = 0; j < kSegCols; ++j) {
+      blo[j] = bias ? DT<T>::to_f(bias[kvh * D + c0 + j]) : 0.f;
+      bhi[j] = bias ? DT<T>::to_f(bias[kvh * D + kHalfD + c0 + j]) : 0.f;
+      clo[j] = rope ? cs[c0 + j] : 0.f;
+      chi[j] = rope ? cs[kHalfD + c0 + j] : 0.f;
+      slo[j] = rope ? sn[c0 + j] : 0.f;
+      shi[j] = rope ? sn[kHalfD + c0 + j] : 0.f;
+    }
+    slot = a.slots[m];
+  }
+
   // ------------------------------------------- partial rows -> shared memory
   // one decision per warp: tcgen05.ld is executed by all lanes or none
   const bool done = __all_sync(0xffffffffu, mbar_wait_bounded(acc, 0));
@@ -206,15 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------- sum the kSplit partials of this CTA's rows, write them
   {
-    const int rl = threadIdx.x / 8, seg = threadIdx.x % 8;
-    const int r = static_cast<int>(rank) * kRowsPer + rl;  // row of the tile
-    const int m = m0 + r;                                  // token
-    const int c0 = seg * kSegCols;
     float lo[kSegCols], hi[kSegCols];
 #pragma unroll
     for (int j = 0; j < kSegCols; ++j) lo[j] = hi[j] = 0.f;
     const float* src = part + r * L::kPartStride;
-    for (uint32_t cta = 0; cta < static_cast<uint32_t>(kSplit); ++cta) {  // rank order
+    // all kSplit loads in flight at once; the sums still run in rank order
+#pragma unroll
+    for (uint32_t cta = 0; cta < static_cast<uint32_t>(kSplit); ++cta) {
 #pragma unroll
       for (int q = 0; q < kSegCols; q += 4) {
         const float4 x = ld_dsmem4(src + c0 + q, cta);
@@ -224,28 +252,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (m < a.M) {
-      const T* bias = reinterpret_cast<const T*>(is_k ? a.bias_k : a.bias_v);
       float ylo[kSegCols], yhi[kSegCols];
 #pragma unroll
       for (int j = 0; j < kSegCols; ++j) {
         // the projection's output: accumulator + bias, rounded once
-        const float blo = bias ? DT<T>::to_f(bias[kvh * D + c0 + j]) : 0.f;
-        const float bhi = bias ? DT<T>::to_f(bias[kvh * D + kHalfD + c0 + j]) : 0.f;
-        ylo[j] = DT<T>::to_f(DT<T>::from_f(lo[j] + blo));
-        yhi[j] = DT<T>::to_f(DT<T>::from_f(hi[j] + bhi));
+        ylo[j] = DT<T>::to_f(DT<T>::from_f(lo[j] + blo[j]));
+        yhi[j] = DT<T>::to_f(DT<T>::from_f(hi[j] + bhi[j]));
       }
-      if (is_k && a.cos != nullptr) {
-        const float* cs = a.cos + static_cast<int64_t>(m) * a.rope_stride;
-        const float* sn = a.sin + static_cast<int64_t>(m) * a.rope_stride;
+      if (rope) {
 #pragma unroll
         for (int j = 0; j < kSegCols; ++j) {
-          const int d = c0 + j, u = kHalfD + c0 + j;
           const float xl = ylo[j], xh = yhi[j];
-          ylo[j] = rope_elem<T>(xl, xh, cs[d], sn[d], false);
-          yhi[j] = rope_elem<T>(xh, xl, cs[u], sn[u], true);
+          ylo[j] = rope_elem<T>(xl, xh, clo[j], slo[j], false);
+          yhi[j] = rope_elem<T>(xh, xl, chi[j], shi[j], true);
         }
       }
-      const int64_t slot = a.slots[m];
       if (slot < 0 || slot >= a.num_slots) {
         set_err(a.err, IR_DEVERR_SLOT);
       } else {
