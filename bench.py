@@ -78,7 +78,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--only", default="",
                    help="--config kernels: run one case (cache_write_c3, cache_write_bulk, "
-                        "lse_merge_c4, lse_merge_b256, peer_exchange_world1_b256)")
+                        "lse_merge_c4, lse_merge_b256, kv_proj_c5, kv_proj_c5_torch, "
+                        "peer_exchange_world1_b256)")
     p.add_argument("--inline-merge", action="store_true",
                    help="merge rows of <= 4 pieces in the decode kernel (zeroed workspace)")
     p.add_argument("--dynamic-tail", action="store_true",
@@ -1372,6 +1373,34 @@ def run_kernels(args):
         timed(name, lambda i, o=o, lse=lse, out=out: ops.lse_merge(o, lse, torch.bfloat16,
                                                                     out=out),
               o.numel() * 4 + lse.numel() * 4 + out.numel() * 2, args.steps)
+    # K/V projection + bias + RoPE + cache write at the C5 layer shape (128 new
+    # tokens, hidden 3584, 4 kv heads x 128), and the same work in PyTorch
+    if not args.only or args.only.startswith("kv_proj"):
+        hid, hkv, d, n = 3584, 4, 128, 128
+        x = torch.randn(n, hid, generator=g, device=dev).to(torch.bfloat16)
+        wk = (torch.randn(hkv * d, hid, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wv = (torch.randn(hkv * d, hid, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        bk = (torch.randn(hkv * d, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        bv = (torch.randn(hkv * d, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        inv = 1.0 / (1e6 ** (torch.arange(0, d, 2, device=dev, dtype=torch.float32) / d))
+        f = torch.randint(0, 2048, (n,), generator=g, device=dev).float()[:, None] * inv
+        cos, sin = torch.cat((f, f), -1).cos(), torch.cat((f, f), -1).sin()
+        slots = torch.randperm(pool_k.shape[0], generator=g, device=dev)[:n].contiguous()
+        kvp = torch.zeros(pool_k.shape[0], hkv, d, dtype=torch.bfloat16, device=dev)
+        vvp = torch.zeros_like(kvp)
+        nb = 2 * hkv * d * hid * 2 + n * hid * 2 + 2 * n * hkv * d * 2
+
+        def torch_path(i):
+            k = torch.nn.functional.linear(x, wk, bk).view(n, hkv, d)
+            v = torch.nn.functional.linear(x, wv, bv).view(n, hkv, d)
+            c, s_ = cos[:, None].to(k.dtype), sin[:, None].to(k.dtype)
+            k = k * c + torch.cat((-k[..., d // 2:], k[..., :d // 2]), -1) * s_
+            kvp[slots] = k
+            vvp[slots] = v
+
+        timed("kv_proj_c5", lambda i: ops.kv_proj_rope_write(x, wk, wv, bk, bv, cos, sin,
+                                                             slots, kvp, vvp), nb, args.steps)
+        timed("kv_proj_c5_torch", torch_path, nb, args.steps)
     # peer exchange, world of one (7168 rows of 128)
     b, h, d = 256, 28, 128
     o = torch.randn(b, h, d, generator=g, device=dev)
