@@ -99,6 +99,9 @@ def parse_args():
                    help="c4 over several GPUs: partials by peer stores or an NCCL all-gather")
     p.add_argument("--batch", type=int, default=0,
                    help="override the workload's per-GPU batch (c2/c3/c4)")
+    p.add_argument("--prefill-path", type=int, default=0, choices=[0, 1, 2, 3],
+                   help="p1: prefill kernel override (ir_set_prefill_path): 0 auto, 1 rows "
+                        "as decode rows, 2 tcgen05, 3 tcgen05 CTA pairs")
     p.add_argument("--decode-path", type=int, default=0,
                    help="kernel override (ir_set_decode_path): 0 auto, 1 CUDA-core, "
                         "2 TMA, 3 TMA with one copy per head and half")
@@ -1434,6 +1437,10 @@ def run_kernels(args):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_PATHS = {1: "rows as decode rows", 2: "tcgen05",
+                 3: "tcgen05 CTA pairs (cta_group::2, 256-row tiles)"}
+
+
 def p1_summary(dev, world, rank, steps=10, warmup=3):
     """The ``prefill_p1`` object of the default line: P1 (8 causal 4096-token
     prompts, Qwen2.5-7B attention geometry) on the tcgen05 prefill kernel,
@@ -1481,7 +1488,7 @@ def p1_summary(dev, world, rank, steps=10, warmup=3):
     return {"workload": "P1: 8 causal prompts x 4096 tokens, Qwen2.5-7B attention (28 q / "
                         "4 kv heads, head_dim 128), block 16, per GPU",
             "metric": "paged prefill attention TFLOP/s (causal, useful FLOPs)",
-            "kernel_path": {1: "rows as decode rows", 2: "tcgen05"}.get(path, path),
+            "kernel_path": PREFILL_PATHS.get(path, path),
             "value": round(w.flops() * world / (ms_job / 1e3) / 1e12, 1), "unit": "TFLOP/s",
             "ms_per_step": round(ms_job, 4), "steps": steps, "scaling": "weak",
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
@@ -1520,7 +1527,7 @@ def run_prefill(args):
     ctx = torch.from_numpy(w.context_lens).to(dev)
     qs = torch.from_numpy(w.q_start).to(dev)
     out = torch.empty_like(q)
-    ops.set_prefill_path(args.decode_path if args.decode_path in (1, 2) else 0)
+    ops.set_prefill_path(args.prefill_path)
     path, _ = ops.prefill_plan(q, kp, bt, qs, w.block_size, w.scale)
     flops = w.flops()
 
@@ -1579,7 +1586,7 @@ def run_prefill(args):
                                "Qwen2.5-7B attention (28 q / 4 kv heads, head_dim 128), "
                                "block 16, causal",
                    "total_q_rows": w.total_q, "flops_per_step": flops,
-                   "kernel_path": {1: "rows as decode rows", 2: "tcgen05"}[path],
+                   "kernel_path": PREFILL_PATHS[path],
                    "l2": "q + out = 470 MB per step, larger than L2",
                    "timing": "K back-to-back launches, CUDA events, max over ranks"},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,

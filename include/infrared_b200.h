@@ -398,11 +398,14 @@ typedef struct ir_prefill_shape {
 
 /* Kernel choice for ir_paged_prefill: 0 auto, 1 rows as decode rows (every
  * query row decoded as its own sequence; any dtype), 2 the tcgen05 tensor-core
- * kernel (bf16/fp16, power-of-two block sizes >= 8; auto picks it whenever
- * eligible). Process-wide; a test and tuning hook. */
+ * kernel (bf16/fp16, power-of-two block sizes >= 8), 3 its CTA-pair form
+ * (the same, head_dim 128: two SMs share 256-row query tiles through
+ * cta_group::2 MMAs, each staging half of every K/V tile; only on request,
+ * as it measures slower). Auto picks 2 when eligible, else 1. Process-wide;
+ * a test and tuning hook. */
 int ir_set_prefill_path(int path);
 
-/* Path (1 or 2) ir_paged_prefill takes for this shape. */
+/* Path (1, 2 or 3) ir_paged_prefill takes for this shape. */
 int ir_paged_prefill_plan(const ir_prefill_shape* shape, int* path);
 
 /* Workspace bytes ir_paged_prefill needs (0 for the tensor-core path). */

@@ -417,7 +417,7 @@ int decode_impl(Mode mode, void* out, float* lse_o, float* lse_out,
 
 // ------------------------------------------------------------ prefill
 
-int g_prefill_path = 0;  // 0 auto, 1 rows as decode rows, 2 tensor cores
+int g_prefill_path = 0;  // 0 auto, 1 rows as decode rows, 2 tensor cores, 3 CTA pairs
 
 bool make_q_map(CUtensorMap* map, const void* q, int total_q, int h, int d, int64_t q_stride,
                 int dtype) {
@@ -465,9 +465,18 @@ bool prefill_tc_eligible(const ir_prefill_shape* s) {
          (s->out_stride * 2) % 16 == 0;
 }
 
+// The CTA-pair form shares 256-row items between two SMs (D = 128). Only on
+// request: it measured slower than the single-CTA form on long prompts (both
+// issue one N = 128 MMA per ~95 cycles, and a pair spends two SMs on one
+// issuing thread).
+bool prefill_pair_eligible(const ir_prefill_shape* s) {
+  return prefill_tc_eligible(s) && s->head_dim == 128;
+}
+
 int prefill_path(const ir_prefill_shape* s) {
   if (g_prefill_path == 1) return 1;
   if (g_prefill_path == 2) return prefill_tc_eligible(s) ? 2 : -1;
+  if (g_prefill_path == 3) return prefill_pair_eligible(s) ? 3 : -1;
   return prefill_tc_eligible(s) ? 2 : 1;
 }
 
@@ -926,7 +935,7 @@ int ir_lse_merge(void* out, int64_t out_stride, const float* o_parts,
 }
 
 int ir_set_prefill_path(int path) {
-  if (path < 0 || path > 2) return fail(IR_ERR_INVALID_ARG, "path must be 0, 1 or 2");
+  if (path < 0 || path > 3) return fail(IR_ERR_INVALID_ARG, "path must be 0, 1, 2 or 3");
   std::lock_guard<std::mutex> lk(g_mu);
   g_prefill_path = path;
   return IR_OK;
@@ -961,14 +970,15 @@ int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v
     return fail(IR_ERR_INVALID_ARG, "null pointer");
   int path = prefill_path(s);
   if (path < 0) return fail(IR_ERR_UNSUPPORTED, "tensor-core prefill forced but shape not eligible");
-  if (path == 2 && !(aligned(q, 16) && aligned(out, 16) && aligned(k_pool, 16) &&
+  if (path >= 2 && !(aligned(q, 16) && aligned(out, 16) && aligned(k_pool, 16) &&
                      aligned(v_pool, 16))) {
-    if (g_prefill_path == 2)
+    if (g_prefill_path >= 2)
       return fail(IR_ERR_UNSUPPORTED, "tensor-core prefill forced but pointers misaligned");
     path = 1;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (path == 2) {
+  if (path >= 2) {
+    const bool pair = path == 3;
     irb::PrefillArgs a{};
     a.q = q;
     a.q_stride = s->q_stride;
@@ -992,16 +1002,18 @@ int ir_paged_prefill(void* out, const void* q, const void* k_pool, const void* v
     a.err = err_flag;
     CUtensorMap tmq, tmk, tmv;
     const int rows = s->block_size < 128 ? s->block_size : 128;
+    // a CTA of a pair stages 64 keys of each K tile
+    const int krows = pair && rows > 64 ? 64 : rows;
     if (!make_q_map(&tmq, q, s->total_q, s->num_heads, s->head_dim, s->q_stride, s->dtype) ||
         !make_pool_map(&tmk, k_pool, s->num_slots, s->num_kv_heads, s->head_dim, s->dtype,
-                       rows) ||
+                       krows) ||
         !make_pool_map(&tmv, v_pool, s->num_slots, s->num_kv_heads, s->head_dim, s->dtype,
                        rows))
       return fail(IR_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     int sms = 0;
     int rc2 = cached(-1, sm_count_now, 0, &sms);
     if (rc2) return cuda_status(rc2, "device query");
-    int e = irb::launch_prefill_tc(tmq, tmk, tmv, a, s->dtype, sms > 0 ? sms : 148, st);
+    int e = irb::launch_prefill_tc(tmq, tmk, tmv, a, s->dtype, sms > 0 ? sms : 148, pair, st);
     return cuda_status(e, "prefill kernel launch");
   }
   // rows as decode rows: each query row is a sequence of context position + 1

@@ -153,6 +153,66 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
   }
 }
 
+// ---------------------------------------------------------------- clusters
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of all CTAs of the cluster; release/acquire order the shared
+// memory writes before it with the distributed reads after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of the location `local` has in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)),
+               "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier of any CTA of the cluster (`cbar` from cluster_addr),
+// releasing this thread's earlier writes at cluster scope (a full memory
+// barrier first: costly on a critical path).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cbar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cbar)
+               : "memory");
+}
+
+// The same arrive with the default (CTA-scope) release: enough to hand a
+// peer's MMA issuer tensor-memory data that tcgen05.fence::before_thread_sync
+// ordered before it (the way CTA pairs release accumulators and operands).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cbar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
+}
+
+// Bounded wait on a barrier of this CTA that threads of other CTAs arrive on:
+// acquire at cluster scope, so their writes before the arrival are visible.
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity) {
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    if (try_wait()) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 
 // 3-D tiled tensor copy global -> shared, completion counted on `bar`.
@@ -176,6 +236,19 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map,
       "tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y),
       "r"(z), "r"(w)
+      : "memory");
+}
+
+// 3-D tiled tensor copy into this CTA's shared memory whose completion is
+// counted on an mbarrier of either CTA of a CTA pair (`cbar`, a
+// shared::cluster address): the form a pair's MMA issuer uses to learn that
+// both CTAs' halves of an operand tile have landed.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t cbar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cbar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 

@@ -29,9 +29,12 @@ struct PrefillArgs {
 
 // tcgen05 kernel: 16-bit dtypes, D in {64, 128}, block size a power of two
 // >= 8; tmq views q as (D, H, total_q), tmk/tmv the pools as (D, Hkv, slots)
-// with boxes {64, 1, 128} and {64, 1, min(bs, 128)} (128-byte swizzle).
+// with boxes {64, 1, 128} (q) and {64, 1, min(bs, 128)} (128-byte swizzle).
+// pair: the CTA-pair form (D = 128; cta_group::2, 256-row items), whose K
+// map has boxes {64, 1, min(bs, 64)}.
 int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
-                      const PrefillArgs& a, int dtype, int sm_count, cudaStream_t stream);
+                      const PrefillArgs& a, int dtype, int sm_count, bool pair,
+                      cudaStream_t stream);
 
 // kv_proj.cu: K/V projection of M new tokens (x [M, K], W_k / W_v [Hkv*D, K]
 // row-major, K % 64 == 0) with bias, RoPE on K and the pool write in the

@@ -72,19 +72,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// All threads of all CTAs of the cluster; release/acquire order the shared
-// memory writes before it with the distributed reads after it.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // 16 bytes of CTA `rank`'s shared memory at the address `local` has in this CTA.
 __device__ __forceinline__ float4 ld_dsmem4(const void* local, uint32_t rank) {
   uint32_t remote;

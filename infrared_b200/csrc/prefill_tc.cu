@@ -31,6 +31,20 @@
 //               in TMEM is rescaled); the reference is handed from tile to
 //               tile through shared memory, so the two warps sharing a
 //               scheduler work on different tiles at once.
+//
+// Pair form (PAIR, D = 128): the two CTAs of a cluster (ranks 0 and 1, one SM
+// each) share 256-row work items; rank c owns rows 128c..128c+127 (its TMEM
+// lanes and its softmax warps) and the pair's tensor cores run one
+// tcgen05.mma.cta_group::2 of M = 256 per step, issued by rank 0. Each CTA
+// stages half of every K tile (64 keys, all of D) and half of every V tile
+// (all 128 keys, its 64 columns of D): the MMA reads the B operand's halves
+// from both SMs, so each SM moves half the K/V bytes through its shared
+// memory and Q.K^T reads 6 KB instead of 8 KB of it per 16-element step.
+// Barriers counting both CTAs (stage full, Q full, P full, O free) live in
+// rank 0: rank 1's copies complete on them across the pair and its softmax
+// threads arrive on them remotely; rank 0's commits signal both CTAs' copies
+// of the per-CTA barriers (stage empty, S full, P.V done) at once.
+//
 // Every wait is bounded (2 s); on a timeout the CTA flags IR_DEVERR_TIMEOUT,
 // lets its copies and MMAs drain (bounded), frees its tensor memory and ends.
 #include "tcgen05.cuh"
@@ -47,23 +61,30 @@ constexpr int kWgThreads = 128;  // one softmax warpgroup: one thread per query 
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSBuf = 3;  // S buffers: Q.K^T runs two tiles ahead of the softmax
 constexpr uint32_t kColO = kSBuf * kKeys;  // S buffers at columns 0, 128, 256; O at 384
+constexpr int kPairStages = 2;  // ring stages of the pair form (16 KB per side each)
 constexpr float kRescaleLog2 = 8.f;  // move the reference max when it grows by > 2^8
 
 
-template <int D>
+template <int D, bool PAIR>
 struct PLayout {
   static constexpr int kHalves = D / 64;
-  static constexpr int kHalf = kRows * 128;              // one 64-column half of a tile
-  static constexpr int kQ = kHalves * kHalf;             // Q tile
-  static constexpr int kSide = kHalves * kKeys * 128;    // one K or V tile
-  static constexpr int NS = D == 128 ? 2 : 4;            // stages per ring
+  static constexpr int kHalf = kRows * 128;              // one 64-column half of the Q tile
+  static constexpr int kQ = kHalves * kHalf;             // Q tile (this CTA's rows)
+  // keys of a K tile staged here (a pair splits them) and one 64-column half of them
+  static constexpr int kKRows = PAIR ? kKeys / 2 : kKeys;
+  static constexpr int kKHalf = kKRows * 128;
+  static constexpr int kKSide = kHalves * kKHalf;
+  // 64-column halves of a V tile staged here (a pair splits the columns)
+  static constexpr int kVHalves = PAIR ? 1 : kHalves;
+  static constexpr int kVSide = kVHalves * kKeys * 128;
+  static constexpr int NS = PAIR ? kPairStages : (D == 128 ? 2 : 4);  // stages per ring
   static constexpr int off_q = 0;
   static constexpr int off_k = kQ;
-  static constexpr int off_v = off_k + NS * kSide;
-  static constexpr int off_bar = off_v + NS * kSide;
+  static constexpr int off_v = off_k + NS * kKSide;
+  static constexpr int off_bar = off_v + NS * kVSide;
   // q_full, q_empty, k_full[NS], k_empty[NS], v_full[NS], v_empty[NS], s_full[kSBuf],
-  // s_free[kSBuf], p_full[2], p_done[2], o_free, drain, ref_full[2], l_ready
-  static constexpr int kBars = 2 + 4 * NS + 2 * kSBuf + 9;
+  // s_free[kSBuf], p_full[2], p_done[2], o_free, drain, ref_full[2], l_ready, v_last
+  static constexpr int kBars = 2 + 4 * NS + 2 * kSBuf + 10;
   static constexpr int off_misc = off_bar + kBars * 8;
   // reference max per row after tile g, [g & 1][128 rows], then the row sums one
   // softmax warpgroup hands to the other at the end of an item [128 rows]
@@ -72,15 +93,16 @@ struct PLayout {
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1 KB alignment
 };
 
-// CTA blockIdx.x -> (sequence, q tile of that sequence) by a warp-wide scan of
-// tiles per sequence; seq = -1 when the index is past the last tile.
+// Tile index t -> (sequence, q tile of that sequence) by a warp-wide scan of
+// TR-row tiles per sequence; seq = -1 when the index is past the last tile.
+template <int TR>
 __device__ __forceinline__ void locate_tile(const PrefillArgs& a, int t, int lane, int* seq,
                                             int* tile) {
   int acc = 0;
   for (int base = 0; base < a.S; base += 32) {
     const int sq = base + lane;
     int nt = 0;
-    if (sq < a.S) nt = (a.q_start[sq + 1] - a.q_start[sq] + kRows - 1) / kRows;
+    if (sq < a.S) nt = (a.q_start[sq + 1] - a.q_start[sq] + TR - 1) / TR;
     if (nt < 0) nt = 0;
     int incl = nt;
 #pragma unroll
@@ -103,7 +125,8 @@ __device__ __forceinline__ void locate_tile(const PrefillArgs& a, int t, int lan
   *tile = 0;
 }
 
-// One work item: 128 query rows of one sequence for one query head.
+// One work item: TR (128, or 256 for a CTA pair) query rows of one sequence
+// for one query head.
 struct Item {
   int s;      // sequence; -1: past the last item; -2: invalid metadata (skipped)
   int h, kvh;
@@ -116,38 +139,42 @@ struct Item {
 
 // Item `it` of the list (q tile major, head minor; the q tiles of a sequence
 // from the last, longest one down). Warp-collective: every lane gets the same.
+template <int TR = kRows>
 __device__ __forceinline__ Item item_of(const PrefillArgs& a, int it, int lane) {
   Item x;
   x.h = it % a.H;
   x.kvh = x.h / a.n_rep;
   int sq, t;
-  locate_tile(a, it / a.H, lane, &sq, &t);
+  locate_tile<TR>(a, it / a.H, lane, &sq, &t);
   x.s = sq;
   if (sq < 0) return x;
   const int qs = a.q_start[sq];
   const int ql = a.q_start[sq + 1] - qs;
-  const int qt = (ql + kRows - 1) / kRows - 1 - t;
+  const int qt = (ql + TR - 1) / TR - 1 - t;
   const int ctx = a.context_lens[sq];
   if (ctx < ql || ctx > a.max_blocks * a.bs) {
     x.s = -2;
     return x;
   }
-  x.r0 = qs + qt * kRows;
-  x.nrows = min(kRows, ql - qt * kRows);
-  x.pos0 = ctx - ql + qt * kRows;
+  x.r0 = qs + qt * TR;
+  x.nrows = min(TR, ql - qt * TR);
+  x.pos0 = ctx - ql + qt * TR;
   x.n_kv = (x.pos0 + x.nrows - 1) / kKeys + 1;
   x.ctx = ctx;
   return x;
 }
 
-template <typename T, int D>
+
+template <typename T, int D, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmq,
                       const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const PrefillArgs a,
                       const int n_items) {
-  using L = PLayout<D>;
+  static_assert(!PAIR || D == 128, "the pair form takes D = 128");
+  using L = PLayout<D, PAIR>;
   constexpr int NS = L::NS;
+  constexpr int TR = PAIR ? 2 * kRows : kRows;  // query rows of a work item
   constexpr bool kBf16 = DT<T>::code == IR_DTYPE_BF16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -166,8 +193,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = o_free + 1;
   uint64_t* ref_full = drain + 1;     // [2] the reference max after tile g is in sref[g & 1]
   uint64_t* l_ready = ref_full + 2;   // the other warpgroup's row sums are in lsum
+  uint64_t* v_last = l_ready + 1;     // pair: this CTA's V half of an item's last tile landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::off_misc);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const bool lead = rank == 0;  // issues the MMAs (always, without a pair)
+  // the items are dealt over CTAs, or over pairs
+  const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  constexpr uint32_t kBoth = PAIR ? 2u : 1u;  // CTAs whose stage bytes rank 0 counts
+  // Fewer commits per tile (each costs the MMA thread about as much as an
+  // MMA): with a 2-stage ring, a K stage is free once the Q.K^T of the tile
+  // two back completed (S full) and a V stage and an S buffer once a P.V did
+  // (P.V done), so those barriers stand in for K empty, V empty and S free.
+  // No phase can alias: the next phase of each needs a tile that the waiter
+  // itself has not loaded (or issued) yet.
+  constexpr bool kLean = NS == 2;
+  // arrivals on P full / O free: every softmax thread of the CTA (of both CTAs
+  // of a pair)
+  constexpr uint32_t kSoftArrivals = kBoth * kWgThreads;
 
   if (threadIdx.x == 32) {
     mbar_init(q_full, 1);
@@ -183,13 +227,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s_free[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&p_full[i], kWgThreads);
+      mbar_init(&p_full[i], kSoftArrivals);
       mbar_init(&p_done[i], 1);
       mbar_init(&ref_full[i], kWgThreads);
     }
-    mbar_init(o_free, kWgThreads);
+    mbar_init(o_free, kSoftArrivals);
     mbar_init(drain, 1);
     mbar_init(l_ready, kWgThreads);
+    mbar_init(v_last, 1);
     fence_mbar_init();
   }
   if (threadIdx.x == 64) {
@@ -197,32 +242,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tensormap(&tmk);
     prefetch_tensormap(&tmv);
   }
-  if (warp == 0) tc::alloc(tmem_slot, kTmemCols);
+  // both CTAs of a pair have initialised their barriers before either signals
+  // the other's, and both are running before the pair allocates
+  if constexpr (PAIR) cluster_sync();
+  if (warp == 0) {
+    if constexpr (PAIR)
+      tc::alloc2(tmem_slot, kTmemCols);  // warp 0 of both CTAs: the same columns in each
+    else
+      tc::alloc(tmem_slot, kTmemCols);
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   // Every role walks the same items in the same order; g counts the CTA's
   // K/V tiles over all its items (ring stages and S buffers follow g), ii
-  // its items (Q buffer and O accumulator phases follow ii).
+  // its items (Q buffer, O accumulator and v_last phases follow ii).
 
   if (warp == 8 || warp == 9) {
     // ---------------------------------------------------------- producers
     // Warp 8 loads Q and fills the K ring, warp 9 the V ring, so K tiles run
     // ahead of the V waits. Lane i < nbox resolves box i of a tile
     // (block-table lookup) one tile ahead and issues that box's copies.
+    // In a pair, rank 0 posts the bytes of both CTAs on its full barriers
+    // and both CTAs' copies complete there.
     const bool is_k = warp == 8;
     uint64_t* full = is_k ? k_full : v_full;
     uint64_t* empty = is_k ? k_empty : v_empty;
     const CUtensorMap* tm = is_k ? &tmk : &tmv;
     uint8_t* ring = smem + (is_k ? L::off_k : L::off_v);
-    const int R = a.bs < kKeys ? a.bs : kKeys;  // rows per box
-    const int nbox = kKeys / R;                 // <= 16
+    const int side = is_k ? L::kKSide : L::kVSide;
+    const int span = is_k ? L::kKRows : kKeys;  // keys of a tile staged here
+    const int first = is_k ? static_cast<int>(rank) * L::kKRows : 0;  // the first of them
+    // 64-column halves staged here: all for K; for V one per CTA of a pair
+    const int half0 = is_k ? 0 : static_cast<int>(rank);  // the first of them
+    const int halfb = span * 128;                        // bytes of one staged half
+    const int R = a.bs < span ? a.bs : span;             // rows per box
+    const int nbox = span / R;                           // <= 16
     const int oob = static_cast<int>(a.num_slots);  // read as zeros by the copy
     bool ok = true;
     int g = 0, ii = 0;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-      const Item x = item_of(a, it, lane);
+    int g_prev = -1;  // the previous item's last tile
+    for (int it = unit; it < n_items && ok; it += units) {
+      const Item x = item_of<TR>(a, it, lane);
       if (x.s == -1) break;
       if (x.s < 0) continue;
       // Q of this item, once the previous item's last Q.K^T has completed
@@ -232,17 +294,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) w = mbar_wait_bounded(q_empty, (ii & 1) ^ 1) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, w, 0)) return false;
         if (lane == 0) {
-          mbar_arrive_expect_tx(q_full, L::kQ);
+          const int qrow = x.r0 + static_cast<int>(rank) * kRows;
+          if constexpr (PAIR) {
+            if (lead) mbar_arrive_expect_tx(q_full, 2 * L::kQ);
+            const uint32_t cb = cluster_addr(q_full, 0);
 #pragma unroll
-          for (int hf = 0; hf < L::kHalves; ++hf)
-            tma_load_3d(smem + L::off_q + hf * L::kHalf, &tmq, q_full, 64 * hf, x.h, x.r0);
+            for (int hf = 0; hf < L::kHalves; ++hf)
+              tma_load_3d_pair(smem + L::off_q + hf * L::kHalf, &tmq, cb, 64 * hf, x.h, qrow);
+          } else {
+            mbar_arrive_expect_tx(q_full, L::kQ);
+#pragma unroll
+            for (int hf = 0; hf < L::kHalves; ++hf)
+              tma_load_3d(smem + L::off_q + hf * L::kHalf, &tmq, q_full, 64 * hf, x.h, qrow);
+          }
         }
         return true;
       };
       const int32_t* btr = a.block_tables + static_cast<int64_t>(x.s) * a.bt_stride;
       auto row_of = [&](int j) {
         if (lane >= nbox || j >= x.n_kv) return oob;
-        const int key0 = j * kKeys + lane * R;
+        const int key0 = j * kKeys + first + lane * R;
         if (key0 >= x.ctx) return oob;
         const int id = btr[key0 / a.bs];
         if (id < 0 || id >= a.num_blocks) {
@@ -255,20 +326,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < x.n_kv; ++j, ++g) {
         const int row_next = row_of(j + 1);
         const int st = g % NS;
+        // a pair's V half of the item's last tile completes on this CTA's own
+        // v_last, so that its softmax can zero the rows past the context
+        // before the P.V reads them (rank 0's full barrier then only counts
+        // the phase; P full covers the data)
+        const bool last_v = PAIR && !is_k && j == x.n_kv - 1;
         int w = 1;
-        if (lane == 0) w = mbar_wait_bounded(&empty[st], ((g / NS) & 1) ^ 1) ? 1 : 0;
+        if (lane == 0) {
+          if (!kLean)
+            w = mbar_wait_bounded(&empty[st], ((g / NS) & 1) ^ 1) ? 1 : 0;
+          else if (g >= NS)
+            w = (is_k ? mbar_wait_bounded(&s_full[(g - NS) % kSBuf], ((g - NS) / kSBuf) & 1)
+                      : mbar_wait_bounded(&p_done[(g - NS) & 1], ((g - NS) >> 1) & 1))
+                    ? 1
+                    : 0;
+          // v_last takes its next phase only after the P.V of the previous
+          // item's last tile (whose softmax waited on the previous phase)
+          // completed; a wait the ring wait above already implies is skipped
+          if (w && last_v && g_prev >= 0 && g - g_prev < NS)
+            w = (kLean ? mbar_wait_bounded(&p_done[g_prev & 1], (g_prev >> 1) & 1)
+                       : mbar_wait_bounded(&empty[g_prev % NS], (g_prev / NS) & 1))
+                    ? 1
+                    : 0;
+        }
         if (!__shfl_sync(0xffffffffu, w, 0)) {
           ok = false;
           break;
         }
         // lane i issues the copies of box i (the expected bytes are posted first)
-        if (lane == 0) mbar_arrive_expect_tx(&full[st], L::kSide);
+        if (lane == 0) {
+          if (last_v) {
+            mbar_arrive_expect_tx(v_last, side);
+            if (lead) mbar_arrive(&full[st]);
+          } else if (lead) {
+            mbar_arrive_expect_tx(&full[st], kBoth * side);
+          }
+        }
         __syncwarp();
         if (lane < nbox) {
-          uint8_t* dst = ring + st * L::kSide + lane * R * 128;
+          uint8_t* dst = ring + st * side + lane * R * 128;
+          const uint32_t cb = PAIR ? cluster_addr(&full[st], 0) : 0u;
 #pragma unroll
-          for (int hf = 0; hf < L::kHalves; ++hf)
-            tma_load_3d(dst + hf * (kKeys * 128), tm, &full[st], 64 * hf, x.kvh, row_cur);
+          for (int hf = 0; hf < (is_k ? L::kHalves : L::kVHalves); ++hf) {
+            const int col = 64 * (half0 + hf);
+            if (!PAIR)
+              tma_load_3d(dst + hf * halfb, tm, &full[st], col, x.kvh, row_cur);
+            else if (last_v)
+              tma_load_3d(dst + hf * halfb, tm, v_last, col, x.kvh, row_cur);
+            else
+              tma_load_3d_pair(dst + hf * halfb, tm, cb, col, x.kvh, row_cur);
+          }
         }
         row_cur = row_next;
         if (is_k && j == 0 && !load_q()) {
@@ -277,62 +384,115 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
       }
+      g_prev = g - 1;
       ++ii;
     }
     if (lane == 0) {
       if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
-      // no copy may still be writing when the CTA ends
-      if (is_k && ii > 0) mbar_wait_bounded(q_full, (ii - 1) & 1);
-      for (int j = g > NS ? g - NS : 0; j < g; ++j) mbar_wait_bounded(&full[j % NS], (j / NS) & 1);
+      // no copy may still be writing when the CTA ends: rank 0's full
+      // barriers count both CTAs' copies (a pair leaves together)
+      if (lead) {
+        if (is_k && ii > 0) mbar_wait_bounded(q_full, (ii - 1) & 1);
+        for (int j = g > NS ? g - NS : 0; j < g; ++j)
+          mbar_wait_bounded(&full[j % NS], (j / NS) & 1);
+      }
+      if (PAIR && !is_k && ii > 0) mbar_wait_bounded(v_last, (ii - 1) & 1);
     }
   } else if (warp == 10) {
     // ---------------------------------------------------------- MMA issuer
+    // (rank 0 of a pair issues for both CTAs; rank 1's warp idles)
+    auto mma_ss = [](uint32_t d, uint64_t ad, uint64_t bd, uint32_t id, bool acc) {
+      if constexpr (PAIR)
+        tc::mma2_f16_ss(d, ad, bd, id, acc);
+      else
+        tc::mma_f16_ss(d, ad, bd, id, acc);
+    };
+    auto mma_ts = [](uint32_t d, uint32_t at, uint64_t bd, uint32_t id, bool acc) {
+      if constexpr (PAIR)
+        tc::mma2_f16_ts(d, at, bd, id, acc);
+      else
+        tc::mma_f16_ts(d, at, bd, id, acc);
+    };
+    // signal a barrier in both CTAs of a pair, or in rank 0 only
+    auto commit_both = [](uint64_t* bar) {
+      if constexpr (PAIR)
+        tc::commit2(bar, 3);
+      else
+        tc::commit(bar);
+    };
+    auto commit_lead = [](uint64_t* bar) {
+      if constexpr (PAIR)
+        tc::commit2(bar, 1);
+      else
+        tc::commit(bar);
+    };
+    // P full / O free collect arrivals from both CTAs of a pair; the item's
+    // last P follows shared-memory writes of the peer (zeroed V rows) released
+    // at cluster scope, so that wait acquires at cluster scope
+    auto wait_both = [](uint64_t* bar, uint32_t par, bool cluster_scope) {
+      return PAIR && cluster_scope ? mbar_wait_bounded_cluster(bar, par)
+                                   : mbar_wait_bounded(bar, par);
+    };
     const uint32_t qb = smem_u32(smem + L::off_q);
-    constexpr uint32_t kIdS = tc::idesc_f16(kRows, kKeys, kBf16, false);
-    constexpr uint32_t kIdO = tc::idesc_f16(kRows, D, kBf16, true);
+    constexpr uint32_t kIdS = tc::idesc_f16(PAIR ? 2 * kRows : kRows, kKeys, kBf16, false);
+    constexpr uint32_t kIdO = tc::idesc_f16(PAIR ? 2 * kRows : kRows, D, kBf16, true);
     bool ok = true;
     int g = 0, ii = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-      const Item x = item_of(a, it, lane);
+    int last_pv = -1;  // the last tile whose P.V has been issued
+    for (int it = unit; it < n_items && lead; it += units) {
+      const Item x = item_of<TR>(a, it, lane);
       if (x.s == -1) break;
       if (x.s < 0) continue;
       if (lane == 0) {
         auto issue_qk = [&](int gg, int j) -> bool {
           const int st = gg % NS, sb = gg % kSBuf;
           if (!mbar_wait_bounded(&k_full[st], (gg / NS) & 1)) return false;
-          if (!mbar_wait_bounded(&s_free[sb], ((gg / kSBuf) & 1) ^ 1)) return false;
+          if (!kLean) {
+            if (!mbar_wait_bounded(&s_free[sb], ((gg / kSBuf) & 1) ^ 1)) return false;
+          } else if (gg >= kSBuf) {
+            // S buffer sb held the P of tile gg - 3, read by its P.V; when the
+            // P.V of gg - 1 (the same P.V-done slot, one phase later) has been
+            // issued too (an item's first tile), wait for that one instead,
+            // which implies the other
+            const int t = last_pv >= gg - 1 ? gg - 1 : gg - kSBuf;
+            if (!mbar_wait_bounded(&p_done[t & 1], (t >> 1) & 1)) return false;
+          }
           tc::fence_after_sync();
-          const uint32_t kb = smem_u32(smem + L::off_k + st * L::kSide);
+          const uint32_t kb = smem_u32(smem + L::off_k + st * L::kKSide);
 #pragma unroll
           for (int k = 0; k < D / 16; ++k) {
             const uint32_t qo = (k >> 2) * L::kHalf + (k & 3) * 32;
-            const uint32_t ko = (k >> 2) * (kKeys * 128) + (k & 3) * 32;
-            tc::mma_f16_ss(tmem + sb * kKeys, tc::sw128_desc(qb + qo, 16, 1024),
-                           tc::sw128_desc(kb + ko, 16, 1024), kIdS, k > 0);
+            const uint32_t ko = (k >> 2) * L::kKHalf + (k & 3) * 32;
+            mma_ss(tmem + sb * kKeys, tc::sw128_desc(qb + qo, 16, 1024),
+                   tc::sw128_desc(kb + ko, 16, 1024), kIdS, k > 0);
           }
-          tc::commit(&s_full[sb]);
-          tc::commit(&k_empty[st]);
-          if (j == x.n_kv - 1) tc::commit(q_empty);  // the item's Q is no longer read
+          commit_both(&s_full[sb]);
+          if (!kLean) commit_both(&k_empty[st]);
+          if (j == x.n_kv - 1) commit_both(q_empty);  // the item's Q is no longer read
           return true;
         };
         auto issue_pv = [&](int gg, int j) -> bool {
           const int st = gg % NS, b = gg & 1, sb = gg % kSBuf;
-          // the previous item's O has been read before this item's first P.V
-          if (j == 0 && !mbar_wait_bounded(o_free, (ii & 1) ^ 1)) return false;
+          // the previous item's O has been read before this item's first P.V;
+          // P full is checked before V full: the P of tile gg + 2 (same slot)
+          // cannot complete the slot's next phase this soon after Q.K^T of gg + 2
+          if (j == 0 && !wait_both(o_free, (ii & 1) ^ 1, false)) return false;
+          if (!wait_both(&p_full[b], (gg >> 1) & 1, j == x.n_kv - 1)) return false;
           if (!mbar_wait_bounded(&v_full[st], (gg / NS) & 1)) return false;
-          if (!mbar_wait_bounded(&p_full[b], (gg >> 1) & 1)) return false;
           tc::fence_after_sync();
-          const uint32_t vb = smem_u32(smem + L::off_v + st * L::kSide);
+          const uint32_t vb = smem_u32(smem + L::off_v + st * L::kVSide);
           // P (16-bit, two keys per column) sits in columns 64..127 of S buffer sb
           const uint32_t pt = tmem + sb * kKeys + 64;
 #pragma unroll
           for (int k = 0; k < kKeys / 16; ++k)
-            tc::mma_f16_ts(tmem + kColO, pt + k * 8,
-                           tc::sw128_desc(vb + k * 2048, kKeys * 128, 1024), kIdO,
-                           j > 0 || k > 0);
-          tc::commit(&p_done[b]);
-          tc::commit(&v_empty[st]);
-          tc::commit(&s_free[sb]);  // S buffer sb (holding P) may take Q.K^T again
+            mma_ts(tmem + kColO, pt + k * 8, tc::sw128_desc(vb + k * 2048, kKeys * 128, 1024),
+                   kIdO, j > 0 || k > 0);
+          commit_both(&p_done[b]);
+          last_pv = gg;
+          if (!kLean) {
+            commit_both(&v_empty[st]);
+            commit_lead(&s_free[sb]);  // S buffer sb (holding P) may take Q.K^T again
+          }
           return true;
         };
         // Q.K^T of tile j + 2 is queued ahead of P.V of tile j: the next S
@@ -352,10 +512,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       g += x.n_kv;
       ++ii;
     }
-    if (lane == 0) {
+    if (lead && lane == 0) {
       if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
       // every MMA issued has completed before the tensor memory is freed
-      tc::commit(drain);
+      // (and, in a pair, before either CTA's shared memory goes away)
+      commit_lead(drain);
       mbar_wait_bounded(drain, 0);
     }
   } else {
@@ -371,12 +532,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     // after reading slot g & 1.) Each warpgroup keeps its own row sums; at the
     // end of an item the other warpgroup hands its sums to the warpgroup of
     // the item's last tile through lsum / l_ready, and that one normalises
-    // and writes the item's rows and releases O.
+    // and writes the item's rows and releases O. In a pair, rank c's thread r
+    // owns item row 128c + r, and the P full / O free arrivals go to rank 0.
     const int wg = warp >> 2;
     const int r = threadIdx.x & (kRows - 1);  // query row = TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     float* sref = reinterpret_cast<float*>(smem + L::off_ref);  // [2][128]
     float* lsum = sref + 2 * kRows;                              // [128]
+    const int rbase = static_cast<int>(rank) * kRows;  // this CTA's first row of an item
+    const uint32_t c_pfull0 = PAIR ? cluster_addr(&p_full[0], 0) : 0u;
+    const uint32_t c_pfull1 = PAIR ? cluster_addr(&p_full[1], 0) : 0u;
+    const uint32_t c_ofree = PAIR ? cluster_addr(o_free, 0) : 0u;
+    // In a pair every softmax thread arrives on rank 0's barrier: P and O live
+    // in tensor memory, ordered by tcgen05.fence::before_thread_sync, and a
+    // CTA-scope release hands them over; only a tile whose V rows this
+    // thread zeroed in shared memory releases at cluster scope
+    auto arrive_p_full = [&](int b, bool wrote_smem) {
+      if constexpr (PAIR) {
+        const uint32_t cb = b ? c_pfull1 : c_pfull0;
+        if (wrote_smem)
+          mbar_arrive_cluster(cb);
+        else
+          mbar_arrive_remote(cb);
+      } else {
+        mbar_arrive(&p_full[b]);
+      }
+    };
+    auto arrive_o_free = [&]() {
+      if constexpr (PAIR)
+        mbar_arrive_remote(c_ofree);
+      else
+        mbar_arrive(o_free);
+    };
     bool ok = true;
     // tcgen05.ld / st are warp-collective: every wait result is warp-uniform;
     // after a failed wait the remaining waits are skipped (arrivals go on), so
@@ -424,14 +611,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::st32(lane_addr + col, pk);  // waits for the store
     };
     int g = 0, ii = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-      const Item x = item_of(a, it, lane);
+    for (int it = unit; it < n_items; it += units) {
+      const Item x = item_of<TR>(a, it, lane);
       if (x.s == -1) break;
       if (x.s < 0) {
         if (threadIdx.x == 0) set_err(a.err, IR_DEVERR_CONTEXT_LEN);
         continue;
       }
-      const int pos = x.pos0 + r;
+      const int pos = x.pos0 + rbase + r;
       const int lim = min(pos, x.ctx - 1);  // last key this row may attend
       const int gl = g + x.n_kv - 1;        // the item's last tile
       float l = 0.f;           // this warpgroup's part of the row sum, relative to m_l
@@ -499,25 +686,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::ld64(lane_addr + sb * kKeys, v);
         mask(v, k0, lim);
         exp_store(v, pcol, nm2, s2);
-        if (j == x.n_kv - 1 && k0 + r >= x.ctx) {
-          // key row r of the last tile lies past the context: zero its V row
-          // so that 0 * (stale pool bits) cannot reach the output
-          if (ok && mbar_wait_bounded(&v_full[gg % NS], (gg / NS) & 1)) {
+        bool zeroed = false;
+        if (j == x.n_kv - 1) {
+          // key row r of the last tile past the context: zero its V row (this
+          // CTA's columns) so that 0 * (stale pool bits) cannot reach the output
+          const int vst = gg % NS;
+          bool landed;
+          if constexpr (PAIR)
+            landed = wait_all(v_last, ii & 1);
+          else
+            landed = __any_sync(0xffffffffu, k0 + r >= x.ctx) &&
+                     wait_all(&v_full[vst], (gg / NS) & 1);
+          if (landed && k0 + r >= x.ctx) {
+            zeroed = true;
 #pragma unroll
-            for (int h = 0; h < L::kHalves; ++h) {
-              uint8_t* vrow = smem + L::off_v + (gg % NS) * L::kSide + h * (kKeys * 128) +
+            for (int h = 0; h < L::kVHalves; ++h) {
+              uint8_t* vrow = smem + L::off_v + vst * L::kVSide + h * (kKeys * 128) +
                               (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
               for (int k = 0; k < 8; ++k)
                 *reinterpret_cast<uint4*>(vrow + k * 16) = make_uint4(0, 0, 0, 0);
             }
-          } else {
-            ok = false;
           }
         }
         fence_proxy_async_shared();
         tc::fence_before_sync();
-        mbar_arrive(&p_full[b]);
+        arrive_p_full(b, zeroed);
         const float2 u0 = f2unpack(add2(s2[0], s2[1]));
         const float2 u1 = f2unpack(add2(s2[2], s2[3]));
         const float fl = m_l == m_use ? 1.f : ex2(m_l - m_use);  // 0 before the first tile
@@ -538,13 +732,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (wait_all(&p_done[gl & 1], (gl >> 1) & 1)) {
           tc::fence_after_sync();
           const float inv = 1.f / l_row;
-          T* dst = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(x.r0 + r) * a.out_stride +
+          T* dst = reinterpret_cast<T*>(a.out) +
+                   static_cast<int64_t>(x.r0 + rbase + r) * a.out_stride +
                    static_cast<int64_t>(x.h) * D;
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
             float o[32];
             tc::ld32(lane_addr + kColO + c * 32, o);  // whole warp (collective)
-            if (r < x.nrows) {
+            if (rbase + r < x.nrows) {
 #pragma unroll
               for (int d = 0; d < 32; d += 8) {
                 uint4 w;
@@ -559,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc::fence_before_sync();
         }
-        mbar_arrive(o_free);  // the next item's first P.V may overwrite O
+        arrive_o_free();  // the next item's first P.V may overwrite O
       }
       g += x.n_kv;
       ++ii;
@@ -568,42 +763,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_before_sync();
   }
   __syncthreads();
+  // neither CTA of a pair leaves while its peer may still signal its
+  // barriers, read its shared memory or write its tensor memory
+  if constexpr (PAIR) cluster_sync();
   if (warp == 0) {
     tc::fence_after_sync();
-    tc::dealloc(tmem, kTmemCols);
+    if constexpr (PAIR)
+      tc::dealloc2(tmem, kTmemCols);
+    else
+      tc::dealloc(tmem, kTmemCols);
   }
 }
 
-template <typename T, int D>
+
+template <typename T, int D, bool PAIR>
 int launch_t(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
-             const PrefillArgs& a, int n_items, int ctas, cudaStream_t stream) {
-  using L = PLayout<D>;
+             const PrefillArgs& a, int n_items, int sm_count, cudaStream_t stream) {
+  using L = PLayout<D, PAIR>;
   static_assert(L::kAlloc <= 227 * 1024, "shared memory budget");
-  auto kern = prefill_tc_kernel<T, D>;
+  auto kern = prefill_tc_kernel<T, D, PAIR>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
   if (e != cudaSuccess) return static_cast<int>(e);
-  kern<<<ctas, kThreads, L::kAlloc, stream>>>(tmq, tmk, tmv, a, n_items);
-  return static_cast<int>(cudaGetLastError());
+  if constexpr (!PAIR) {
+    // one persistent CTA per SM
+    const int ctas = n_items < sm_count ? n_items : sm_count;
+    kern<<<ctas, kThreads, L::kAlloc, stream>>>(tmq, tmk, tmv, a, n_items);
+    return static_cast<int>(cudaGetLastError());
+  } else {
+    // one persistent pair per pair of SMs that can hold one at a time
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = L::kAlloc;
+    cfg.stream = stream;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(sm_count & ~1));
+    static int resident = 0;  // pairs the device holds at once (asked once)
+    int clusters = resident;
+    if (clusters <= 0) {
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+        (void)cudaGetLastError();
+        clusters = sm_count / 2;
+      } else {
+        resident = clusters;
+      }
+    }
+    const int pairs = n_items < clusters ? n_items : clusters;
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    e = cudaLaunchKernelEx(&cfg, kern, tmq, tmk, tmv, a, n_items);
+    return static_cast<int>(e);
+  }
 }
 
 }  // namespace
 
 int launch_prefill_tc(const CUtensorMap& tmq, const CUtensorMap& tmk, const CUtensorMap& tmv,
-                      const PrefillArgs& a, int dtype, int sm_count, cudaStream_t stream) {
+                      const PrefillArgs& a, int dtype, int sm_count, bool pair,
+                      cudaStream_t stream) {
   // items: an upper bound of the q tiles (every sequence adds at most one
-  // partial tile) times the heads; one persistent CTA per SM walks them
-  const int64_t tiles = (a.total_q + kRows - 1) / kRows + a.S;
+  // partial tile) times the heads; persistent CTAs (or pairs) walk them
+  const int tr = pair ? 2 * kRows : kRows;
+  const int64_t tiles = (a.total_q + tr - 1) / tr + a.S;
   const int64_t items = tiles * a.H;
   if (items == 0) return 0;
   if (items > INT32_MAX) return static_cast<int>(cudaErrorInvalidValue);
-  const int ctas = static_cast<int>(items < sm_count ? items : sm_count);
   const int n = static_cast<int>(items);
+  if (pair) {
+    if (a.D != 128) return static_cast<int>(cudaErrorInvalidValue);
+    return dtype == IR_DTYPE_BF16
+               ? launch_t<__nv_bfloat16, 128, true>(tmq, tmk, tmv, a, n, sm_count, stream)
+               : launch_t<__half, 128, true>(tmq, tmk, tmv, a, n, sm_count, stream);
+  }
   if (dtype == IR_DTYPE_BF16)
-    return a.D == 128 ? launch_t<__nv_bfloat16, 128>(tmq, tmk, tmv, a, n, ctas, stream)
-                      : launch_t<__nv_bfloat16, 64>(tmq, tmk, tmv, a, n, ctas, stream);
-  return a.D == 128 ? launch_t<__half, 128>(tmq, tmk, tmv, a, n, ctas, stream)
-                    : launch_t<__half, 64>(tmq, tmk, tmv, a, n, ctas, stream);
+    return a.D == 128 ? launch_t<__nv_bfloat16, 128, false>(tmq, tmk, tmv, a, n, sm_count, stream)
+                      : launch_t<__nv_bfloat16, 64, false>(tmq, tmk, tmv, a, n, sm_count, stream);
+  return a.D == 128 ? launch_t<__half, 128, false>(tmq, tmk, tmv, a, n, sm_count, stream)
+                    : launch_t<__half, 64, false>(tmq, tmk, tmv, a, n, sm_count, stream);
 }
 
 }  // namespace irb

@@ -4,7 +4,12 @@
 //
 // Conventions used by the kernels of this library:
 //  * one MMA shape family: kind::f16 (bf16 or fp16 operands, fp32
-//    accumulate), cta_group::1, M = 128 (D row m = TMEM lane m);
+//    accumulate), cta_group::1, M = 128 (D row m = TMEM lane m); or
+//    cta_group::2, M = 256 over a CTA pair (cluster ranks 0 and 1): rank c
+//    holds A rows 128c..128c+127 and D rows likewise in its own TMEM lanes,
+//    and B columns (N) N/2·c..N/2·c+N/2-1 in its own shared memory at the
+//    same offsets as its peer; rank 0 issues the MMA for both. A kernel uses
+//    one cta_group throughout (alloc, mma, commit, dealloc);
 //  * operand tiles in shared memory use the 128-byte swizzle: rows of 128 B
 //    (64 16-bit elements), 8-row atoms of 1024 B, atoms 1024-byte aligned —
 //    exactly the layout a TMA copy with CU_TENSOR_MAP_SWIZZLE_128B writes.
@@ -168,6 +173,55 @@ __device__ __forceinline__ void st32(uint32_t taddr, const float (&v)[32]) {
       "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
+}
+
+
+// ---------------------------------------------------------------- CTA pairs
+// cta_group::2 forms (see the conventions above). Issued by rank 0 only,
+// except alloc / dealloc, which the same warp of both CTAs executes.
+
+__device__ __forceinline__ void mma2_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma2_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Arrive (once) on the mbarrier at `bar`'s offset in every CTA of the pair
+// whose bit is set in `cta_mask` (1: rank 0, 2: rank 1, 3: both) when every
+// MMA this thread issued so far completes.
+__device__ __forceinline__ void commit2(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
+__device__ __forceinline__ void alloc2(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr),
+               "r"(ncols)
+               : "memory");
 }
 
 }  // namespace tc

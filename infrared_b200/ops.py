@@ -642,7 +642,8 @@ def lse_merge(o_parts: torch.Tensor, lse_parts: torch.Tensor,
 
 
 def set_prefill_path(path: int) -> None:
-    """0 auto, 1 rows as decode rows, 2 the tcgen05 tensor-core kernel."""
+    """0 auto, 1 rows as decode rows, 2 the tcgen05 tensor-core kernel, 3 its
+    CTA-pair form (head_dim 128, cta_group::2; only on request)."""
     check(_lib.load().ir_set_prefill_path(int(path)))
 
 

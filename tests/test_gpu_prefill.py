@@ -2,7 +2,9 @@
 
 Bars: fp32 within 1e-5 max-abs of the reference's own golden outputs; bf16 /
 fp16 within atol = rtol = 2e-2 of the fp32 oracle on the same rounded
-inputs, on both kernels (tcgen05 tensor cores and rows-as-decode).
+inputs, on every kernel form: tcgen05 tensor cores (path 2), the CTA-pair
+tensor-core form (path 3, cta_group::2, head_dim 128) and rows-as-decode
+(path 1).
 """
 
 import numpy as np
@@ -46,11 +48,13 @@ def test_prefill_golden_fp32(golden, name):
     assert np.abs(host_f32(out) - golden[f"prefill/{name}/out"]).max() <= 1e-5
 
 
-@pytest.mark.parametrize("path", [2, 1])
+@pytest.mark.parametrize("path", [2, 3, 1])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("name", sorted(cases.PREFILL_CASES))
 def test_prefill_golden_half(name, dtype, path):
     c = cases.prefill_inputs(name)
+    if path == 3 and c["q"].shape[-1] != 128:
+        pytest.skip("the CTA-pair form takes head_dim 128")
     q, kp, vp, bt, ctx, qs = _device_case(c, dtype)
     ops.set_prefill_path(path)
     assert ops.prefill_plan(q, kp, bt, qs, c["bs"])[0] == path
@@ -95,13 +99,17 @@ SWEEP = [
 ]
 
 
+@pytest.mark.parametrize("path", [2, 3])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("cfg", SWEEP)
-def test_prefill_sweep_tensor_cores(cfg, dtype):
+def test_prefill_sweep_tensor_cores(cfg, dtype, path):
     h, hkv, d, bs, chunks = cfg
+    if path == 3 and d != 128:
+        pytest.skip("the CTA-pair form takes head_dim 128")
     q, kp, vp, bt, ctx, qs, bt_np, ctx_np, qs_np = _random_frame(7 + h + d + bs, h, hkv, d, bs,
                                                                  chunks, dtype)
-    assert ops.prefill_plan(q, kp, bt, qs, bs)[0] == 2
+    ops.set_prefill_path(path)
+    assert ops.prefill_plan(q, kp, bt, qs, bs)[0] == path
     scale = d ** -0.5
     out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, scale, bs)
     want = orc.prefill_from_tables(host_f32(q), host_f32(kp)[None], host_f32(vp)[None], 0,
@@ -136,6 +144,75 @@ def test_prefill_paths_agree_and_are_deterministic():
     ops.set_prefill_path(1)
     c = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.088, bs)
     assert (a.float() - c.float()).abs().max().item() < 2e-2
+    ops.set_prefill_path(3)
+    e = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.088, bs)
+    f = irb.paged_prefill(q, kp, vp, bt, ctx, qs, 0.088, bs)
+    assert torch.equal(e, f)
+    assert (a.float() - e.float()).abs().max().item() < 2e-2
+
+
+# (H, Hkv, bs, [(cached, forwarded), ...]) at head_dim 128: long prompts whose
+# 256-row pair items end ragged (both halves, one half, a lone row)
+PAIR_FRAMES = [
+    (28, 4, 16, [(0, 700), (37, 300), (0, 1), (5, 257), (0, 256)]),
+    (28, 4, 64, [(0, 1024), (900, 129)]),
+    (16, 2, 128, [(70, 513), (0, 255)]),
+    (8, 8, 8, [(3, 300)]),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("cfg", PAIR_FRAMES)
+def test_prefill_cta_pairs_long_prompts(cfg, dtype):
+    """The CTA-pair form on long prompts (on request; auto keeps the
+    single-CTA form): rows of both halves of every pair item against the
+    oracle (a sample of rows per sequence for the long ones), and close to
+    the single-CTA form."""
+    h, hkv, bs, chunks = cfg
+    d = 128
+    q, kp, vp, bt, ctx, qs, bt_np, ctx_np, qs_np = _random_frame(11 + h + bs, h, hkv, d, bs,
+                                                                 chunks, dtype)
+    assert ops.prefill_plan(q, kp, bt, qs, bs)[0] == 2
+    ops.set_prefill_path(3)
+    assert ops.prefill_plan(q, kp, bt, qs, bs)[0] == 3
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, d ** -0.5, bs)
+    qh, kh, vh = host_f32(q), host_f32(kp)[None], host_f32(vp)[None]
+    got = host_f32(out)
+    for s_i, (cached, ql) in enumerate(chunks):
+        r0 = int(qs_np[s_i])
+        rows = sorted({0, 1, 127, 128, 129, 255, 256, ql // 2, ql - 2, ql - 1} & set(range(ql)))
+        for r in rows:
+            want = orc.prefill_from_tables(qh[r0 + r:r0 + r + 1], kh, vh, 0, bt_np[s_i:s_i + 1],
+                                           np.array([cached + r + 1], np.int32),
+                                           np.array([0, 1], np.int32), bs, d ** -0.5, h // hkv)
+            assert_close_bf16(got[r0 + r:r0 + r + 1], want)
+    ops.set_prefill_path(2)
+    single = irb.paged_prefill(q, kp, vp, bt, ctx, qs, d ** -0.5, bs)
+    assert (out.float() - single.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("path", [2, 3])
+def test_prefill_stale_pool_rows_past_context_stay_out(path):
+    """Pool slots past a sequence's context inside its last block hold NaN:
+    no output row may see them (the kernels zero those V rows in shared
+    memory and mask those keys)."""
+    h, hkv, d, bs = 28, 4, 128, 16
+    chunks = [(0, 300), (13, 250), (0, 37)]
+    q, kp, vp, bt, ctx, qs, bt_np, ctx_np, qs_np = _random_frame(21, h, hkv, d, bs, chunks,
+                                                                 torch.bfloat16)
+    for s_i, n in enumerate(ctx_np):
+        last = int(bt_np[s_i, (int(n) - 1) // bs])
+        for pos in range(int(n), -(-int(n) // bs) * bs):
+            slot = last * bs + pos % bs
+            kp[slot] = float("nan")
+            vp[slot] = float("nan")
+    ops.set_prefill_path(path)
+    out = irb.paged_prefill(q, kp, vp, bt, ctx, qs, d ** -0.5, bs)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    want = orc.prefill_from_tables(host_f32(q), host_f32(kp)[None], host_f32(vp)[None], 0,
+                                   bt_np, ctx_np, qs_np, bs, d ** -0.5, h // hkv)
+    assert_close_bf16(host_f32(out), want)
 
 
 def test_prefill_bad_context_is_flagged_not_faulted():
