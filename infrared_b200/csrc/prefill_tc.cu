@@ -7,15 +7,17 @@
 // infrared/model/inputs.py:38-94 applied to infrared's paged read).
 //
 // Work item = 128 query rows of one sequence for one query head; one
-// persistent CTA per SM walks the items, longest first. Eleven warps:
+// persistent CTA per SM walks the items, longest first. Twelve warps:
 //   warps 8, 9  producers: TMA copies of the Q tile (once) and of each
 //               128-key K tile (warp 8) and V tile (warp 9), one box per
 //               block and 64-column half, into rings of NS stages; the
 //               block-table lookups are spread over the lanes and done one
 //               tile ahead;
-//   warp 10     MMA issuer (one thread): S = Q.K^T (M=128, N=128 keys,
-//               K=D) into one of three TMEM buffers, two tiles ahead, with
-//               Q and K from 128-byte-swizzled shared memory; and
+//   warps 10, 11 MMA issuers (one thread each, so that the tensor pipe
+//               overlaps the two streams): warp 10 issues S = Q.K^T (M=128,
+//               N=128 keys, K=D) into one of three TMEM buffers, up to two
+//               tiles ahead of the softmax, with Q and K from
+//               128-byte-swizzled shared memory; warp 11 issues
 //               O += P.V (M=128, N=D, K=128 keys) into the TMEM accumulator
 //               with P read from tensor memory (the A operand) and V from
 //               shared memory, tcgen05.mma kind::f16; tcgen05.commit
@@ -56,7 +58,8 @@ namespace {
 
 constexpr int kRows = 128;     // query rows per CTA (MMA M)
 constexpr int kKeys = 128;     // keys per K/V tile
-constexpr int kThreads = 352;  // warps 0-7 softmax (two warpgroups), 8-9 producers, 10 MMA
+// warps 0-7 softmax (two warpgroups), 8-9 producers, 10 Q.K^T issuer, 11 P.V issuer
+constexpr int kThreads = 384;
 constexpr int kWgThreads = 128;  // one softmax warpgroup: one thread per query row
 constexpr uint32_t kTmemCols = 512;
 constexpr int kSBuf = 3;  // S buffers: Q.K^T runs two tiles ahead of the softmax
@@ -202,12 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int unit = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int units = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   constexpr uint32_t kBoth = PAIR ? 2u : 1u;  // CTAs whose stage bytes rank 0 counts
-  // Fewer commits per tile (each costs the MMA thread about as much as an
-  // MMA): with a 2-stage ring, a K stage is free once the Q.K^T of the tile
-  // two back completed (S full) and a V stage and an S buffer once a P.V did
-  // (P.V done), so those barriers stand in for K empty, V empty and S free.
-  // No phase can alias: the next phase of each needs a tile that the waiter
-  // itself has not loaded (or issued) yet.
+  // Fewer commits per tile: with a 2-stage ring, a K stage is free once the
+  // Q.K^T of the tile two back completed (S full) and a V stage once its P.V
+  // did (P.V done), so those barriers stand in for K empty and V empty. No
+  // phase can alias: the next phase of each needs a tile that the waiting
+  // producer has not loaded yet.
   constexpr bool kLean = NS == 2;
   // arrivals on P full / O free: every softmax thread of the CTA (of both CTAs
   // of a pair)
@@ -232,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ref_full[i], kWgThreads);
     }
     mbar_init(o_free, kSoftArrivals);
-    mbar_init(drain, 1);
+    mbar_init(drain, 2);  // one commit from each MMA issuer
     mbar_init(l_ready, kWgThreads);
     mbar_init(v_last, 1);
     fence_mbar_init();
@@ -398,9 +400,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (PAIR && !is_k && ii > 0) mbar_wait_bounded(v_last, (ii - 1) & 1);
     }
-  } else if (warp == 10) {
-    // ---------------------------------------------------------- MMA issuer
-    // (rank 0 of a pair issues for both CTAs; rank 1's warp idles)
+  } else if (warp == 10 || warp == 11) {
+    // ---------------------------------------------------------- MMA issuers
+    // Warp 10 issues the Q.K^T MMAs and warp 11 the P.V MMAs (one thread
+    // each): MMAs issued from two threads overlap in the tensor pipe, where
+    // one thread's stream runs them one after the other (a 128 x 128 x 16
+    // Q.K^T + P.V pair: ~118 cycles from two threads, ~187 from one). Rank 0
+    // of a pair issues for both CTAs; rank 1's two warps idle.
+    const bool is_qk = warp == 10;
     auto mma_ss = [](uint32_t d, uint64_t ad, uint64_t bd, uint32_t id, bool acc) {
       if constexpr (PAIR)
         tc::mma2_f16_ss(d, ad, bd, id, acc);
@@ -438,25 +445,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kIdO = tc::idesc_f16(PAIR ? 2 * kRows : kRows, D, kBf16, true);
     bool ok = true;
     int g = 0, ii = 0;
-    int last_pv = -1;  // the last tile whose P.V has been issued
     for (int it = unit; it < n_items && lead; it += units) {
       const Item x = item_of<TR>(a, it, lane);
       if (x.s == -1) break;
       if (x.s < 0) continue;
-      if (lane == 0) {
-        auto issue_qk = [&](int gg, int j) -> bool {
-          const int st = gg % NS, sb = gg % kSBuf;
-          if (!mbar_wait_bounded(&k_full[st], (gg / NS) & 1)) return false;
-          if (!kLean) {
-            if (!mbar_wait_bounded(&s_free[sb], ((gg / kSBuf) & 1) ^ 1)) return false;
-          } else if (gg >= kSBuf) {
-            // S buffer sb held the P of tile gg - 3, read by its P.V; when the
-            // P.V of gg - 1 (the same P.V-done slot, one phase later) has been
-            // issued too (an item's first tile), wait for that one instead,
-            // which implies the other
-            const int t = last_pv >= gg - 1 ? gg - 1 : gg - kSBuf;
-            if (!mbar_wait_bounded(&p_done[t & 1], (t >> 1) & 1)) return false;
-          }
+      if (lane == 0 && is_qk) {
+        // S = Q.K^T of each tile into S buffer g % 3, as soon as the K tile
+        // has landed and the P.V of the tile three back has read that buffer
+        ok = mbar_wait_bounded(q_full, ii & 1);
+        for (int j = 0; j < x.n_kv && ok; ++j) {
+          const int gg = g + j, st = gg % NS, sb = gg % kSBuf;
+          ok = mbar_wait_bounded(&k_full[st], (gg / NS) & 1) &&
+               mbar_wait_bounded(&s_free[sb], ((gg / kSBuf) & 1) ^ 1);
+          if (!ok) break;
           tc::fence_after_sync();
           const uint32_t kb = smem_u32(smem + L::off_k + st * L::kKSide);
 #pragma unroll
@@ -469,16 +470,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           commit_both(&s_full[sb]);
           if (!kLean) commit_both(&k_empty[st]);
           if (j == x.n_kv - 1) commit_both(q_empty);  // the item's Q is no longer read
-          return true;
-        };
-        auto issue_pv = [&](int gg, int j) -> bool {
-          const int st = gg % NS, b = gg & 1, sb = gg % kSBuf;
-          // the previous item's O has been read before this item's first P.V;
-          // P full is checked before V full: the P of tile gg + 2 (same slot)
-          // cannot complete the slot's next phase this soon after Q.K^T of gg + 2
-          if (j == 0 && !wait_both(o_free, (ii & 1) ^ 1, false)) return false;
-          if (!wait_both(&p_full[b], (gg >> 1) & 1, j == x.n_kv - 1)) return false;
-          if (!mbar_wait_bounded(&v_full[st], (gg / NS) & 1)) return false;
+        }
+      } else if (lane == 0) {
+        // O += P.V of each tile once its P is in tensor memory (and, at an
+        // item's first tile, the previous item's O has been read)
+        for (int j = 0; j < x.n_kv && ok; ++j) {
+          const int gg = g + j, st = gg % NS, b = gg & 1, sb = gg % kSBuf;
+          ok = (j > 0 || wait_both(o_free, (ii & 1) ^ 1, false)) &&
+               wait_both(&p_full[b], (gg >> 1) & 1, j == x.n_kv - 1) &&
+               mbar_wait_bounded(&v_full[st], (gg / NS) & 1);
+          if (!ok) break;
           tc::fence_after_sync();
           const uint32_t vb = smem_u32(smem + L::off_v + st * L::kVSide);
           // P (16-bit, two keys per column) sits in columns 64..127 of S buffer sb
@@ -488,21 +489,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_ts(tmem + kColO, pt + k * 8, tc::sw128_desc(vb + k * 2048, kKeys * 128, 1024),
                    kIdO, j > 0 || k > 0);
           commit_both(&p_done[b]);
-          last_pv = gg;
-          if (!kLean) {
-            commit_both(&v_empty[st]);
-            commit_lead(&s_free[sb]);  // S buffer sb (holding P) may take Q.K^T again
-          }
-          return true;
-        };
-        // Q.K^T of tile j + 2 is queued ahead of P.V of tile j: the next S
-        // never waits in the tensor pipe behind a P.V that waits for a softmax
-        ok = mbar_wait_bounded(q_full, ii & 1);
-        if (ok) ok = issue_qk(g, 0);
-        if (ok && x.n_kv > 1) ok = issue_qk(g + 1, 1);
-        for (int j = 0; j < x.n_kv && ok; ++j) {
-          if (j + 2 < x.n_kv) ok = issue_qk(g + j + 2, j + 2);
-          if (ok) ok = issue_pv(g + j, j);
+          commit_lead(&s_free[sb]);  // S buffer sb (holding P) may take Q.K^T again
+          if (!kLean) commit_both(&v_empty[st]);
         }
       }
       if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
@@ -515,7 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lead && lane == 0) {
       if (!ok) set_err(a.err, IR_DEVERR_TIMEOUT);
       // every MMA issued has completed before the tensor memory is freed
-      // (and, in a pair, before either CTA's shared memory goes away)
+      // (and, in a pair, before either CTA's shared memory goes away): the
+      // drain barrier counts both issuers' commits
       commit_lead(drain);
       mbar_wait_bounded(drain, 0);
     }
