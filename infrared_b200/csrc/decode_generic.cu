@@ -192,18 +192,61 @@ __global__ void __launch_bounds__(kGenThreads)
 template <typename T, int W>
 __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a) {
   launch_dependents();   // the next kernel may start its own prologue now
-  wait_prerequisites();  // the decode grid's pieces and prefix are complete
   __shared__ float4 s_acc[W][32];
   __shared__ float s_m[W], s_s[W];
+  __shared__ long long s_sum[W][3];
   const int kvh = blockIdx.x / a.n_rep, n = blockIdx.x % a.n_rep, b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t pb = a.ws_prefix[b];
-  const int64_t nb = a.ws_prefix[b + 1] - pb;
-  const int64_t total = a.ws_prefix[a.B];
+  const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
+  // The tile prefix this row's pieces follow from (the decode kernel's
+  // ws_prefix) depends on the context lengths alone: inputs complete before
+  // the decode grid let this grid start, so for batches one pass of this
+  // CTA's threads covers it is summed here while the decode still runs,
+  // taking a round trip off the wait below (larger batches read the decode
+  // kernel's prefix after the wait: most of their rows are not split, and
+  // their CTAs would sum the whole batch for nothing). Every CTA waits
+  // before it returns, so this grid never completes before the decode grid.
+  const bool early = a.B <= 32 * W;  // the same in every CTA of the grid
+  int64_t total = 0, pb = 0, p0 = 0, nb = 0;
+  if (early) {
+    long long below = 0, below0 = 0, all = 0;
+    if (static_cast<int>(threadIdx.x) < a.B) {
+      const int i = threadIdx.x;
+      const long long t = tiles_of(a, i);
+      all = t;
+      if (i < b) below = t;
+      if (i < b0) below0 = t;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      all += __shfl_xor_sync(0xffffffffu, all, o);
+      below += __shfl_xor_sync(0xffffffffu, below, o);
+      below0 += __shfl_xor_sync(0xffffffffu, below0, o);
+    }
+    if (lane == 0) {
+      s_sum[warp][0] = all;
+      s_sum[warp][1] = below;
+      s_sum[warp][2] = below0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      total += s_sum[w][0];
+      pb += s_sum[w][1];
+      p0 += s_sum[w][2];
+    }
+    nb = tiles_of(a, b);
+  }
+  wait_prerequisites();  // the decode grid's pieces and prefix are complete
+  if (!early) {
+    pb = a.ws_prefix[b];
+    nb = a.ws_prefix[b + 1] - pb;
+    total = a.ws_prefix[a.B];
+    p0 = a.ws_prefix[b0];
+  }
   if (nb <= 0) return;  // empty context: written by the decode kernel
   // the decode kernel's units (static shares, then dynamic units if any)
-  const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
-  const UnitPlan up = unit_plan(total, a.G, a.dyn, a.dyn ? a.ws_prefix[b0] : 0);
+  const UnitPlan up = unit_plan(total, a.G, a.dyn, a.dyn ? p0 : 0);
   const int glo = unit_of(up, pb);
   const int parts = unit_of(up, pb + nb - 1) - glo + 1;
   if (parts == 1) return;  // written whole by one unit
