@@ -208,6 +208,15 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
   // before it returns, so this grid never completes before the decode grid.
   const bool early = a.B <= 32 * W;  // the same in every CTA of the grid
   int64_t total = 0, pb = 0, p0 = 0, nb = 0;
+  // the decode kernel's units holding this row (static shares, then
+  // dynamic units if any)
+  int glo = 0, parts = 0;
+  auto find_units = [&]() {
+    if (nb <= 0) return;
+    const UnitPlan up = unit_plan(total, a.G, a.dyn, a.dyn ? p0 : 0);
+    glo = unit_of(up, pb);
+    parts = unit_of(up, pb + nb - 1) - glo + 1;
+  };
   if (early) {
     long long below = 0, below0 = 0, all = 0;
     if (static_cast<int>(threadIdx.x) < a.B) {
@@ -236,6 +245,7 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
       p0 += s_sum[w][2];
     }
     nb = tiles_of(a, b);
+    find_units();
   }
   wait_prerequisites();  // the decode grid's pieces and prefix are complete
   if (!early) {
@@ -243,12 +253,9 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
     nb = a.ws_prefix[b + 1] - pb;
     total = a.ws_prefix[a.B];
     p0 = a.ws_prefix[b0];
+    find_units();
   }
   if (nb <= 0) return;  // empty context: written by the decode kernel
-  // the decode kernel's units (static shares, then dynamic units if any)
-  const UnitPlan up = unit_plan(total, a.G, a.dyn, a.dyn ? p0 : 0);
-  const int glo = unit_of(up, pb);
-  const int parts = unit_of(up, pb + nb - 1) - glo + 1;
   if (parts == 1) return;  // written whole by one unit
   if (a.inline_merge && parts <= kInlineMax) return;  // merged in the decode kernel
   const int64_t base = static_cast<int64_t>(kvh) * a.ws_slots + glo + b;
