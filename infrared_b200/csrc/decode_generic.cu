@@ -188,7 +188,9 @@ __global__ void __launch_bounds__(kGenThreads)
 // log-sum-exp, each lane owning 4 consecutive head-dim columns (16-byte
 // loads), then the W warp states are combined through shared memory. The
 // pieces' loads are independent, so a merge costs a few L2 round trips even
-// when a sequence spans dozens of CTAs (W = 8 there, 4 otherwise).
+// when a sequence spans dozens of CTAs (W = 8 or 16 there; 4 for 4-7 pieces;
+// one warp below that, so that every merge CTA of a large grid fits beside
+// the decode CTAs and starts its row as soon as the decode grid ends).
 template <typename T, int W>
 __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a) {
   launch_dependents();   // the next kernel may start its own prologue now
@@ -200,13 +202,13 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
   const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
   // The tile prefix this row's pieces follow from (the decode kernel's
   // ws_prefix) depends on the context lengths alone: inputs complete before
-  // the decode grid let this grid start, so for batches one pass of this
-  // CTA's threads covers it is summed here while the decode still runs,
-  // taking a round trip off the wait below (larger batches read the decode
-  // kernel's prefix after the wait: most of their rows are not split, and
-  // their CTAs would sum the whole batch for nothing). Every CTA waits
-  // before it returns, so this grid never completes before the decode grid.
-  const bool early = a.B <= 32 * W;  // the same in every CTA of the grid
+  // the decode grid let this grid start, so for batches of up to 128
+  // sequences it is summed here while the decode still runs, taking a round
+  // trip off the wait below (larger batches read the decode kernel's prefix
+  // after the wait: most of their rows are not split, and their CTAs would
+  // sum the whole batch for nothing). Every CTA waits before it returns, so
+  // this grid never completes before the decode grid.
+  const bool early = a.B <= 128;  // the same in every CTA of the grid
   int64_t total = 0, pb = 0, p0 = 0, nb = 0;
   // the decode kernel's units holding this row (static shares, then
   // dynamic units if any)
@@ -219,12 +221,11 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
   };
   if (early) {
     long long below = 0, below0 = 0, all = 0;
-    if (static_cast<int>(threadIdx.x) < a.B) {
-      const int i = threadIdx.x;
+    for (int i = threadIdx.x; i < a.B; i += 32 * W) {
       const long long t = tiles_of(a, i);
-      all = t;
-      if (i < b) below = t;
-      if (i < b0) below0 = t;
+      all += t;
+      if (i < b) below += t;
+      if (i < b0) below0 += t;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -394,12 +395,14 @@ template <typename T>
 int launch_merge_w(const DecodeArgs& a, cudaStream_t s) {
   // a sequence of average length spans about G / B shares, and the rows of
   // the last kDynSeqs sequences also hold the dynamic units: with 8 or 16 or
-  // more pieces per row, 8 or 16 warps fold them in fewer rounds
+  // more pieces per row, 8 or 16 warps fold them in fewer rounds; with fewer
+  // than 4, one warp per row (measured: C2 +1.6 %, C3 +2.3 % against 4)
   const int b = a.B > 0 ? a.B : 1;
   const int tail = b < kDynSeqs ? b : kDynSeqs;
   const int pieces = a.G / b + (a.dyn ? kDynUnitsPerCta * a.G / tail : 0);
   if (pieces >= 16) return launch_merge_t<T, 16>(a, s);
-  return pieces >= 8 ? launch_merge_t<T, 8>(a, s) : launch_merge_t<T, 4>(a, s);
+  if (pieces >= 8) return launch_merge_t<T, 8>(a, s);
+  return pieces >= 4 ? launch_merge_t<T, 4>(a, s) : launch_merge_t<T, 1>(a, s);
 }
 
 int launch_split_merge(const DecodeArgs& a, int dtype, cudaStream_t s) {
