@@ -202,13 +202,13 @@ __global__ void __launch_bounds__(32 * W) split_merge_kernel(const DecodeArgs a)
   const int b0 = a.B > kDynSeqs ? a.B - kDynSeqs : 0;
   // The tile prefix this row's pieces follow from (the decode kernel's
   // ws_prefix) depends on the context lengths alone: inputs complete before
-  // the decode grid let this grid start, so for batches of up to 128
+  // the decode grid let this grid start, so for batches of up to 256
   // sequences it is summed here while the decode still runs, taking a round
   // trip off the wait below (larger batches read the decode kernel's prefix
   // after the wait: most of their rows are not split, and their CTAs would
   // sum the whole batch for nothing). Every CTA waits before it returns, so
   // this grid never completes before the decode grid.
-  const bool early = a.B <= 128;  // the same in every CTA of the grid
+  const bool early = a.B <= 256;  // the same in every CTA of the grid
   int64_t total = 0, pb = 0, p0 = 0, nb = 0;
   // the decode kernel's units holding this row (static shares, then
   // dynamic units if any)
