@@ -5,7 +5,8 @@
 // The generic kernel uses the same balanced tile shares and segment outputs
 // as the TMA kernel (decode_common.cuh), so one split merge serves both. A CTA
 // of 128 threads walks its tiles in order: it stages the 16 K and V rows of a
-// tile in shared memory (gathered row by row through the block table),
+// tile in shared memory (16-byte chunks gathered through the block table, the
+// next tile's chunks loaded into registers while the current one computes),
 // computes the 16 x group scores with fp32 dot products, updates the
 // per-head online softmax (exp2 with the scale folded into log2 units) and
 // accumulates P.V with each thread owning one head-dim column.
@@ -42,18 +43,129 @@ __global__ void __launch_bounds__(kGenThreads)
   const int d = tid % D, hg = tid / D;
   const T* kpool = reinterpret_cast<const T*>(a.k_pool);
   const T* vpool = reinterpret_cast<const T*>(a.v_pool);
-  float acc[NH];
-  int b = ri.b_first;
-  int64_t pb = ri.p_first;
-  int nb = tiles_of(a, b);
-  int cur_b = -1;
-
-  for (int64_t t = start; t < end; ++t) {
-    while (t >= pb + nb) {
-      pb += nb;
-      ++b;
-      nb = tiles_of(a, b);
+  // K and V rows move in 16-byte chunks: thread tid owns chunks tid,
+  // tid + 128, ... of each tile side, and the next tile's chunks are loaded
+  // into registers before the current tile is computed, so that the loads
+  // overlap the math. Pools that are not 16-byte aligned (the host sends
+  // those here too) are read element by element into the same chunks.
+  constexpr int EPC = 16 / static_cast<int>(sizeof(T));  // elements per chunk
+  constexpr int CPR = D / EPC;                            // chunks per row
+  constexpr int NCH = kTile * CPR;                        // chunks per tile side
+  constexpr int CPT = (NCH + kGenThreads - 1) / kGenThreads;
+  const bool vec = ((reinterpret_cast<uintptr_t>(kpool) |
+                     reinterpret_cast<uintptr_t>(vpool)) & 15) == 0;
+  uint4 kr[CPT], vr[CPT];
+  // the sequence (tile prefix pb, nb tiles) holding a tile
+  struct Cursor {
+    int b;
+    int64_t pb;
+    int nb;
+  };
+  auto advance = [&](Cursor& c, int64_t t) {
+    while (t >= c.pb + c.nb) {
+      c.pb += c.nb;
+      ++c.b;
+      c.nb = tiles_of(a, c.b);
     }
+  };
+  // the raw chunks of tile t: zero past the context, and for the new token of
+  // a fused cache write (filled in when the tile is stored)
+  auto load_tile = [&](const Cursor& c, int64_t t) {
+    const int tok0 = static_cast<int>(t - c.pb) * kTile;
+    const int ctx = clamp_ctx(a.context_lens[c.b], a);
+    const int32_t* btr = a.block_tables + c.b * a.bt_stride;
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) {
+      kr[k] = make_uint4(0, 0, 0, 0);
+      vr[k] = make_uint4(0, 0, 0, 0);
+      const int i = tid + k * kGenThreads;
+      if (i >= NCH) continue;
+      const int r = i / CPR, cc = i % CPR;
+      const int pos = tok0 + r;
+      if (pos >= ctx || (a.k_new != nullptr && pos == ctx - 1)) continue;
+      const int id = btr[pos / a.bs];
+      if (id >= 0 && id < a.num_blocks) {
+        const int64_t row = static_cast<int64_t>(id) * a.bs + pos % a.bs;
+        const int64_t off = (row * a.Hkv + kvh) * D + cc * EPC;
+        if (vec) {
+          kr[k] = *reinterpret_cast<const uint4*>(kpool + off);
+          vr[k] = *reinterpret_cast<const uint4*>(vpool + off);
+        } else {
+          T* kt = reinterpret_cast<T*>(&kr[k]);
+          T* vt = reinterpret_cast<T*>(&vr[k]);
+#pragma unroll
+          for (int e = 0; e < EPC; ++e) {
+            kt[e] = kpool[off + e];
+            vt[e] = vpool[off + e];
+          }
+        }
+      } else if (cc == 0) {
+        set_err(a.err, IR_DEVERR_BLOCK_ID);
+      }
+    }
+  };
+  // the chunks into shared memory as fp32; the new token of a fused cache
+  // write comes from the inputs (RoPE applied to K when given) and is stored
+  // into the pools here, by the thread that owns its chunk
+  auto store_tile = [&](const Cursor& c, int64_t t) {
+    const int tok0 = static_cast<int>(t - c.pb) * kTile;
+    const int ctx = clamp_ctx(a.context_lens[c.b], a);
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) {
+      const int i = tid + k * kGenThreads;
+      if (i >= NCH) continue;
+      const int r = i / CPR, cc = i % CPR;
+      T* kt = reinterpret_cast<T*>(&kr[k]);
+      T* vt = reinterpret_cast<T*>(&vr[k]);
+      const int pos = tok0 + r;
+      if (a.k_new != nullptr && pos < ctx && pos == ctx - 1) {
+        const T* kn = reinterpret_cast<const T*>(a.k_new);
+        const T* vn = reinterpret_cast<const T*>(a.v_new);
+        const int64_t src = c.b * a.kv_stride + static_cast<int64_t>(kvh) * D;
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) {
+          const int col = cc * EPC + e;
+          T x = kn[src + col];
+          if (a.rope_cos != nullptr) {
+            const int64_t rr = c.b * a.rope_stride + col;
+            x = DT<T>::from_f(rope_elem<T>(DT<T>::to_f(x), DT<T>::to_f(kn[src + (col + D / 2) % D]),
+                                           a.rope_cos[rr], a.rope_sin[rr], col >= D / 2));
+          }
+          kt[e] = x;
+          vt[e] = vn[src + col];
+        }
+        const int id = a.block_tables[c.b * a.bt_stride + pos / a.bs];
+        const int64_t sw = a.slot_mapping[c.b];
+        const int64_t want = static_cast<int64_t>(id) * a.bs + pos % a.bs;
+        if (cc == 0 && sw != want) set_err(a.err, IR_DEVERR_WRITE_SLOT);
+        if (sw >= 0 && sw < a.num_slots) {
+          const int64_t dst = (sw * a.Hkv + kvh) * D + cc * EPC;
+#pragma unroll
+          for (int e = 0; e < EPC; ++e) {
+            const_cast<T*>(kpool)[dst + e] = kt[e];
+            const_cast<T*>(vpool)[dst + e] = vt[e];
+          }
+        } else if (cc == 0 && sw >= a.num_slots) {
+          set_err(a.err, IR_DEVERR_SLOT);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < EPC; ++e) {
+        k_s[r][cc * EPC + e] = DT<T>::to_f(kt[e]);
+        v_s[r][cc * EPC + e] = DT<T>::to_f(vt[e]);
+      }
+    }
+  };
+  float acc[NH];
+  Cursor cur{ri.b_first, ri.p_first, tiles_of(a, ri.b_first)};
+  Cursor nxt = cur;
+  int cur_b = -1;
+  load_tile(cur, start);
+  for (int64_t t = start; t < end; ++t) {
+    advance(cur, t);
+    const int b = cur.b;
+    const int64_t pb = cur.pb;
+    const int nb = cur.nb;
     const int j = static_cast<int>(t - pb);
     const int tok0 = j * kTile;
     const int ctx = clamp_ctx(a.context_lens[b], a);
@@ -81,48 +193,11 @@ __global__ void __launch_bounds__(kGenThreads)
 #pragma unroll
       for (int k = 0; k < NH; ++k) acc[k] = 0.f;
     }
-    // stage the tile's K and V rows
-    const int32_t* btr = a.block_tables + b * a.bt_stride;
-    for (int i = tid; i < kTile * D; i += kGenThreads) {
-      const int r = i / D, c = i % D;
-      float kv = 0.f, vv = 0.f;
-      if (r < nvalid) {
-        const int pos = tok0 + r;
-        const int id = btr[pos / a.bs];
-        if (a.k_new != nullptr && pos == ctx - 1) {
-          // fused cache write: the new token's K/V come from the inputs
-          const int64_t src = b * a.kv_stride + static_cast<int64_t>(kvh) * D + c;
-          T kn = reinterpret_cast<const T*>(a.k_new)[src];
-          const T vn = reinterpret_cast<const T*>(a.v_new)[src];
-          if (a.rope_cos != nullptr) {
-            const T kp = reinterpret_cast<const T*>(a.k_new)[src - c + (c + D / 2) % D];
-            const int64_t r = b * a.rope_stride + c;
-            kn = DT<T>::from_f(rope_elem<T>(DT<T>::to_f(kn), DT<T>::to_f(kp), a.rope_cos[r],
-                                            a.rope_sin[r], c >= D / 2));
-          }
-          kv = DT<T>::to_f(kn);
-          vv = DT<T>::to_f(vn);
-          const int64_t sw = a.slot_mapping[b];
-          const int64_t want = static_cast<int64_t>(id) * a.bs + pos % a.bs;
-          if (c == 0 && sw != want) set_err(a.err, IR_DEVERR_WRITE_SLOT);
-          if (sw >= 0 && sw < a.num_slots) {
-            const int64_t dst = (sw * a.Hkv + kvh) * D + c;
-            const_cast<T*>(kpool)[dst] = kn;
-            const_cast<T*>(vpool)[dst] = vn;
-          } else if (c == 0 && sw >= a.num_slots) {
-            set_err(a.err, IR_DEVERR_SLOT);
-          }
-        } else if (id >= 0 && id < a.num_blocks) {
-          const int64_t row = static_cast<int64_t>(id) * a.bs + pos % a.bs;
-          const int64_t off = (row * a.Hkv + kvh) * D + c;
-          kv = DT<T>::to_f(kpool[off]);
-          vv = DT<T>::to_f(vpool[off]);
-        } else if (c == 0) {
-          set_err(a.err, IR_DEVERR_BLOCK_ID);
-        }
-      }
-      k_s[r][c] = kv;
-      v_s[r][c] = vv;
+    // stage tile t (its chunks are in registers), then start loading t + 1
+    store_tile(cur, t);
+    if (t + 1 < end) {
+      advance(nxt, t + 1);
+      load_tile(nxt, t + 1);
     }
     __syncthreads();
     for (int i = tid; i < kTile * a.n_rep; i += kGenThreads) {
