@@ -159,7 +159,7 @@ def test_workload_properties():
     assert len(set(int(t) for t in tails)) == w.batch
 
 
-def test_c2_bytes_match_survey_estimate():
+def test_c2_bytes_in_expected_range_and_match_oracle_count():
     w = wl.c2(seed=0)
     assert w.batch == 64 and (w.context_lens >= 512).all() and (w.context_lens <= 4096).all()
     assert 200e6 < w.algorithmic_bytes() < 400e6
