@@ -25,8 +25,11 @@ __global__ void __launch_bounds__(kGenThreads)
     decode_generic_kernel(const DecodeArgs a) {
   constexpr int HPT = kGenThreads / D;            // head groups per column
   constexpr int NH = (kMaxGroup + HPT - 1) / HPT;  // heads per thread
-  __shared__ float q_s[kMaxGroup][D];
-  __shared__ float k_s[kTile][D + 1];
+  // rows of K padded to D + 4 floats: 16-byte aligned for the vector reads
+  // of the score loop, and the 8 rows one 8-lane phase reads hit distinct
+  // banks
+  __shared__ __align__(16) float q_s[kMaxGroup][D];
+  __shared__ __align__(16) float k_s[kTile][D + 4];
   __shared__ float v_s[kTile][D];
   __shared__ float p_s[kMaxGroup][kTile];
   __shared__ float m_s[kMaxGroup], l_s[kMaxGroup], alpha_s[kMaxGroup];
@@ -203,8 +206,16 @@ __global__ void __launch_bounds__(kGenThreads)
     for (int i = tid; i < kTile * a.n_rep; i += kGenThreads) {
       const int r = i % kTile, n = i / kTile;
       float s = 0.f;
-#pragma unroll 8
-      for (int c = 0; c < D; ++c) s = fmaf(q_s[n][c], k_s[r][c], s);
+#pragma unroll 4
+      for (int c = 0; c < D; c += 4) {
+        // the same products in the same order as one element at a time
+        const float4 qv = *reinterpret_cast<const float4*>(&q_s[n][c]);
+        const float4 kv = *reinterpret_cast<const float4*>(&k_s[r][c]);
+        s = fmaf(qv.x, kv.x, s);
+        s = fmaf(qv.y, kv.y, s);
+        s = fmaf(qv.z, kv.z, s);
+        s = fmaf(qv.w, kv.w, s);
+      }
       p_s[n][r] = r < nvalid ? s * a.scale_log2 : -INFINITY;
     }
     __syncthreads();
